@@ -1,0 +1,187 @@
+// Shared device helpers for the gfxinfer-b200 kernels (sm_100a).
+//
+// Numerics contract: this library is compiled with -fmad=false, -prec-div=true,
+// -prec-sqrt=true and -ftz=false, so each float operation written here is one
+// IEEE round-to-nearest-even operation. Fused multiply-adds appear only where
+// written as fmaf(). Every reduction uses a fixed order, which lets the CPU
+// oracle reproduce kernel outputs bit for bit.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "gfxb/gfxb.h"
+
+namespace gfxb {
+
+constexpr unsigned kGroup = 128;
+constexpr unsigned kWarp = 32;
+
+// ---- status plumbing ------------------------------------------------------
+
+void set_error(const char* message);
+void set_error_cuda(cudaError_t error, const char* context);
+int fail(int status, const char* message);
+int launch_status(const char* context);
+
+#define GFXB_REQUIRE(condition, message) \
+  do {                                   \
+    if (!(condition)) return ::gfxb::fail(GFXB_INVALID_ARGUMENT, message); \
+  } while (0)
+
+// ---- scalar conversions ---------------------------------------------------
+
+__device__ __forceinline__ float h2f(__half value) { return __half2float(value); }
+__device__ __forceinline__ __half f2h(float value) { return __float2half_rn(value); }
+__device__ __forceinline__ float bf2f(std::uint16_t bits) {
+  return __uint_as_float(static_cast<std::uint32_t>(bits) << 16);
+}
+
+// __float2int_rn: NaN -> 0, saturating, ties to even.
+__device__ __forceinline__ int f2i_rn(float value) { return __float2int_rn(value); }
+
+// ---- exp / log1p ----------------------------------------------------------
+// e^x by Cody-Waite two-constant reduction x = n*ln2 + r (W. J. Cody and
+// W. Waite, "Software Manual for the Elementary Functions", 1980), e^r by its
+// degree-7 Taylor polynomial in Horner form, then exact scaling by 2^n.
+
+__device__ __forceinline__ float pow2i(int k) {
+  return __uint_as_float(static_cast<std::uint32_t>(k + 127) << 23);
+}
+
+__device__ __forceinline__ float gx_expf(float x) {
+  if (x != x) return x;
+  if (x > 88.7228394f) return __uint_as_float(0x7f800000u);
+  if (x < -104.0f) return 0.0f;
+  const float n = rintf(__fmul_rn(x, 1.44269502f));
+  float r = fmaf(n, -0.693145751953125f, x);
+  r = fmaf(n, -1.428606765330187e-6f, r);
+  float p = 1.98412698e-4f;
+  p = fmaf(p, r, 1.38888889e-3f);
+  p = fmaf(p, r, 8.33333333e-3f);
+  p = fmaf(p, r, 4.16666667e-2f);
+  p = fmaf(p, r, 1.66666667e-1f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  const int e = static_cast<int>(n);
+  if (e > 127) return __fmul_rn(__fmul_rn(p, pow2i(127)), pow2i(e - 127));
+  if (e < -126) return __fmul_rn(__fmul_rn(p, pow2i(e + 64)), pow2i(-64));
+  return __fmul_rn(p, pow2i(e));
+}
+
+// ln(u), u >= 1: u = m*2^e, m in [sqrt(1/2), sqrt(2)], ln(m) = 2*atanh(s),
+// s = (m-1)/(m+1), odd series to s^11.
+__device__ __forceinline__ float gx_log_ge1(float u) {
+  const std::uint32_t bits = __float_as_uint(u);
+  int e = static_cast<int>((bits >> 23) & 0xffu) - 127;
+  float m = __uint_as_float((bits & 0x007fffffu) | 0x3f800000u);
+  if (m > 1.41421356f) {
+    m = __fmul_rn(m, 0.5f);
+    e += 1;
+  }
+  const float s = __fdiv_rn(__fsub_rn(m, 1.0f), __fadd_rn(m, 1.0f));
+  const float s2 = __fmul_rn(s, s);
+  float p = 0.0909090909f;
+  p = fmaf(p, s2, 0.111111111f);
+  p = fmaf(p, s2, 0.142857143f);
+  p = fmaf(p, s2, 0.2f);
+  p = fmaf(p, s2, 0.333333333f);
+  p = fmaf(p, s2, 1.0f);
+  const float lm = __fmul_rn(__fmul_rn(2.0f, s), p);
+  return fmaf(static_cast<float>(e), 0.693147181f, lm);
+}
+
+// log(1+x), x >= 0 (D. Goldberg 1991, Theorem 4).
+__device__ __forceinline__ float gx_log1pf(float x) {
+  if (x != x) return x;
+  if (x == __uint_as_float(0x7f800000u)) return x;
+  const float u = __fadd_rn(1.0f, x);
+  if (u == 1.0f) return x;
+  return __fmul_rn(gx_log_ge1(u), __fdiv_rn(x, __fsub_rn(u, 1.0f)));
+}
+
+__device__ __forceinline__ float gx_sigmoid(float x) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, gx_expf(-x)));
+}
+
+__device__ __forceinline__ float gx_silu(float x) {
+  return __fdiv_rn(x, __fadd_rn(1.0f, gx_expf(-x)));
+}
+
+// 1 / sqrt(x), both steps correctly rounded (stands in for rsqrtf so the CPU
+// oracle can reproduce it).
+__device__ __forceinline__ float inv_sqrt_rn(float x) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(x));
+}
+
+// ---- fixed-order reductions -----------------------------------------------
+
+// Lane 0 receives the pairwise tree of the shuffle-down sequence 16, 8, 4, 2, 1.
+__device__ __forceinline__ float warp_sum_down(float value) {
+  value = __fadd_rn(value, __shfl_down_sync(0xffffffffu, value, 16));
+  value = __fadd_rn(value, __shfl_down_sync(0xffffffffu, value, 8));
+  value = __fadd_rn(value, __shfl_down_sync(0xffffffffu, value, 4));
+  value = __fadd_rn(value, __shfl_down_sync(0xffffffffu, value, 2));
+  value = __fadd_rn(value, __shfl_down_sync(0xffffffffu, value, 1));
+  return value;
+}
+
+// Every lane receives the same pairwise tree (xor butterfly 16, 8, 4, 2, 1);
+// identical to warp_sum_down's lane-0 value because float addition commutes.
+__device__ __forceinline__ float warp_sum_xor(float value) {
+  value = __fadd_rn(value, __shfl_xor_sync(0xffffffffu, value, 16));
+  value = __fadd_rn(value, __shfl_xor_sync(0xffffffffu, value, 8));
+  value = __fadd_rn(value, __shfl_xor_sync(0xffffffffu, value, 4));
+  value = __fadd_rn(value, __shfl_xor_sync(0xffffffffu, value, 2));
+  value = __fadd_rn(value, __shfl_xor_sync(0xffffffffu, value, 1));
+  return value;
+}
+
+// Tree over up to eight per-warp sums padded with zeros to 32 lanes (the
+// second stage of the reference's 256-thread block reduction).
+__device__ __forceinline__ float tree_of_eight(const float* sums, unsigned count) {
+  float a[8];
+#pragma unroll
+  for (unsigned i = 0; i < 8; ++i) a[i] = i < count ? sums[i] : 0.0f;
+  // padding lanes 8..31 are zero: x + 0 == x, so only offsets 4, 2, 1 change values
+#pragma unroll
+  for (unsigned i = 0; i < 4; ++i) a[i] = __fadd_rn(a[i], a[i + 4]);
+#pragma unroll
+  for (unsigned i = 0; i < 2; ++i) a[i] = __fadd_rn(a[i], a[i + 2]);
+  return __fadd_rn(a[0], a[1]);
+}
+
+// ---- streaming loads --------------------------------------------------------
+
+__device__ __forceinline__ uint4 ldg_stream16(const void* pointer) {
+  uint4 value;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(value.x), "=r"(value.y), "=r"(value.z), "=r"(value.w)
+               : "l"(pointer));
+  return value;
+}
+
+__device__ __forceinline__ uint2 ldg_stream8(const void* pointer) {
+  uint2 value;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+               : "=r"(value.x), "=r"(value.y)
+               : "l"(pointer));
+  return value;
+}
+
+__device__ __forceinline__ void mma_s8_16832(int (&c)[4], const std::uint32_t (&a)[4],
+                                             std::uint32_t b0, std::uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
+
+}  // namespace gfxb

@@ -1,0 +1,914 @@
+// Low-bit dequant-GEMV for sm_100a: W2/W3/W4 group-128 weights x A4/A8
+// activations on the int8 tensor cores (mma.sync m16n8k32 s8).
+//
+// Replaces the reference's RDNA4 WMMA kernels (lowbit_gemv.hip:461-755). The
+// arithmetic contract is the reference's: per 128-column group an exact int32
+// dot of weight codes and activation codes, then an fp32 fma chain over
+// groups in ascending order with the product of the two fp16 scales
+// (lowbit_gemv.hip:525-536). The result is therefore bit-identical to the
+// reference's, independent of how this kernel splits the work.
+//
+// Codes enter the tensor core unsigned (u = q - beta/alpha): W3 u = q + 4,
+// W4 u = q + 8, W2 u = (q + 3) / 2, and the exact correction
+// dot = alpha * mma(u, a) + beta * sum(a) uses a per-group activation sum
+// carried in the activation pack.
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace gfxb {
+namespace {
+
+constexpr std::uint32_t kM7 = 0x07070707u;
+constexpr std::uint32_t kM3 = 0x03030303u;
+constexpr std::uint32_t kM4 = 0x04040404u;
+constexpr std::uint32_t kM15 = 0x0f0f0f0fu;
+
+template <int Bits>
+struct Codec;
+
+template <>
+struct Codec<2> {
+  static constexpr int alpha = 2, beta = -3;
+};
+template <>
+struct Codec<3> {
+  static constexpr int alpha = 1, beta = -4;
+};
+template <>
+struct Codec<4> {
+  static constexpr int alpha = 1, beta = -8;
+};
+
+__host__ __device__ constexpr int bits_of(int format) {
+  return format == GFXB_W2 ? 2 : (format == GFXB_W3 ? 3 : 4);
+}
+
+// ---------------------------------------------------------------------------
+// b200 layout. For lane L (g = L/4, t = L%4) the tensor-core A fragment of
+// k-step s (0..3) holds registers q = 0..3, byte j = 0..3, covering
+//   row = g + 8*(q & 1),  k = 32*s + 16*(q >> 1) + 4*t + j.
+// ---------------------------------------------------------------------------
+
+template <int Bits>
+struct LaneWords;
+
+template <>
+struct LaneWords<3> {
+  uint4 p0;  // block + 16*L        : words w0..w3
+  uint2 p1;  // block + 512 + 8*L   : words w4..w5
+};
+template <>
+struct LaneWords<4> {
+  uint4 p0;  // block + 16*L
+  uint4 p1;  // block + 512 + 16*L
+};
+template <>
+struct LaneWords<2> {
+  uint4 p0;  // block + 16*L
+};
+
+__device__ __forceinline__ void load_lane(const std::uint8_t* block, unsigned lane, LaneWords<3>& w) {
+  w.p0 = ldg_stream16(block + 16u * lane);
+  w.p1 = ldg_stream8(block + 512u + 8u * lane);
+}
+__device__ __forceinline__ void load_lane(const std::uint8_t* block, unsigned lane, LaneWords<4>& w) {
+  w.p0 = ldg_stream16(block + 16u * lane);
+  w.p1 = ldg_stream16(block + 512u + 16u * lane);
+}
+__device__ __forceinline__ void load_lane(const std::uint8_t* block, unsigned lane, LaneWords<2>& w) {
+  w.p0 = ldg_stream16(block + 16u * lane);
+}
+
+// W3: a word triple (x0, x1, x2) carries the 32 codes of k-steps (sa, sb):
+// six registers from 3-bit fields at bits 0-2 / 3-5 of each byte, two more
+// assembled from the spare bits 6-7 (low bits) and x2's bits 6 / 7 (high bit).
+__device__ __forceinline__ void unpack_w3_triple(std::uint32_t x0, std::uint32_t x1, std::uint32_t x2,
+                                                 std::uint32_t (&ra)[4], std::uint32_t (&rb)[4]) {
+  ra[0] = x0 & kM7;
+  ra[1] = (x0 >> 3) & kM7;
+  ra[2] = x1 & kM7;
+  ra[3] = (x1 >> 3) & kM7;
+  rb[0] = x2 & kM7;
+  rb[1] = (x2 >> 3) & kM7;
+  rb[2] = ((x0 >> 6) & kM3) | ((x2 >> 4) & kM4);
+  rb[3] = ((x1 >> 6) & kM3) | ((x2 >> 5) & kM4);
+}
+
+__device__ __forceinline__ void unpack(const LaneWords<3>& w, std::uint32_t (&a)[4][4]) {
+  unpack_w3_triple(w.p0.x, w.p0.y, w.p0.z, a[0], a[1]);
+  unpack_w3_triple(w.p0.w, w.p1.x, w.p1.y, a[2], a[3]);
+}
+
+__device__ __forceinline__ void unpack_w4_pair(std::uint32_t lo, std::uint32_t hi, std::uint32_t (&r)[4]) {
+  r[0] = lo & kM15;
+  r[1] = (lo >> 4) & kM15;
+  r[2] = hi & kM15;
+  r[3] = (hi >> 4) & kM15;
+}
+
+__device__ __forceinline__ void unpack(const LaneWords<4>& w, std::uint32_t (&a)[4][4]) {
+  unpack_w4_pair(w.p0.x, w.p0.y, a[0]);
+  unpack_w4_pair(w.p0.z, w.p0.w, a[1]);
+  unpack_w4_pair(w.p1.x, w.p1.y, a[2]);
+  unpack_w4_pair(w.p1.z, w.p1.w, a[3]);
+}
+
+__device__ __forceinline__ void unpack_w2_word(std::uint32_t x, std::uint32_t (&r)[4]) {
+  r[0] = x & kM3;
+  r[1] = (x >> 2) & kM3;
+  r[2] = (x >> 4) & kM3;
+  r[3] = (x >> 6) & kM3;
+}
+
+__device__ __forceinline__ void unpack(const LaneWords<2>& w, std::uint32_t (&a)[4][4]) {
+  unpack_w2_word(w.p0.x, a[0]);
+  unpack_w2_word(w.p0.y, a[1]);
+  unpack_w2_word(w.p0.z, a[2]);
+  unpack_w2_word(w.p0.w, a[3]);
+}
+
+// ---------------------------------------------------------------------------
+// GEMV over the b200 layout
+// ---------------------------------------------------------------------------
+
+struct MatrixArg {
+  const std::uint8_t* codes;
+  const __half* scales;
+  void* output;
+  std::uint32_t tiles;
+  std::uint32_t output_f16;
+};
+
+struct GemvArgs {
+  MatrixArg m[4];
+  std::uint32_t count;
+  const std::int8_t* act;
+  const __half* act_scales;
+  const std::int32_t* act_sums;
+  std::uint32_t columns;
+  std::uint32_t groups;
+  std::uint32_t batch;
+};
+
+// Locate the matrix a CTA's global tile index belongs to.
+__device__ __forceinline__ MatrixArg select_matrix(const GemvArgs& args, std::uint32_t& tile) {
+  MatrixArg m = args.m[0];
+#pragma unroll
+  for (int i = 1; i < 4; ++i) {
+    if (static_cast<std::uint32_t>(i) < args.count && tile >= m.tiles) {
+      tile -= m.tiles;
+      m = args.m[i];
+    }
+  }
+  return m;
+}
+
+// One CTA (8 warps) per 16-row tile. Round r: warp w computes the int32 dots
+// of group 8r+w with 4 mma per 8-token block, writes them to shared memory;
+// then each (row, token) thread extends its fp32 fma chain by the round's
+// groups in ascending order. Weights are prefetched two rounds ahead.
+template <int Bits, int NB>
+__global__ __launch_bounds__(256) void gemv_b200_kernel(const GemvArgs args) {
+  std::uint32_t tile = blockIdx.x;
+  const MatrixArg m = select_matrix(args, tile);
+  const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const unsigned gl = lane >> 2, tq = lane & 3u;
+  const std::uint32_t G = args.groups, B = args.batch, K = args.columns;
+  constexpr std::uint32_t kBlock = Bits * 256u;
+  constexpr int kAlpha = Codec<Bits>::alpha, kBeta = Codec<Bits>::beta;
+  const std::uint8_t* tile_codes = m.codes + static_cast<std::size_t>(tile) * G * kBlock;
+  const __half* tile_scales = m.scales + static_cast<std::size_t>(tile) * G * 16u;
+
+  __shared__ std::int32_t dots[8][16][NB * 8];
+
+  const std::uint32_t pairs = 16u * B;
+  float accumulator[2] = {0.0f, 0.0f};
+
+  LaneWords<Bits> w_cur{}, w_next{}, w_after{};
+  if (warp < G) load_lane(tile_codes + warp * kBlock, lane, w_cur);
+  if (warp + 8 < G) load_lane(tile_codes + (warp + 8) * kBlock, lane, w_next);
+
+  const std::uint32_t rounds = (G + 7u) / 8u;
+  for (std::uint32_t r = 0; r < rounds; ++r) {
+    const std::uint32_t g = 8u * r + warp;
+    if (g + 16u < G) load_lane(tile_codes + (g + 16u) * kBlock, lane, w_after);
+
+    // Scales this thread's chain needs for the round, issued early.
+    const std::uint32_t round_groups = min(8u, G - 8u * r);
+    float scale_product[2][8];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const std::uint32_t pair = threadIdx.x + 256u * p;
+      if (pair < pairs) {
+        const std::uint32_t row = pair & 15u, token = pair >> 4;
+#pragma unroll
+        for (unsigned w = 0; w < 8; ++w) {
+          if (w < round_groups) {
+            const std::uint32_t gg = 8u * r + w;
+            scale_product[p][w] = __fmul_rn(h2f(tile_scales[gg * 16u + row]),
+                                            h2f(args.act_scales[token * G + gg]));
+          }
+        }
+      }
+    }
+
+    if (g < G) {
+      std::uint32_t a[4][4];
+      unpack(w_cur, a);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        std::uint32_t token = nb * 8u + gl;
+        token = token < B ? token : B - 1u;
+        const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * K +
+                                static_cast<std::size_t>(g) * kGroup + tq * 32u;
+        const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(ap));
+        const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(ap + 16));
+        int c[4] = {0, 0, 0, 0};
+        mma_s8_16832(c, a[0], b0.x, b0.y);
+        mma_s8_16832(c, a[1], b0.z, b0.w);
+        mma_s8_16832(c, a[2], b1.x, b1.y);
+        mma_s8_16832(c, a[3], b1.z, b1.w);
+        const std::uint32_t t0 = nb * 8u + 2u * tq, t1 = t0 + 1u;
+        if (t0 < B) {
+          const int s0 = args.act_sums[t0 * G + g];
+          dots[warp][gl][t0] = kAlpha * c[0] + kBeta * s0;
+          dots[warp][gl + 8][t0] = kAlpha * c[2] + kBeta * s0;
+        }
+        if (t1 < B) {
+          const int s1 = args.act_sums[t1 * G + g];
+          dots[warp][gl][t1] = kAlpha * c[1] + kBeta * s1;
+          dots[warp][gl + 8][t1] = kAlpha * c[3] + kBeta * s1;
+        }
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const std::uint32_t pair = threadIdx.x + 256u * p;
+      if (pair < pairs) {
+        const std::uint32_t row = pair & 15u, token = pair >> 4;
+#pragma unroll
+        for (unsigned w = 0; w < 8; ++w) {
+          if (w < round_groups) {
+            accumulator[p] = fmaf(static_cast<float>(dots[w][row][token]), scale_product[p][w],
+                                  accumulator[p]);
+          }
+        }
+      }
+    }
+    __syncthreads();
+    w_cur = w_next;
+    w_next = w_after;
+  }
+
+  const std::uint32_t rows = m.tiles * 16u;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const std::uint32_t pair = threadIdx.x + 256u * p;
+    if (pair < pairs) {
+      const std::uint32_t row = pair & 15u, token = pair >> 4;
+      const std::size_t index = static_cast<std::size_t>(token) * rows + tile * 16u + row;
+      if (m.output_f16) {
+        static_cast<__half*>(m.output)[index] = f2h(accumulator[p]);
+      } else {
+        static_cast<float*>(m.output)[index] = accumulator[p];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Reference-layout GEMM (drop-in for launch_gfx12_i4_gemm / _i8_gemm): gfx12
+// tiled weights staged per warp in shared memory, activations read in the
+// reference's packed-A4 or row-major A8 layout, group sums formed on the fly.
+// ---------------------------------------------------------------------------
+
+// Spread four consecutive 3-bit codes (a 12-bit field) into four bytes.
+__device__ __forceinline__ std::uint32_t spread3(std::uint32_t f) {
+  f &= 0xfffu;
+  std::uint32_t x = (f & 0x3fu) | ((f & 0xfc0u) << 10);
+  return (x & 0x00070007u) | ((x & 0x00380038u) << 5);
+}
+__device__ __forceinline__ std::uint32_t spread4(std::uint32_t f) {
+  f &= 0xffffu;
+  std::uint32_t x = (f & 0xffu) | ((f & 0xff00u) << 8);
+  return (x & 0x000f000fu) | ((x & 0x00f000f0u) << 4);
+}
+__device__ __forceinline__ std::uint32_t spread2(std::uint32_t f) {
+  f &= 0xffu;
+  std::uint32_t x = (f & 0xfu) | ((f & 0xf0u) << 12);
+  return (x & 0x00030003u) | ((x & 0x000c000cu) << 6);
+}
+
+// Signed nibbles (two's complement) -> signed bytes, four at a time.
+__device__ __forceinline__ std::uint32_t nibbles_to_s8(std::uint32_t packed16) {
+  const std::uint32_t biased = spread4(packed16) ^ 0x08080808u;   // v + 8 in [0, 15]
+  return ((biased | 0x80808080u) - 0x08080808u) ^ 0x80808080u;    // per-byte v
+}
+
+template <int Bits, bool Act8, int NB>
+__global__ __launch_bounds__(256) void gemm_gfx12_kernel(
+    const std::uint8_t* __restrict__ weights, const __half* __restrict__ weight_scales,
+    const std::uint8_t* __restrict__ activations, const __half* __restrict__ activation_scales,
+    float* __restrict__ output, std::uint32_t rows, std::uint32_t columns, std::uint32_t batch) {
+  const std::uint32_t tile = blockIdx.x;
+  const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const unsigned gl = lane >> 2, tq = lane & 3u;
+  const std::uint32_t G = columns / kGroup, B = batch, K = columns;
+  constexpr std::uint32_t kBlock = Bits * 256u;
+  constexpr std::uint32_t kFrag = Bits == 2 ? 8u : (Bits == 3 ? 12u : 16u);
+  constexpr int kAlpha = Codec<Bits>::alpha, kBeta = Codec<Bits>::beta;
+  __shared__ std::uint32_t stage[8][kBlock / 4 + 4];
+  __shared__ std::int32_t dots[8][16][NB * 8];
+  const std::uint32_t pairs = 16u * B;
+  float accumulator[2] = {0.0f, 0.0f};
+  const std::uint32_t rounds = (G + 7u) / 8u;
+  for (std::uint32_t r = 0; r < rounds; ++r) {
+    const std::uint32_t g = 8u * r + warp;
+    const std::uint32_t round_groups = min(8u, G - 8u * r);
+    if (g < G) {
+      const std::uint8_t* block = weights + (static_cast<std::size_t>(tile) * G + g) * kBlock;
+      for (std::uint32_t offset = lane * 16u; offset < kBlock; offset += 512u) {
+        const uint4 v = ldg_stream16(block + offset);
+        stage[warp][offset / 4 + 0] = v.x;
+        stage[warp][offset / 4 + 1] = v.y;
+        stage[warp][offset / 4 + 2] = v.z;
+        stage[warp][offset / 4 + 3] = v.w;
+      }
+      __syncwarp();
+      std::uint32_t a[4][4];
+#pragma unroll
+      for (unsigned s = 0; s < 4; ++s) {
+#pragma unroll
+        for (unsigned q = 0; q < 4; ++q) {
+          const unsigned row = gl + 8u * (q & 1u), half = q >> 1;
+          const std::uint32_t frag_bit = ((s * 16u + row) * kFrag) * 8u;
+          const std::uint32_t bit = frag_bit + (Bits * (16u * half + 4u * tq));
+          const std::uint32_t lo = stage[warp][bit / 32u];
+          const std::uint32_t hi = stage[warp][bit / 32u + 1u];
+          const std::uint32_t field = __funnelshift_r(lo, hi, bit & 31u);
+          if constexpr (Bits == 3) {
+            a[s][q] = spread3(field);
+          } else if constexpr (Bits == 4) {
+            a[s][q] = spread4(field) ^ 0x08080808u;
+          } else {
+            a[s][q] = spread2(field);
+          }
+        }
+      }
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        std::uint32_t token = nb * 8u + gl;
+        token = token < B ? token : B - 1u;
+        std::uint32_t bregs[4][2];
+        int partial = 0;
+#pragma unroll
+        for (unsigned s = 0; s < 4; ++s) {
+#pragma unroll
+          for (unsigned h = 0; h < 2; ++h) {
+            const std::uint32_t k = g * kGroup + 32u * s + 16u * h + 4u * tq;
+            std::uint32_t value;
+            if constexpr (Act8) {
+              value = __ldg(reinterpret_cast<const std::uint32_t*>(
+                  activations + static_cast<std::size_t>(token) * K + k));
+            } else {
+              const std::uint16_t packed = __ldg(reinterpret_cast<const std::uint16_t*>(
+                  activations + static_cast<std::size_t>(token) * (K / 2u) + k / 2u));
+              value = nibbles_to_s8(packed);
+            }
+            bregs[s][h] = value;
+            partial = __dp4a(static_cast<int>(value), 0x01010101, partial);
+          }
+        }
+        partial += __shfl_xor_sync(0xffffffffu, partial, 1);
+        partial += __shfl_xor_sync(0xffffffffu, partial, 2);
+        const int sum0 = __shfl_sync(0xffffffffu, partial, (2u * tq) * 4u);
+        const int sum1 = __shfl_sync(0xffffffffu, partial, (2u * tq + 1u) * 4u);
+        int c[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (unsigned s = 0; s < 4; ++s) mma_s8_16832(c, a[s], bregs[s][0], bregs[s][1]);
+        const std::uint32_t t0 = nb * 8u + 2u * tq, t1 = t0 + 1u;
+        if (t0 < B) {
+          dots[warp][gl][t0] = kAlpha * c[0] + kBeta * sum0;
+          dots[warp][gl + 8][t0] = kAlpha * c[2] + kBeta * sum0;
+        }
+        if (t1 < B) {
+          dots[warp][gl][t1] = kAlpha * c[1] + kBeta * sum1;
+          dots[warp][gl + 8][t1] = kAlpha * c[3] + kBeta * sum1;
+        }
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const std::uint32_t pair = threadIdx.x + 256u * p;
+      if (pair < pairs) {
+        const std::uint32_t row = pair & 15u, token = pair >> 4;
+        for (unsigned w = 0; w < round_groups; ++w) {
+          const std::uint32_t gg = 8u * r + w;
+          const float product = __fmul_rn(h2f(weight_scales[(tile * G + gg) * 16u + row]),
+                                          h2f(activation_scales[token * G + gg]));
+          accumulator[p] = fmaf(static_cast<float>(dots[w][row][token]), product, accumulator[p]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const std::uint32_t pair = threadIdx.x + 256u * p;
+    if (pair < pairs) {
+      const std::uint32_t row = pair & 15u, token = pair >> 4;
+      output[static_cast<std::size_t>(token) * rows + tile * 16u + row] = accumulator[p];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// activation packs
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ std::uint32_t fragment_offset(std::uint32_t k) {
+  const std::uint32_t s = k >> 5, rest = k & 31u, half = rest >> 4, t = (rest & 15u) >> 2, j = k & 3u;
+  return t * 32u + s * 8u + half * 4u + j;
+}
+
+template <int Bits>
+__global__ __launch_bounds__(128) void pack_activation_kernel(
+    const __half* __restrict__ input, std::int8_t* __restrict__ codes, __half* __restrict__ scales,
+    std::int32_t* __restrict__ sums, std::uint8_t* __restrict__ packed_a4,
+    std::uint32_t columns, std::uint32_t groups) {
+  const std::uint32_t linear = blockIdx.x;
+  const std::uint32_t token = linear / groups, group = linear - token * groups;
+  const unsigned i = threadIdx.x, lane = i & 31u, warp = i >> 5;
+  const std::size_t base = static_cast<std::size_t>(token) * columns + group * kGroup;
+  const float x = h2f(input[base + i]);
+  float amax = fabsf(x);
+#pragma unroll
+  for (unsigned offset = 16; offset != 0; offset >>= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
+  }
+  __shared__ float warp_max[4];
+  __shared__ int warp_sum[4];
+  if (lane == 0) warp_max[warp] = amax;
+  __syncthreads();
+  amax = fmaxf(fmaxf(warp_max[0], warp_max[1]), fmaxf(warp_max[2], warp_max[3]));
+  constexpr float kDivisor = Bits == 4 ? 7.0f : 127.0f;
+  constexpr int kLimit = Bits == 4 ? 7 : 127;
+  const __half scale_h = f2h(amax == 0.0f ? 1.0f : __fdiv_rn(amax, kDivisor));
+  const float scale = h2f(scale_h);
+  int q = f2i_rn(__fdiv_rn(x, scale));
+  q = max(-kLimit, min(kLimit, q));
+  codes[base + fragment_offset(i)] = static_cast<std::int8_t>(q);
+  int total = q;
+#pragma unroll
+  for (unsigned offset = 16; offset != 0; offset >>= 1) total += __shfl_xor_sync(0xffffffffu, total, offset);
+  if (lane == 0) warp_sum[warp] = total;
+  const int neighbour = __shfl_down_sync(0xffffffffu, q, 1);
+  if (Bits == 4 && packed_a4 != nullptr && (i & 1u) == 0) {
+    packed_a4[static_cast<std::size_t>(token) * (columns / 2u) + group * 64u + i / 2u] =
+        static_cast<std::uint8_t>((q & 0x0f) | ((neighbour & 0x0f) << 4));
+  }
+  __syncthreads();
+  if (i == 0) {
+    scales[linear] = scale_h;
+    sums[linear] = warp_sum[0] + warp_sum[1] + warp_sum[2] + warp_sum[3];
+  }
+}
+
+template <int Bits>
+__global__ __launch_bounds__(128) void quantize_reference_kernel(
+    const __half* __restrict__ input, std::uint8_t* __restrict__ output, __half* __restrict__ scales,
+    std::uint32_t columns, std::uint32_t groups) {
+  const std::uint32_t linear = blockIdx.x;
+  const std::uint32_t token = linear / groups, group = linear - token * groups;
+  const unsigned i = threadIdx.x, lane = i & 31u, warp = i >> 5;
+  const std::size_t base = static_cast<std::size_t>(token) * columns + group * kGroup;
+  const float x = h2f(input[base + i]);
+  float amax = fabsf(x);
+#pragma unroll
+  for (unsigned offset = 16; offset != 0; offset >>= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
+  }
+  __shared__ float warp_max[4];
+  if (lane == 0) warp_max[warp] = amax;
+  __syncthreads();
+  amax = fmaxf(fmaxf(warp_max[0], warp_max[1]), fmaxf(warp_max[2], warp_max[3]));
+  constexpr float kDivisor = Bits == 4 ? 7.0f : 127.0f;
+  constexpr int kLimit = Bits == 4 ? 7 : 127;
+  const __half scale_h = f2h(amax == 0.0f ? 1.0f : __fdiv_rn(amax, kDivisor));
+  int q = f2i_rn(__fdiv_rn(x, h2f(scale_h)));
+  q = max(-kLimit, min(kLimit, q));
+  if constexpr (Bits == 8) {
+    output[base + i] = static_cast<std::uint8_t>(static_cast<std::int8_t>(q));
+  } else {
+    const int neighbour = __shfl_down_sync(0xffffffffu, q, 1);
+    if ((i & 1u) == 0) {
+      output[static_cast<std::size_t>(token) * (columns / 2u) + group * 64u + i / 2u] =
+          static_cast<std::uint8_t>((q & 0x0f) | ((neighbour & 0x0f) << 4));
+    }
+  }
+  if (i == 0) scales[linear] = scale_h;
+}
+
+// ---------------------------------------------------------------------------
+// layout conversion and synthetic weights
+// ---------------------------------------------------------------------------
+
+// Code sources: each yields the unsigned code u (reference code mapping of
+// quantization.cpp:29-56, W4 biased by +8) of logical (row, column).
+struct RowMajorSource {
+  const std::uint8_t* codes;
+  std::uint32_t columns;
+  int bits;
+  __device__ std::uint32_t operator()(std::uint32_t row, std::uint32_t column) const {
+    if (bits == 2) {
+      const std::uint8_t* r = codes + static_cast<std::size_t>(row) * (columns / 4u);
+      return (r[column / 4u] >> ((column & 3u) * 2u)) & 3u;
+    }
+    if (bits == 4) {
+      const std::uint8_t* r = codes + static_cast<std::size_t>(row) * (columns / 2u);
+      return ((r[column / 2u] >> ((column & 1u) * 4u)) & 15u) ^ 8u;
+    }
+    const std::uint8_t* r = codes + static_cast<std::size_t>(row) * (columns * 3u / 8u);
+    const std::uint32_t group = column / kGroup, local = column % kGroup;
+    const std::uint32_t byte = local / 8u, bit = local & 7u;
+    std::uint32_t code = 0;
+#pragma unroll
+    for (std::uint32_t plane = 0; plane < 3; ++plane) {
+      code |= ((r[group * 48u + plane * 16u + byte] >> bit) & 1u) << plane;
+    }
+    return code;
+  }
+};
+
+struct Gfx12Source {
+  const std::uint8_t* codes;
+  std::uint32_t columns;
+  int bits;
+  __device__ std::uint32_t operator()(std::uint32_t row, std::uint32_t column) const {
+    const std::uint32_t groups = columns / kGroup;
+    const std::uint32_t fragment_bytes = bits == 2 ? 8u : (bits == 3 ? 12u : 16u);
+    const std::uint32_t tile = row / 16u, local_row = row & 15u;
+    const std::uint32_t group = column / kGroup, k_tile = (column % kGroup) / 32u, item = column & 31u;
+    const std::uint8_t* fragment =
+        codes + (((static_cast<std::size_t>(tile) * groups + group) * 4u + k_tile) * 16u + local_row) *
+                    fragment_bytes;
+    const std::uint32_t bit = item * static_cast<std::uint32_t>(bits);
+    std::uint32_t word = fragment[bit / 8u];
+    if (bit / 8u + 1u < fragment_bytes) word |= static_cast<std::uint32_t>(fragment[bit / 8u + 1u]) << 8;
+    const std::uint32_t code = (word >> (bit & 7u)) & ((1u << bits) - 1u);
+    return bits == 4 ? (code ^ 8u) : code;
+  }
+};
+
+__device__ __forceinline__ std::uint64_t mix64(std::uint64_t z) {
+  z += 0x9e3779b97f4a7c15ULL;
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ std::uint64_t hash3(std::uint64_t seed, std::uint64_t stream, std::uint64_t index) {
+  return mix64(mix64(seed ^ (stream * 0xd1b54a32d192ed03ULL)) + index);
+}
+
+// Synthetic weights: reference code = top `bits` bits of hash(seed, 2*tensor, row*K + col).
+struct HashSource {
+  std::uint64_t seed;
+  std::uint32_t tensor;
+  std::uint32_t columns;
+  int bits;
+  __device__ std::uint32_t operator()(std::uint32_t row, std::uint32_t column) const {
+    const std::uint64_t h = hash3(seed, 2ull * tensor, static_cast<std::uint64_t>(row) * columns + column);
+    const std::uint32_t code = static_cast<std::uint32_t>(h >> (64 - bits));
+    return bits == 4 ? (code ^ 8u) : code;
+  }
+};
+
+template <class Source>
+__global__ void write_b200_kernel(Source source, std::uint8_t* __restrict__ out, std::uint32_t groups,
+                                  std::uint64_t lanes_total, int bits) {
+  const std::uint64_t index = static_cast<std::uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= lanes_total) return;
+  const std::uint32_t lane = static_cast<std::uint32_t>(index & 31u);
+  const std::uint64_t block_index = index >> 5;
+  const std::uint32_t tile = static_cast<std::uint32_t>(block_index / groups);
+  const std::uint32_t group = static_cast<std::uint32_t>(block_index % groups);
+  const std::uint32_t gl = lane >> 2, tq = lane & 3u;
+  auto code = [&](std::uint32_t s, std::uint32_t q, std::uint32_t j) -> std::uint32_t {
+    const std::uint32_t row = tile * 16u + gl + 8u * (q & 1u);
+    const std::uint32_t column = group * kGroup + 32u * s + 16u * (q >> 1) + 4u * tq + j;
+    return source(row, column);
+  };
+  std::uint8_t* block = out + block_index * static_cast<std::uint64_t>(bits) * 256u;
+  if (bits == 3) {
+    std::uint32_t words[6] = {0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (std::uint32_t triple = 0; triple < 2; ++triple) {
+      const std::uint32_t sa = 2u * triple, sb = sa + 1u;
+      std::uint32_t x0 = 0, x1 = 0, x2 = 0;
+#pragma unroll
+      for (std::uint32_t j = 0; j < 4; ++j) {
+        const std::uint32_t shift = 8u * j;
+        x0 |= (code(sa, 0, j) | (code(sa, 1, j) << 3) | ((code(sb, 2, j) & 3u) << 6)) << shift;
+        x1 |= (code(sa, 2, j) | (code(sa, 3, j) << 3) | ((code(sb, 3, j) & 3u) << 6)) << shift;
+        x2 |= (code(sb, 0, j) | (code(sb, 1, j) << 3) | ((code(sb, 2, j) >> 2) << 6) |
+               ((code(sb, 3, j) >> 2) << 7))
+              << shift;
+      }
+      words[3 * triple] = x0;
+      words[3 * triple + 1] = x1;
+      words[3 * triple + 2] = x2;
+    }
+    std::uint32_t* p0 = reinterpret_cast<std::uint32_t*>(block + 16u * lane);
+    std::uint32_t* p1 = reinterpret_cast<std::uint32_t*>(block + 512u + 8u * lane);
+    p0[0] = words[0];
+    p0[1] = words[1];
+    p0[2] = words[2];
+    p0[3] = words[3];
+    p1[0] = words[4];
+    p1[1] = words[5];
+  } else if (bits == 4) {
+    std::uint32_t words[8];
+#pragma unroll
+    for (std::uint32_t s = 0; s < 4; ++s) {
+      std::uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (std::uint32_t j = 0; j < 4; ++j) {
+        lo |= (code(s, 0, j) | (code(s, 1, j) << 4)) << (8u * j);
+        hi |= (code(s, 2, j) | (code(s, 3, j) << 4)) << (8u * j);
+      }
+      words[2 * s] = lo;
+      words[2 * s + 1] = hi;
+    }
+    std::uint32_t* p0 = reinterpret_cast<std::uint32_t*>(block + 16u * lane);
+    std::uint32_t* p1 = reinterpret_cast<std::uint32_t*>(block + 512u + 16u * lane);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      p0[i] = words[i];
+      p1[i] = words[4 + i];
+    }
+  } else {
+    std::uint32_t* p0 = reinterpret_cast<std::uint32_t*>(block + 16u * lane);
+#pragma unroll
+    for (std::uint32_t s = 0; s < 4; ++s) {
+      std::uint32_t word = 0;
+#pragma unroll
+      for (std::uint32_t j = 0; j < 4; ++j) {
+        word |= (code(s, 0, j) | (code(s, 1, j) << 2) | (code(s, 2, j) << 4) | (code(s, 3, j) << 6))
+                << (8u * j);
+      }
+      p0[s] = word;
+    }
+  }
+}
+
+__global__ void tile_scales_kernel(const __half* __restrict__ rowmajor, __half* __restrict__ tiled,
+                                   std::uint32_t rows, std::uint32_t groups) {
+  const std::uint64_t index = static_cast<std::uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= static_cast<std::uint64_t>(rows) * groups) return;
+  const std::uint32_t row = static_cast<std::uint32_t>(index / groups);
+  const std::uint32_t group = static_cast<std::uint32_t>(index % groups);
+  tiled[(static_cast<std::size_t>(row / 16u) * groups + group) * 16u + (row & 15u)] = rowmajor[index];
+}
+
+template <class Source>
+int launch_write_b200(const Source& source, std::uint8_t* out, std::size_t rows, std::size_t columns,
+                      int bits, cudaStream_t stream) {
+  const std::uint64_t groups = columns / kGroup;
+  const std::uint64_t lanes = (rows / 16u) * groups * 32u;
+  const unsigned threads = 256;
+  const std::uint64_t blocks = (lanes + threads - 1) / threads;
+  write_b200_kernel<Source><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+      source, out, static_cast<std::uint32_t>(groups), lanes, bits);
+  return launch_status("b200 weight layout kernel launch failed");
+}
+
+int validate_matrix_shape(int format, std::size_t rows, std::size_t columns) {
+  if (format != GFXB_W2 && format != GFXB_W3 && format != GFXB_W4) {
+    return fail(GFXB_UNSUPPORTED, "weight format must be W2G128, W3G128 or W4G128");
+  }
+  if (rows == 0 || rows % 16 != 0 || columns == 0 || columns % kGroup != 0) {
+    return fail(GFXB_INVALID_ARGUMENT, "weight matrix needs N divisible by 16 and K divisible by 128");
+  }
+  if (rows > (1ull << 31) || columns > (1ull << 24)) {
+    return fail(GFXB_INVALID_ARGUMENT, "weight matrix dimensions exceed the supported range");
+  }
+  return GFXB_OK;
+}
+
+template <int Bits, int NB>
+void launch_gemv_typed(const GemvArgs& args, unsigned grid, cudaStream_t stream) {
+  gemv_b200_kernel<Bits, NB><<<grid, 256, 0, stream>>>(args);
+}
+
+template <int Bits>
+void launch_gemv_bits(const GemvArgs& args, unsigned grid, cudaStream_t stream) {
+  const unsigned nb = (args.batch + 7u) / 8u;
+  switch (nb) {
+    case 1: launch_gemv_typed<Bits, 1>(args, grid, stream); break;
+    case 2: launch_gemv_typed<Bits, 2>(args, grid, stream); break;
+    case 3: launch_gemv_typed<Bits, 3>(args, grid, stream); break;
+    default: launch_gemv_typed<Bits, 4>(args, grid, stream); break;
+  }
+}
+
+template <int Bits, bool Act8>
+void launch_gfx12_bits(const std::uint8_t* w, const __half* ws, const std::uint8_t* act, const __half* as,
+                       float* out, std::uint32_t rows, std::uint32_t columns, std::uint32_t batch,
+                       cudaStream_t stream) {
+  const unsigned nb = (batch + 7u) / 8u;
+  const unsigned grid = rows / 16u;
+  switch (nb) {
+    case 1: gemm_gfx12_kernel<Bits, Act8, 1><<<grid, 256, 0, stream>>>(w, ws, act, as, out, rows, columns, batch); break;
+    case 2: gemm_gfx12_kernel<Bits, Act8, 2><<<grid, 256, 0, stream>>>(w, ws, act, as, out, rows, columns, batch); break;
+    case 3: gemm_gfx12_kernel<Bits, Act8, 3><<<grid, 256, 0, stream>>>(w, ws, act, as, out, rows, columns, batch); break;
+    default: gemm_gfx12_kernel<Bits, Act8, 4><<<grid, 256, 0, stream>>>(w, ws, act, as, out, rows, columns, batch); break;
+  }
+}
+
+int gfx12_gemm(int format, const std::uint8_t* w, const std::uint16_t* ws, const std::uint8_t* act,
+               const std::uint16_t* as, float* out, std::size_t rows, std::size_t columns,
+               unsigned batch, bool act8, cudaStream_t stream) {
+  const int shape = validate_matrix_shape(format, rows, columns);
+  if (shape != GFXB_OK) return shape;
+  GFXB_REQUIRE(w != nullptr && ws != nullptr && act != nullptr && as != nullptr && out != nullptr,
+               "gfx12 GEMM requires non-null buffers");
+  GFXB_REQUIRE(batch >= 1 && batch <= 32, "gfx12 GEMM batch must be in [1, 32]");
+  const auto* scales = reinterpret_cast<const __half*>(ws);
+  const auto* act_scales = reinterpret_cast<const __half*>(as);
+  const auto r = static_cast<std::uint32_t>(rows), k = static_cast<std::uint32_t>(columns);
+  const int bits = bits_of(format);
+  if (act8) {
+    if (bits == 2) launch_gfx12_bits<2, true>(w, scales, act, act_scales, out, r, k, batch, stream);
+    else if (bits == 3) launch_gfx12_bits<3, true>(w, scales, act, act_scales, out, r, k, batch, stream);
+    else launch_gfx12_bits<4, true>(w, scales, act, act_scales, out, r, k, batch, stream);
+  } else {
+    if (bits == 2) launch_gfx12_bits<2, false>(w, scales, act, act_scales, out, r, k, batch, stream);
+    else if (bits == 3) launch_gfx12_bits<3, false>(w, scales, act, act_scales, out, r, k, batch, stream);
+    else launch_gfx12_bits<4, false>(w, scales, act, act_scales, out, r, k, batch, stream);
+  }
+  return launch_status("gfx12 GEMM launch failed");
+}
+
+}  // namespace
+
+// Exposed to the host runtime (engine weight generation).
+int generate_b200_weights(std::uint64_t seed, std::uint32_t tensor, int format, std::uint8_t* codes,
+                          std::size_t rows, std::size_t columns, cudaStream_t stream) {
+  const int shape = validate_matrix_shape(format, rows, columns);
+  if (shape != GFXB_OK) return shape;
+  const int bits = bits_of(format);
+  return launch_write_b200(HashSource{seed, tensor, static_cast<std::uint32_t>(columns), bits}, codes,
+                           rows, columns, bits, stream);
+}
+
+}  // namespace gfxb
+
+using namespace gfxb;
+
+extern "C" int gfxb_repack_rowmajor_to_b200(int format, const std::uint8_t* rowmajor_codes,
+                                            std::uint8_t* b200_codes, std::size_t rows,
+                                            std::size_t columns, void* stream) {
+  const int shape = validate_matrix_shape(format, rows, columns);
+  if (shape != GFXB_OK) return shape;
+  GFXB_REQUIRE(rowmajor_codes != nullptr && b200_codes != nullptr, "repack requires non-null buffers");
+  const int bits = bits_of(format);
+  return launch_write_b200(RowMajorSource{rowmajor_codes, static_cast<std::uint32_t>(columns), bits},
+                           b200_codes, rows, columns, bits, as_stream(stream));
+}
+
+extern "C" int gfxb_repack_gfx12_to_b200(int format, const std::uint8_t* gfx12_codes,
+                                         std::uint8_t* b200_codes, std::size_t rows,
+                                         std::size_t columns, void* stream) {
+  const int shape = validate_matrix_shape(format, rows, columns);
+  if (shape != GFXB_OK) return shape;
+  GFXB_REQUIRE(gfx12_codes != nullptr && b200_codes != nullptr, "repack requires non-null buffers");
+  const int bits = bits_of(format);
+  return launch_write_b200(Gfx12Source{gfx12_codes, static_cast<std::uint32_t>(columns), bits},
+                           b200_codes, rows, columns, bits, as_stream(stream));
+}
+
+extern "C" int gfxb_tile_scales(const std::uint16_t* rowmajor_scales, std::uint16_t* tiled_scales,
+                                std::size_t rows, std::size_t columns, void* stream) {
+  GFXB_REQUIRE(rowmajor_scales != nullptr && tiled_scales != nullptr, "scale tiling requires buffers");
+  GFXB_REQUIRE(rows % 16 == 0 && rows > 0 && columns % kGroup == 0 && columns > 0,
+               "scale tiling needs N divisible by 16 and K divisible by 128");
+  const std::uint64_t total = rows * (columns / kGroup);
+  tile_scales_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, as_stream(stream)>>>(
+      reinterpret_cast<const __half*>(rowmajor_scales), reinterpret_cast<__half*>(tiled_scales),
+      static_cast<std::uint32_t>(rows), static_cast<std::uint32_t>(columns / kGroup));
+  return launch_status("scale tiling launch failed");
+}
+
+extern "C" int gfxb_pack_activation(int activation_bits, const std::uint16_t* input, std::int8_t* codes,
+                                    std::uint16_t* scales, std::int32_t* sums, std::uint8_t* packed_a4,
+                                    std::size_t columns, unsigned batch, void* stream) {
+  GFXB_REQUIRE(activation_bits == 4 || activation_bits == 8, "activation bits must be 4 or 8");
+  GFXB_REQUIRE(input != nullptr && codes != nullptr && scales != nullptr && sums != nullptr,
+               "activation packing requires non-null buffers");
+  GFXB_REQUIRE(columns > 0 && columns % kGroup == 0 && batch >= 1 && batch <= 32,
+               "activation packing requires batch in [1,32] and K divisible by 128");
+  const std::uint32_t groups = static_cast<std::uint32_t>(columns / kGroup);
+  const dim3 grid(groups * batch);
+  const auto* in = reinterpret_cast<const __half*>(input);
+  auto* s = reinterpret_cast<__half*>(scales);
+  if (activation_bits == 4) {
+    pack_activation_kernel<4><<<grid, 128, 0, as_stream(stream)>>>(
+        in, codes, s, sums, packed_a4, static_cast<std::uint32_t>(columns), groups);
+  } else {
+    pack_activation_kernel<8><<<grid, 128, 0, as_stream(stream)>>>(
+        in, codes, s, sums, nullptr, static_cast<std::uint32_t>(columns), groups);
+  }
+  return launch_status("activation packing launch failed");
+}
+
+extern "C" int gfxb_lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, unsigned matrix_count,
+                                const std::int8_t* act_codes, const std::uint16_t* act_scales,
+                                const std::int32_t* act_sums, std::size_t columns, unsigned batch,
+                                void* stream) {
+  GFXB_REQUIRE(matrices != nullptr && matrix_count >= 1 && matrix_count <= 4,
+               "GEMV takes between one and four matrices");
+  GFXB_REQUIRE(act_codes != nullptr && act_scales != nullptr && act_sums != nullptr,
+               "GEMV requires an activation pack");
+  GFXB_REQUIRE(batch >= 1 && batch <= 32, "GEMV batch must be in [1, 32]");
+  GemvArgs args{};
+  std::uint64_t total_tiles = 0;
+  for (unsigned i = 0; i < matrix_count; ++i) {
+    const int shape = validate_matrix_shape(format, matrices[i].rows, columns);
+    if (shape != GFXB_OK) return shape;
+    GFXB_REQUIRE(matrices[i].codes != nullptr && matrices[i].scales != nullptr &&
+                     matrices[i].output != nullptr,
+                 "GEMV matrix binding is invalid");
+    args.m[i].codes = matrices[i].codes;
+    args.m[i].scales = reinterpret_cast<const __half*>(matrices[i].scales);
+    args.m[i].output = matrices[i].output;
+    args.m[i].tiles = static_cast<std::uint32_t>(matrices[i].rows / 16);
+    args.m[i].output_f16 = matrices[i].output_f16 != 0;
+    total_tiles += args.m[i].tiles;
+  }
+  GFXB_REQUIRE(total_tiles <= 0x7fffffffull, "GEMV grid is too large");
+  args.count = matrix_count;
+  args.act = act_codes;
+  args.act_scales = reinterpret_cast<const __half*>(act_scales);
+  args.act_sums = act_sums;
+  args.columns = static_cast<std::uint32_t>(columns);
+  args.groups = static_cast<std::uint32_t>(columns / kGroup);
+  args.batch = batch;
+  const int bits = bits_of(format);
+  const unsigned grid = static_cast<unsigned>(total_tiles);
+  if (bits == 2) launch_gemv_bits<2>(args, grid, as_stream(stream));
+  else if (bits == 3) launch_gemv_bits<3>(args, grid, as_stream(stream));
+  else launch_gemv_bits<4>(args, grid, as_stream(stream));
+  return launch_status("low-bit GEMV launch failed");
+}
+
+extern "C" int gfxb_quantize_activation_i4(const std::uint16_t* input, std::uint8_t* packed_output,
+                                           std::uint16_t* scales, std::size_t columns, unsigned batch,
+                                           void* stream) {
+  GFXB_REQUIRE(input != nullptr && packed_output != nullptr && scales != nullptr && columns > 0 &&
+                   columns % kGroup == 0 && batch >= 1 && batch <= 32,
+               "A4 quantization requires non-null buffers, batch in [1,32], and K divisible by 128");
+  const std::uint32_t groups = static_cast<std::uint32_t>(columns / kGroup);
+  quantize_reference_kernel<4><<<groups * batch, 128, 0, as_stream(stream)>>>(
+      reinterpret_cast<const __half*>(input), packed_output, reinterpret_cast<__half*>(scales),
+      static_cast<std::uint32_t>(columns), groups);
+  return launch_status("A4 activation quantization launch failed");
+}
+
+extern "C" int gfxb_quantize_activation_i8(const std::uint16_t* input, std::int8_t* quantized_output,
+                                           std::uint16_t* scales, std::size_t columns, unsigned batch,
+                                           void* stream) {
+  GFXB_REQUIRE(input != nullptr && quantized_output != nullptr && scales != nullptr && columns > 0 &&
+                   columns % kGroup == 0 && batch >= 1 && batch <= 32,
+               "A8 quantization requires non-null buffers, batch in [1,32], and K divisible by 128");
+  const std::uint32_t groups = static_cast<std::uint32_t>(columns / kGroup);
+  quantize_reference_kernel<8><<<groups * batch, 128, 0, as_stream(stream)>>>(
+      reinterpret_cast<const __half*>(input), reinterpret_cast<std::uint8_t*>(quantized_output),
+      reinterpret_cast<__half*>(scales), static_cast<std::uint32_t>(columns), groups);
+  return launch_status("A8 activation quantization launch failed");
+}
+
+extern "C" int gfxb_gfx12_i4_gemm(int format, const std::uint8_t* tiled_weights,
+                                  const std::uint16_t* tiled_weight_scales,
+                                  const std::uint8_t* packed_activations,
+                                  const std::uint16_t* activation_scales, float* output, std::size_t rows,
+                                  std::size_t columns, unsigned batch, int sequential_w3, void* stream) {
+  if (format == GFXB_W3 && !sequential_w3) {
+    return fail(GFXB_UNSUPPORTED, "only the sequential W3 fragment order is supported");
+  }
+  return gfx12_gemm(format, tiled_weights, tiled_weight_scales, packed_activations, activation_scales,
+                    output, rows, columns, batch, false, as_stream(stream));
+}
+
+extern "C" int gfxb_gfx12_i8_gemm(int format, const std::uint8_t* tiled_weights,
+                                  const std::uint16_t* tiled_weight_scales,
+                                  const std::int8_t* quantized_activations,
+                                  const std::uint16_t* activation_scales, float* output, std::size_t rows,
+                                  std::size_t columns, unsigned batch, void* stream) {
+  return gfx12_gemm(format, tiled_weights, tiled_weight_scales,
+                    reinterpret_cast<const std::uint8_t*>(quantized_activations), activation_scales,
+                    output, rows, columns, batch, true, as_stream(stream));
+}

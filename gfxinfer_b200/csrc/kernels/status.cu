@@ -1,0 +1,65 @@
+// Error plumbing for the C ABI: gfxb_status codes plus a per-thread message,
+// the C counterpart of the reference's Status (include/gfxinfer/status.h).
+#include <string>
+
+#include "common.cuh"
+
+namespace gfxb {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+void set_error(const char* message) { g_last_error = message != nullptr ? message : ""; }
+
+void set_error_cuda(cudaError_t error, const char* context) {
+  g_last_error = std::string(context) + ": " + cudaGetErrorString(error);
+}
+
+int fail(int status, const char* message) {
+  set_error(message);
+  return status;
+}
+
+int launch_status(const char* context) {
+  const cudaError_t error = cudaGetLastError();
+  if (error == cudaSuccess) return GFXB_OK;
+  set_error_cuda(error, context);
+  return error == cudaErrorMemoryAllocation ? GFXB_OUT_OF_MEMORY : GFXB_CUDA_ERROR;
+}
+
+}  // namespace gfxb
+
+extern "C" const char* gfxb_last_error_message(void) { return gfxb::g_last_error.c_str(); }
+
+extern "C" int gfxb_abi_version(void) { return 1; }
+
+extern "C" int gfxb_require_sm100_device(int device_index, gfxb_device_info* info) {
+  int count = 0;
+  cudaError_t error = cudaGetDeviceCount(&count);
+  if (error != cudaSuccess) {
+    gfxb::set_error_cuda(error, "CUDA device enumeration failed");
+    return GFXB_CUDA_ERROR;
+  }
+  if (device_index < 0 || device_index >= count) {
+    return gfxb::fail(GFXB_INVALID_ARGUMENT, "requested CUDA device index is out of range");
+  }
+  cudaDeviceProp properties{};
+  error = cudaGetDeviceProperties(&properties, device_index);
+  if (error != cudaSuccess) {
+    gfxb::set_error_cuda(error, "CUDA device query failed");
+    return GFXB_CUDA_ERROR;
+  }
+  if (info != nullptr) {
+    info->index = device_index;
+    info->compute_major = properties.major;
+    info->compute_minor = properties.minor;
+    info->multiprocessors = properties.multiProcessorCount;
+    info->global_memory_bytes = properties.totalGlobalMem;
+    std::snprintf(info->name, sizeof info->name, "%s", properties.name);
+  }
+  if (properties.major != 10 || properties.minor != 0) {
+    return gfxb::fail(GFXB_UNSUPPORTED, "gfxinfer-b200 requires an sm_100 (B200) device");
+  }
+  return GFXB_OK;
+}
