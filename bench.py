@@ -1,0 +1,314 @@
+"""Benchmark: batch-1 W3A4 decode tokens/s of the 64-layer config-2 model on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = one greedy decode token (64 layers + LM head + argmax) of the
+BASELINE config-2 model (hidden 5120, MLP 17408 W3, GDN/attention W4, W4 LM
+head over vocab 151936, A4 activations, context 512) with seeded random-init
+weights and a 64-token uniform-random prompt. N > 1 runs tensor parallelism
+over N GPUs (one process per GPU under torchrun, NCCL all-reduce), so the
+total work per token is fixed: "scaling": "strong".
+
+value: K greedy steps replayed back to back from device memory (each step's
+argmax feeds the next), CUDA events on the session stream, max over ranks.
+e2e:   K steps through the public greedy_step call: pinned host token in,
+       host token out, synchronised every step.
+The weights (11.2 GB) exceed L2 (126 MB), so no flush is needed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "batch-1 W3A4 decode tokens/s"
+UNIT = "tokens/s"
+
+
+def _config_dict():
+    from gfxinfer_b200.session import CONFIG2
+
+    return dict(CONFIG2)
+
+
+def _kernels_per_step(cfg: dict, tp: int) -> int:
+    layers = cfg["layers"]
+    attention = layers // cfg["attention_interval"]
+    gdn = layers - attention
+    per_gdn, per_attention = 9, 10  # see gfxinfer_b200/csrc/host/runtime.cu enqueue_forward
+    head = 1 + 2 + (2 if tp > 1 else 0)  # LM-head GEMV, argmax (2), TP exchange/select
+    return 1 + gdn * per_gdn + attention * per_attention + head + 1  # embed+norm ... advance
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int) -> None:
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_baseline(steps_tokens: int = 2) -> dict:
+    """The oracle's scalar forward (C, OpenMP) on this host: 4 of the 64 layers (3 GDN + 1 attention)
+    and the LM head at full config-2 width; layer time scaled x16 to the full depth."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from oracle_lib import Oracle, model_config
+
+    oracle = Oracle()
+    cfg = model_config(max_context=64)
+    start = time.perf_counter()
+    seconds_per_token = oracle.lib.or_time_layers(cfg, 3, 1, 1, steps_tokens)
+    wall = time.perf_counter() - start
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": round(1.0 / seconds_per_token, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": (f"{steps_tokens} greedy tokens through 4 of 64 config-2 layers (3 GDN + 1 attention) "
+                       f"and the full LM head at full width; layer time x16 + head time per token "
+                       f"(sample wall {wall:.1f}s incl. weight generation)")}
+
+
+def run_reference(args) -> None:
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    base = cpu_baseline(1)
+    per_step = 1.0 / base["value"]
+    # W warm-up + K timed "steps": each step is one bounded sample token of the CPU forward.
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from oracle_lib import Oracle, model_config
+
+    oracle = Oracle()
+    cfg = model_config(max_context=64)
+    samples = []
+    for i in range(args.warmup + args.steps):
+        t = oracle.lib.or_time_layers(cfg, 3, 1, 1, 1)
+        if i >= args.warmup:
+            samples.append(t)
+    tokens_per_s = 1.0 / statistics.mean(samples)
+    line = {"impl": "reference", "metric": METRIC, "value": round(tokens_per_s, 4), "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1000.0 * statistics.mean(samples), 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
+            "config": {"workload": "config-2 decode: 64-layer hybrid GDN/attention, hidden 5120, MLP 17408 W3, "
+                                   "W4 projections and LM head (vocab 151936), A4, ctx 512",
+                       "seq_len": 512, "global_batch": 1, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(tokens_per_s, 4), "unit": UNIT, "cores": base["cores"], "kind": "port",
+                             "sample": base["sample"]},
+            "e2e": {"value": round(tokens_per_s, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    del per_step
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args) -> None:
+    import numpy as np
+    import torch
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    from gfxinfer_b200 import build
+
+    if rank == 0 and not os.path.exists(os.path.join(ROOT, "gfxinfer_b200", "libgfxb200.so")):
+        build.build()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    from gfxinfer_b200 import session as gs
+
+    cfg = _config_dict()
+    nccl_id = None
+    if world > 1:
+        import torch.distributed as dist
+
+        holder = [gs.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(holder, src=0)
+        nccl_id = holder[0]
+    engine = gs.Engine.create(gs.model_config(**cfg), device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id,
+                              include_mtp=False)
+    session = gs.QwenDecodeSession.create(engine, maximum_context_tokens=cfg["max_context"])
+    stream = torch.cuda.ExternalStream(session.stream(), device=torch.device("cuda", local))
+    rng = np.random.default_rng(cfg["seed"])
+    prompt = [int(t) for t in rng.integers(0, cfg["vocab"], size=64)]
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    token = None
+    for t in prompt:  # serial prefill through the public step, as the reference does
+        token = session.greedy_step(t)
+    for _ in range(args.warmup):
+        token = session.greedy_step(token)
+
+    # --- value: device-resident greedy loop -----------------------------------
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        session.enqueue_greedy(token, args.steps)
+        stop.record(stream)
+        stop.synchronize()
+    barrier()
+    device_ms = start.elapsed_time(stop)
+    token = session.last_token()
+
+    # --- e2e: public greedy_step with host buffers ------------------------------
+    for _ in range(args.warmup):
+        token = session.greedy_step(token)
+    barrier()
+    start.record(stream)
+    for _ in range(args.steps):
+        token = session.greedy_step(token)
+    stop.record(stream)
+    stop.synchronize()
+    barrier()
+    e2e_ms = start.elapsed_time(stop)
+
+    # --- dominant kernel: W3 MLP gate+up GEMV in isolation -------------------------
+    launches = 96
+    gemv_start, gemv_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    session.enqueue_gemv(0, 8)
+    torch.cuda.synchronize()
+    gemv_start.record(stream)
+    gemv_bytes = session.enqueue_gemv(0, launches)
+    gemv_stop.record(stream)
+    gemv_stop.synchronize()
+    gemv_us = gemv_start.elapsed_time(gemv_stop) * 1000.0 / launches
+
+    times = torch.tensor([device_ms, e2e_ms, gemv_us], dtype=torch.float64, device="cuda")
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    device_ms, e2e_ms, gemv_us = times.tolist()
+    if rank == 0:
+        peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+        peak, peak_note = 6650.0, "fallback"
+        if os.path.exists(peaks_path):
+            with open(peaks_path) as f:
+                peak = float(json.load(f)["hbm_gbs"])
+            peak_note = "measured"
+        achieved = gemv_bytes / (gemv_us * 1e-6) / 1e9
+        per_step_bytes = engine.weight_bytes()
+        line = {
+            "metric": METRIC, "value": round(args.steps / (device_ms / 1000.0), 3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(device_ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded random-init weights, random prompt)",
+            "config": {"workload": "config-2 decode: 64-layer hybrid (48 GDN + 16 gated GQA), hidden 5120, "
+                                   "MLP 17408 W3, GDN/attention W4, W4 LM head vocab 151936, A4, batch 1, ctx 512",
+                       "global_batch": 1, "seq_len": cfg["max_context"], "parallelism": f"tp{world}",
+                       "prompt_tokens": 64, "l2": "weights 11.2 GB per token >> 126 MB L2; no flush needed"},
+            "e2e": {"value": round(args.steps / (e2e_ms / 1000.0), 3), "unit": UNIT,
+                    "h2d_bytes_per_step": 4 + 8, "d2h_bytes_per_step": 4},
+            "gpu_launches": _kernels_per_step(cfg, world) * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "W3A4 MLP gate+up GEMV [2x17408x5120] (one launch)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_note, "traffic": None,
+                         "algorithmic_bytes_per_launch": gemv_bytes, "launch_us": round(gemv_us, 3)},
+            "decode_roofline": {"weight_bytes_per_token_per_gpu": per_step_bytes,
+                                "achieved_GBps_per_gpu": round(per_step_bytes / (device_ms / args.steps / 1000.0) / 1e9, 1),
+                                "frac": round(per_step_bytes / (device_ms / args.steps / 1000.0) / 1e9 / peak, 4)},
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(2)
+        print(json.dumps(line), flush=True)
+    session.close()
+    engine.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=128)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if 64 + 2 * (args.warmup + args.steps) > 512:
+        parser.error("prompt + warm-up + timed steps exceed the 512-token context")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

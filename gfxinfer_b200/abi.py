@@ -17,6 +17,17 @@ class GemvMatrix(ctypes.Structure):
 
 P = c_void_p
 
+class ModelConfig(ctypes.Structure):
+    _fields_ = [(name, c_uint32) for name in (
+        "hidden", "intermediate", "layers", "attention_interval", "gdn_key_heads", "gdn_value_heads",
+        "q_heads", "kv_heads", "vocab", "draft_vocab", "mlp_bits", "proj_bits", "head_bits", "emb_bits",
+        "activation_bits", "max_context")] + [("seed", c_uint64)]
+
+
+class SessionConfig(ctypes.Structure):
+    _fields_ = [("maximum_context_tokens", c_uint32), ("graph_verifier_batch", c_uint32), ("use_graphs", c_uint32)]
+
+
 # name -> (restype, argtypes); kept in declaration order of include/gfxb/gfxb.h.
 SIGNATURES: dict[str, tuple] = {
     "gfxb_last_error_message": (c_char_p, []),
@@ -31,6 +42,36 @@ SIGNATURES: dict[str, tuple] = {
     "gfxb_quantize_activation_i8": (c_int, [P, P, P, c_size_t, c_uint, P]),
     "gfxb_gfx12_i4_gemm": (c_int, [c_int, P, P, P, P, P, c_size_t, c_size_t, c_uint, c_int, P]),
     "gfxb_gfx12_i8_gemm": (c_int, [c_int, P, P, P, P, P, c_size_t, c_size_t, c_uint, P]),
+    "gfxb_residual_rms_norm_pack": (c_int, [P, P, P, P, P, c_size_t, c_uint, ctypes.c_float, c_int, c_int, P, P, P, P, P]),
+    "gfxb_silu_multiply_pack": (c_int, [P, P, c_size_t, c_uint, P, c_int, P, P, P, P, P]),
+    "gfxb_gdn_conv_update": (c_int, [P, P, P, P, P, P, c_size_t, c_uint, P]),
+    "gfxb_gdn_recurrent": (c_int, [P] * 13 + [c_uint, c_uint, c_uint, P]),
+    "gfxb_gdn_restore_prefix_all": (c_int, [P] * 6 + [c_size_t, c_uint, c_uint, c_uint, c_uint, c_uint, P]),
+    "gfxb_rope_table": (c_int, [c_size_t, c_uint, ctypes.c_float, P, P]),
+    "gfxb_qk_rms_norm_rope": (c_int, [P, P, P, c_uint, c_size_t, P, P, P, c_uint, c_size_t, c_uint, P, P, c_size_t,
+                                      c_uint64, P, c_uint, P, P, P, c_size_t, P]),
+    "gfxb_gated_attention_scratch_bytes": (c_size_t, [c_uint, c_size_t, c_uint]),
+    "gfxb_gated_attention": (c_int, [P, P, P, P, P, c_size_t, P, c_size_t, c_uint, c_uint, c_uint, P, c_size_t, P]),
+    "gfxb_argmax_scratch_bytes": (c_size_t, [c_uint]),
+    "gfxb_argmax": (c_int, [P, P, P, c_size_t, c_size_t, c_uint, P, c_size_t, P]),
+    "gfxb_read_device_errors": (c_int, [POINTER(c_uint32)]),
+    "gfxb_nccl_unique_id": (c_int, [P]),
+    "gfxb_engine_create_synthetic": (c_int, [POINTER(ModelConfig), c_int, c_int, c_int, P, c_int, POINTER(c_void_p)]),
+    "gfxb_engine_destroy": (c_int, [P]),
+    "gfxb_engine_weight_bytes": (c_int, [P, POINTER(c_uint64)]),
+    "gfxb_session_create": (c_int, [P, POINTER(SessionConfig), POINTER(c_void_p)]),
+    "gfxb_session_destroy": (c_int, [P]),
+    "gfxb_session_greedy_step": (c_int, [P, c_uint32, POINTER(c_uint32)]),
+    "gfxb_session_block_step": (c_int, [P, POINTER(c_uint32), c_uint, POINTER(c_uint32)]),
+    "gfxb_session_mtp_draft": (c_int, [P, c_uint32, POINTER(c_uint32)]),
+    "gfxb_session_speculative_step": (c_int, [P, c_uint32, c_uint, POINTER(c_uint32), POINTER(c_uint), POINTER(c_uint)]),
+    "gfxb_session_position": (c_int, [P, POINTER(c_uint64)]),
+    "gfxb_session_enqueue_greedy": (c_int, [P, c_uint32, c_uint]),
+    "gfxb_session_sync": (c_int, [P]),
+    "gfxb_session_last_token": (c_int, [P, POINTER(c_uint32)]),
+    "gfxb_session_stream": (c_void_p, [P]),
+    "gfxb_session_enqueue_gemv": (c_int, [P, c_int, c_uint, POINTER(c_uint64)]),
+    "gfxb_session_read_state": (c_int, [P, P, P, c_size_t]),
 }
 
 

@@ -1,0 +1,1251 @@
+// Engine and decode session: the B200 counterpart of the reference's
+// src/engine.cpp and src/qwen_runtime.cpp.
+//
+// Engine: one device arena per GPU holding every weight of the model (or of
+// this rank's tensor-parallel shard), generated on the device from a seed.
+// Session: one arena of activations, recurrent states, KV caches and logs;
+// the 64-layer forward for a causal block of 1..32 tokens; the greedy step as
+// a replayed CUDA graph that reads its token and position from device memory;
+// MTP drafting and the speculative verify/rollback transaction.
+//
+// Tensor parallelism (absent in the reference): column-parallel projections
+// (GDN qkv/z, attention q/k/v, MLP gate/up, LM-head vocabulary rows) and
+// row-parallel ones (GDN out, attention o, MLP down, MTP fc) with one NCCL
+// all-reduce of the fp32 partial output, captured inside the graph.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gfxb/gfxb.h"
+#include "kernels/common.cuh"
+#include "kernels/ops.cuh"
+
+namespace gfxb {
+
+int lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, unsigned matrix_count, const std::int8_t* act_codes,
+                const std::uint16_t* act_scales, const std::int32_t* act_sums, std::size_t columns,
+                std::size_t act_stride, unsigned batch, cudaStream_t stream);
+int generate_b200_weights(std::uint64_t seed, std::uint32_t tensor, int format, std::uint8_t* codes,
+                          std::uint16_t* tiled_scales, std::size_t rows, std::size_t columns,
+                          std::size_t global_columns, std::size_t column_offset, const std::uint32_t* segment_local,
+                          const std::uint32_t* segment_global, std::uint32_t segments, cudaStream_t stream);
+int generate_rowmajor_weights(std::uint64_t seed, std::uint32_t tensor, int format, std::uint8_t* codes,
+                              std::uint16_t* scales, std::size_t rows, std::size_t columns, cudaStream_t stream);
+int generate_bf16(std::uint64_t seed, std::uint32_t tensor, std::uint64_t offset, std::uint64_t count, float lo,
+                  float hi, std::uint16_t* out, cudaStream_t stream);
+int read_gemv_error(std::uint32_t* value, bool clear);
+
+namespace {
+
+#define GFXB_TRY(expression)              \
+  do {                                    \
+    const int status_ = (expression);     \
+    if (status_ != GFXB_OK) return status_; \
+  } while (0)
+
+int cuda_check(cudaError_t error, const char* context) {
+  if (error == cudaSuccess) return GFXB_OK;
+  set_error_cuda(error, context);
+  return error == cudaErrorMemoryAllocation ? GFXB_OUT_OF_MEMORY : GFXB_CUDA_ERROR;
+}
+
+// ---------------------------------------------------------------------------
+// NCCL, resolved at run time (the process usually has it loaded already).
+// ---------------------------------------------------------------------------
+
+struct NcclApi {
+  void* handle = nullptr;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+int load_nccl(NcclApi& api) {
+  if (api.handle != nullptr) return GFXB_OK;
+  const char* names[] = {"libnccl.so.2", "libnccl.so"};
+  for (const char* name : names) {
+    api.handle = dlopen(name, RTLD_NOW | RTLD_GLOBAL);
+    if (api.handle != nullptr) break;
+  }
+  if (api.handle == nullptr) return fail(GFXB_UNSUPPORTED, "NCCL (libnccl.so.2) could not be loaded");
+  api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(api.handle, "ncclGetUniqueId"));
+  api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(api.handle, "ncclCommInitRank"));
+  api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(api.handle, "ncclCommDestroy"));
+  api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(api.handle, "ncclAllReduce"));
+  api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(api.handle, "ncclAllGather"));
+  api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(api.handle, "ncclGetErrorString"));
+  if (!api.get_unique_id || !api.comm_init_rank || !api.comm_destroy || !api.all_reduce || !api.all_gather) {
+    return fail(GFXB_UNSUPPORTED, "NCCL is missing required entry points");
+  }
+  return GFXB_OK;
+}
+
+NcclApi& nccl() {
+  static NcclApi api;
+  return api;
+}
+
+int nccl_check(ncclResult_t result, const char* context) {
+  if (result == ncclSuccess) return GFXB_OK;
+  std::string message = std::string(context) + ": " +
+                        (nccl().error_string ? nccl().error_string(result) : "NCCL error");
+  set_error(message.c_str());
+  return GFXB_CUDA_ERROR;
+}
+
+// ---------------------------------------------------------------------------
+// synthetic model: tensor ids shared with the CPU oracle
+// ---------------------------------------------------------------------------
+
+enum Kind : std::uint32_t {
+  kInputNorm = 0, kPostNorm, kGate, kUp, kDown,
+  kQkv, kZ, kA, kB, kConv, kALog, kDtBias, kGdnNorm, kGdnOut,
+  kQ, kK, kV, kQNorm, kKNorm, kO,
+  kFc, kPreEmbNorm, kPreHiddenNorm, kMtpFinalNorm
+};
+constexpr std::uint32_t kLayerGlobal = 4096, kLayerMtp = 4097;
+constexpr std::uint32_t kEmbedding = 0, kFinalNorm = 1, kLmHead = 2;
+constexpr unsigned kMaxBlock = 32;
+
+std::uint32_t tensor_id(std::uint32_t layer, std::uint32_t kind) { return layer * 32u + kind; }
+int format_of(std::uint32_t bits) { return bits == 2 ? GFXB_W2 : (bits == 3 ? GFXB_W3 : GFXB_W4); }
+
+struct QMatrix {
+  std::uint8_t* codes = nullptr;
+  std::uint16_t* scales = nullptr;
+  std::uint32_t rows = 0, cols = 0;
+  int format = 0;
+};
+
+struct Layer {
+  bool attention = false;
+  std::uint32_t state_index = 0;
+  std::uint16_t *input_norm = nullptr, *post_norm = nullptr;
+  QMatrix gate, up, down;
+  QMatrix qkv, z, a, b, out;
+  std::uint16_t *conv = nullptr, *a_log = nullptr, *dt_bias = nullptr, *gdn_norm = nullptr;
+  QMatrix q, k, v;
+  std::uint16_t *q_norm = nullptr, *k_norm = nullptr;
+};
+
+struct Shard {
+  std::uint32_t tp = 1, rank = 0;
+  std::uint32_t nk = 0, kh0 = 0, nv = 0, vh0 = 0;   // GDN key/value heads of this rank
+  std::uint32_t nq = 0, qh0 = 0, nkv = 0, kv0 = 0;  // attention heads of this rank
+  std::uint32_t inter = 0, i0 = 0;                  // MLP intermediate slice
+  std::uint32_t vocab = 0, v0 = 0;                  // LM-head rows
+  std::uint32_t fc_cols = 0, fc0 = 0;               // MTP fc K slice
+  std::uint32_t channels = 0;                       // GDN conv channels of this rank
+};
+
+struct Planner {
+  std::byte* base = nullptr;
+  std::size_t offset = 0;
+  template <class T>
+  T* take(std::size_t count) {
+    const std::size_t at = (offset + 255u) & ~static_cast<std::size_t>(255u);
+    offset = at + count * sizeof(T);
+    return base != nullptr ? reinterpret_cast<T*>(base + at) : nullptr;
+  }
+};
+
+}  // namespace
+}  // namespace gfxb
+
+struct gfxb_engine {
+  gfxb_model_config cfg{};
+  int device = 0;
+  bool has_mtp = false;
+  gfxb::Shard shard;
+  std::byte* arena = nullptr;
+  std::size_t arena_bytes = 0;
+  std::vector<gfxb::Layer> layers;
+  gfxb::Layer mtp;
+  std::uint8_t* emb_codes = nullptr;
+  std::uint16_t* emb_scales = nullptr;
+  gfxb::QMatrix lm_head, fc;
+  std::uint16_t *final_norm = nullptr, *pre_emb_norm = nullptr, *pre_hidden_norm = nullptr,
+                *mtp_final_norm = nullptr;
+  cudaStream_t stream = nullptr;
+  ncclComm_t comm = nullptr;
+  std::uint32_t gdn_layers = 0, attention_layers = 0;
+};
+
+namespace gfxb {
+namespace {
+
+int validate_config(const gfxb_model_config& c, std::uint32_t tp) {
+  auto bad = [](const char* message) { return fail(GFXB_INVALID_ARGUMENT, message); };
+  if (c.hidden == 0 || c.hidden % 256 != 0 || c.hidden / 256 > 40) return bad("hidden must be a multiple of 256");
+  if (c.intermediate % (128 * tp) != 0 || (c.intermediate / tp) % 16 != 0) return bad("intermediate must split into 128-column shards");
+  if (c.layers == 0 || c.attention_interval == 0) return bad("layer count must be positive");
+  if (c.gdn_key_heads == 0 || c.gdn_value_heads % c.gdn_key_heads != 0) return bad("GDN value heads must be a multiple of key heads");
+  if (c.gdn_key_heads % tp != 0 || c.gdn_value_heads % tp != 0) return bad("GDN heads must divide by the TP size");
+  if (c.gdn_value_heads % 16 != 0) return bad("GDN value heads must be a multiple of 16 (a/b projection tiles)");
+  if (c.q_heads % tp != 0 || c.kv_heads == 0 || c.q_heads % c.kv_heads != 0 || c.q_heads / c.kv_heads > 8) return bad("invalid attention head counts");
+  if (c.vocab % (16 * tp) != 0) return bad("vocabulary must split into 16-row shards");
+  if ((2 * c.hidden / tp) % 128 != 0) return bad("MTP fc input must split into 128-column shards");
+  if (c.activation_bits != 4 && c.activation_bits != 8) return bad("activation bits must be 4 or 8");
+  for (std::uint32_t bits : {c.mlp_bits, c.proj_bits, c.head_bits}) {
+    if (bits < 2 || bits > 4) return bad("weight bits must be 2, 3 or 4");
+  }
+  if (c.emb_bits != 2 && c.emb_bits != 4) return bad("embedding bits must be 2 or 4");
+  if (c.max_context == 0) return bad("maximum context must be positive");
+  return GFXB_OK;
+}
+
+Shard make_shard(const gfxb_model_config& c, std::uint32_t tp, std::uint32_t rank) {
+  Shard s;
+  s.tp = tp;
+  s.rank = rank;
+  s.nk = c.gdn_key_heads / tp;
+  s.kh0 = rank * s.nk;
+  s.nv = c.gdn_value_heads / tp;
+  s.vh0 = rank * s.nv;
+  s.nq = c.q_heads / tp;
+  s.qh0 = rank * s.nq;
+  const std::uint32_t group = c.q_heads / c.kv_heads;
+  s.kv0 = s.qh0 / group;
+  s.nkv = (s.qh0 + s.nq - 1) / group - s.kv0 + 1;
+  s.inter = c.intermediate / tp;
+  s.i0 = rank * s.inter;
+  s.vocab = c.vocab / tp;
+  s.v0 = rank * s.vocab;
+  s.fc_cols = 2 * c.hidden / tp;
+  s.fc0 = rank * s.fc_cols;
+  s.channels = 2 * s.nk * 128 + s.nv * 128;
+  return s;
+}
+
+// Plans (pass 1) or places and generates (pass 2) every weight of the shard.
+int build_weights(gfxb_engine& e, Planner& plan, bool generate) {
+  const gfxb_model_config& c = e.cfg;
+  const Shard& s = e.shard;
+  const cudaStream_t stream = e.stream;
+  const std::uint64_t seed = c.seed;
+  auto matrix = [&](QMatrix& m, std::uint32_t tensor, std::uint32_t bits, std::uint32_t rows, std::uint32_t cols,
+                    std::uint32_t global_cols, std::uint32_t col_offset, std::vector<std::uint32_t> local_begin,
+                    std::vector<std::uint32_t> global_begin) -> int {
+    m.format = format_of(bits);
+    m.rows = rows;
+    m.cols = cols;
+    m.codes = plan.take<std::uint8_t>(static_cast<std::size_t>(rows) * cols * bits / 8);
+    m.scales = plan.take<std::uint16_t>(static_cast<std::size_t>(rows) * (cols / 128));
+    if (!generate) return GFXB_OK;
+    return generate_b200_weights(seed, tensor, m.format, m.codes, m.scales, rows, cols, global_cols, col_offset,
+                                 local_begin.data(), global_begin.data(),
+                                 static_cast<std::uint32_t>(local_begin.size()), stream);
+  };
+  auto simple = [&](QMatrix& m, std::uint32_t tensor, std::uint32_t bits, std::uint32_t rows, std::uint32_t cols,
+                    std::uint32_t row0, std::uint32_t global_cols, std::uint32_t col0) -> int {
+    return matrix(m, tensor, bits, rows, cols, global_cols, col0, {0}, {row0});
+  };
+  auto vector_bf16 = [&](std::uint16_t*& out, std::uint32_t tensor, std::uint64_t count, std::uint64_t offset,
+                         float lo, float hi) -> int {
+    out = plan.take<std::uint16_t>(count);
+    if (!generate) return GFXB_OK;
+    return generate_bf16(seed, tensor, offset, count, lo, hi, out, stream);
+  };
+  const std::uint32_t H = c.hidden;
+  auto mlp = [&](Layer& L, std::uint32_t id) -> int {
+    GFXB_TRY(vector_bf16(L.input_norm, tensor_id(id, kInputNorm), H, 0, -0.1f, 0.1f));
+    GFXB_TRY(vector_bf16(L.post_norm, tensor_id(id, kPostNorm), H, 0, -0.1f, 0.1f));
+    GFXB_TRY(simple(L.gate, tensor_id(id, kGate), c.mlp_bits, s.inter, H, s.i0, H, 0));
+    GFXB_TRY(simple(L.up, tensor_id(id, kUp), c.mlp_bits, s.inter, H, s.i0, H, 0));
+    GFXB_TRY(simple(L.down, tensor_id(id, kDown), c.mlp_bits, H, s.inter, 0, c.intermediate, s.i0));
+    return GFXB_OK;
+  };
+  auto attention = [&](Layer& L, std::uint32_t id) -> int {
+    GFXB_TRY(simple(L.q, tensor_id(id, kQ), c.proj_bits, s.nq * 512, H, s.qh0 * 512, H, 0));
+    GFXB_TRY(simple(L.k, tensor_id(id, kK), c.proj_bits, s.nkv * 256, H, s.kv0 * 256, H, 0));
+    GFXB_TRY(simple(L.v, tensor_id(id, kV), c.proj_bits, s.nkv * 256, H, s.kv0 * 256, H, 0));
+    GFXB_TRY(simple(L.out, tensor_id(id, kO), c.proj_bits, H, s.nq * 256, 0, c.q_heads * 256, s.qh0 * 256));
+    GFXB_TRY(vector_bf16(L.q_norm, tensor_id(id, kQNorm), 256, 0, -0.1f, 0.1f));
+    GFXB_TRY(vector_bf16(L.k_norm, tensor_id(id, kKNorm), 256, 0, -0.1f, 0.1f));
+    return GFXB_OK;
+  };
+  auto gdn = [&](Layer& L, std::uint32_t id) -> int {
+    const std::uint32_t nk_all = c.gdn_key_heads * 128, nv_all = c.gdn_value_heads * 128;
+    GFXB_TRY(matrix(L.qkv, tensor_id(id, kQkv), c.proj_bits, s.channels, H, H, 0,
+                    {0, s.nk * 128, 2 * s.nk * 128}, {s.kh0 * 128, nk_all + s.kh0 * 128, 2 * nk_all + s.vh0 * 128}));
+    GFXB_TRY(simple(L.z, tensor_id(id, kZ), c.proj_bits, s.nv * 128, H, s.vh0 * 128, H, 0));
+    GFXB_TRY(simple(L.a, tensor_id(id, kA), c.proj_bits, c.gdn_value_heads, H, 0, H, 0));
+    GFXB_TRY(simple(L.b, tensor_id(id, kB), c.proj_bits, c.gdn_value_heads, H, 0, H, 0));
+    GFXB_TRY(simple(L.out, tensor_id(id, kGdnOut), c.proj_bits, H, s.nv * 128, 0, nv_all, s.vh0 * 128));
+    // conv weights [channels][4] follow the qkv channel map
+    L.conv = plan.take<std::uint16_t>(static_cast<std::size_t>(s.channels) * 4);
+    if (generate) {
+      const std::uint32_t tensor = tensor_id(id, kConv);
+      const std::uint64_t starts[3] = {static_cast<std::uint64_t>(s.kh0) * 128, nk_all + static_cast<std::uint64_t>(s.kh0) * 128,
+                                       2ull * nk_all + static_cast<std::uint64_t>(s.vh0) * 128};
+      const std::uint64_t counts[3] = {s.nk * 128ull, s.nk * 128ull, s.nv * 128ull};
+      std::uint64_t local = 0;
+      for (int i = 0; i < 3; ++i) {
+        GFXB_TRY(generate_bf16(seed, tensor, starts[i] * 4, counts[i] * 4, -0.5f, 0.5f, L.conv + local * 4, stream));
+        local += counts[i];
+      }
+    }
+    GFXB_TRY(vector_bf16(L.a_log, tensor_id(id, kALog), s.nv, s.vh0, -1.0f, 1.0f));
+    GFXB_TRY(vector_bf16(L.dt_bias, tensor_id(id, kDtBias), s.nv, s.vh0, -1.0f, 1.0f));
+    GFXB_TRY(vector_bf16(L.gdn_norm, tensor_id(id, kGdnNorm), 128, 0, 0.8f, 1.2f));
+    return GFXB_OK;
+  };
+  e.layers.resize(c.layers);
+  e.gdn_layers = e.attention_layers = 0;
+  for (std::uint32_t i = 0; i < c.layers; ++i) {
+    Layer& L = e.layers[i];
+    L.attention = (i + 1) % c.attention_interval == 0;
+    L.state_index = L.attention ? e.attention_layers++ : e.gdn_layers++;
+    GFXB_TRY(mlp(L, i));
+    GFXB_TRY(L.attention ? attention(L, i) : gdn(L, i));
+  }
+  // embedding (row-major, replicated), LM head (vocabulary rows), final norm
+  {
+    const int format = format_of(c.emb_bits);
+    e.emb_codes = plan.take<std::uint8_t>(static_cast<std::size_t>(c.vocab) * H * c.emb_bits / 8);
+    e.emb_scales = plan.take<std::uint16_t>(static_cast<std::size_t>(c.vocab) * (H / 128));
+    if (generate) {
+      GFXB_TRY(generate_rowmajor_weights(seed, tensor_id(kLayerGlobal, kEmbedding), format, e.emb_codes, e.emb_scales,
+                                         c.vocab, H, stream));
+    }
+  }
+  GFXB_TRY(simple(e.lm_head, tensor_id(kLayerGlobal, kLmHead), c.head_bits, s.vocab, H, s.v0, H, 0));
+  GFXB_TRY(vector_bf16(e.final_norm, tensor_id(kLayerGlobal, kFinalNorm), H, 0, -0.1f, 0.1f));
+  if (e.has_mtp) {
+    e.mtp.attention = true;
+    GFXB_TRY(mlp(e.mtp, kLayerMtp));
+    GFXB_TRY(attention(e.mtp, kLayerMtp));
+    GFXB_TRY(simple(e.fc, tensor_id(kLayerMtp, kFc), c.proj_bits, H, s.fc_cols, 0, 2 * H, s.fc0));
+    GFXB_TRY(vector_bf16(e.pre_emb_norm, tensor_id(kLayerMtp, kPreEmbNorm), H, 0, -0.1f, 0.1f));
+    GFXB_TRY(vector_bf16(e.pre_hidden_norm, tensor_id(kLayerMtp, kPreHiddenNorm), H, 0, -0.1f, 0.1f));
+    GFXB_TRY(vector_bf16(e.mtp_final_norm, tensor_id(kLayerMtp, kMtpFinalNorm), H, 0, -0.1f, 0.1f));
+  }
+  return GFXB_OK;
+}
+
+}  // namespace
+}  // namespace gfxb
+
+// ===========================================================================
+// session
+// ===========================================================================
+
+struct gfxb_session {
+  gfxb_engine* e = nullptr;
+  gfxb_session_config cfg{};
+  std::byte* arena = nullptr;
+  std::size_t arena_bytes = 0;
+  cudaStream_t stream = nullptr;
+  // activations (capacity kMaxBlock tokens)
+  __half* hidden[2] = {nullptr, nullptr};
+  __half* post_attention = nullptr;
+  std::int8_t* act_codes = nullptr;
+  __half* act_scales = nullptr;
+  std::int32_t* act_sums = nullptr;
+  std::uint32_t act_width = 0;
+  float *proj_main = nullptr, *proj_z = nullptr, *proj_a = nullptr, *proj_b = nullptr, *proj_k = nullptr,
+        *proj_v = nullptr, *update = nullptr, *gate = nullptr, *up = nullptr, *logits = nullptr;
+  __half *conv_out = nullptr, *gdn_out = nullptr, *query = nullptr, *attn_out = nullptr;
+  float* attention_partials = nullptr;
+  std::uint32_t attention_chunks = 0;
+  float* argmax_values = nullptr;
+  std::uint32_t* argmax_indices = nullptr;
+  std::uint32_t* gathered = nullptr;  // TP argmax exchange [tp][kMaxBlock][2]
+  std::uint32_t* exchange = nullptr;  // [kMaxBlock][2]
+  std::uint32_t* selected = nullptr;  // [kMaxBlock] target tokens
+  std::uint32_t* tokens = nullptr;    // [kMaxBlock] input tokens
+  std::uint64_t* position = nullptr;  // base position of the block
+  // MTP
+  __half *mtp_hidden = nullptr, *mtp_input = nullptr, *mtp_embed = nullptr, *target_snapshot = nullptr;
+  std::uint32_t* draft_tokens = nullptr;  // [kMaxBlock]
+  std::uint64_t* mtp_positions = nullptr; // [kMaxBlock]
+  std::uint32_t* seed_token = nullptr;
+  // states
+  __half *conv_states = nullptr, *conv_snapshot = nullptr, *conv_log = nullptr;
+  float *gdn_states = nullptr, *gdn_snapshot = nullptr, *key_log = nullptr, *delta_log = nullptr,
+        *decay_log = nullptr;
+  __half *key_cache = nullptr, *value_cache = nullptr, *mtp_keys = nullptr, *mtp_values = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  // host state
+  std::uint64_t host_position = 0, mtp_position = 0;
+  bool mtp_chain_active = false;
+  bool have_last_hidden = false;
+  const __half* last_hidden = nullptr;
+  std::uint32_t* pinned = nullptr;  // host staging
+  cudaGraphExec_t greedy_graph = nullptr;
+};
+
+namespace gfxb {
+namespace {
+
+constexpr float kEps = 1.0e-6f;
+
+struct Pack {
+  std::int8_t* codes;
+  __half* scales;
+  std::int32_t* sums;
+};
+
+Pack pack_of(gfxb_session& s) { return Pack{s.act_codes, s.act_scales, s.act_sums}; }
+
+int gemv(gfxb_session& s, const std::vector<std::pair<const QMatrix*, void*>>& mats, unsigned batch,
+         std::size_t act_offset = 0, std::size_t act_stride = 0, bool f16_first = false) {
+  gfxb_gemv_matrix items[4];
+  for (std::size_t i = 0; i < mats.size(); ++i) {
+    const QMatrix& m = *mats[i].first;
+    items[i] = gfxb_gemv_matrix{m.codes, m.scales, mats[i].second, m.rows, (i == 0 && f16_first) ? 1 : 0};
+  }
+  const QMatrix& first = *mats[0].first;
+  const std::size_t stride = act_stride != 0 ? act_stride : first.cols;
+  return lowbit_gemv(first.format, items, static_cast<unsigned>(mats.size()), s.act_codes + act_offset,
+                     reinterpret_cast<const std::uint16_t*>(s.act_scales) + act_offset / 128,
+                     s.act_sums + act_offset / 128, first.cols, stride, batch, s.stream);
+}
+
+int all_reduce(gfxb_session& s, float* buffer, std::size_t count) {
+  if (s.e->shard.tp == 1) return GFXB_OK;
+  return nccl_check(nccl().all_reduce(buffer, buffer, count, ncclFloat, ncclSum, s.e->comm, s.stream),
+                    "NCCL all-reduce failed");
+}
+
+int norm_pack(gfxb_session& s, const __half* residual, const float* update, __half* residual_out,
+              const std::uint16_t* weight, unsigned batch, __half* normalized_out = nullptr,
+              std::size_t act_offset = 0) {
+  NormPackArgs a;
+  a.residual = residual;
+  a.update = update;
+  a.residual_out = residual_out;
+  a.weight = weight;
+  a.unit_offset = 1;
+  a.epsilon = kEps;
+  a.elements = s.e->cfg.hidden;
+  a.normalized_out = normalized_out;
+  a.act_codes = s.act_codes + act_offset;
+  a.act_scales = s.act_scales + act_offset / 128;
+  a.act_sums = s.act_sums + act_offset / 128;
+  return launch_norm_pack(a, static_cast<int>(s.e->cfg.activation_bits), batch, s.stream);
+}
+
+int embed_norm_pack(gfxb_session& s, const std::uint32_t* device_tokens, __half* residual_out,
+                    const std::uint16_t* weight, unsigned batch, std::size_t act_offset = 0) {
+  NormPackArgs a;
+  a.weight = weight;
+  a.unit_offset = 1;
+  a.epsilon = kEps;
+  a.elements = s.e->cfg.hidden;
+  a.residual_out = residual_out;
+  a.act_codes = s.act_codes + act_offset;
+  a.act_scales = s.act_scales + act_offset / 128;
+  a.act_sums = s.act_sums + act_offset / 128;
+  a.embedding_codes = s.e->emb_codes;
+  a.embedding_scales = reinterpret_cast<const __half*>(s.e->emb_scales);
+  a.embedding_rows = s.e->cfg.vocab;
+  a.embedding_bits = static_cast<int>(s.e->cfg.emb_bits);
+  a.device_tokens = device_tokens;
+  return launch_norm_pack(a, static_cast<int>(s.e->cfg.activation_bits), batch, s.stream);
+}
+
+int mlp_block(gfxb_session& s, const Layer& L, unsigned batch) {
+  GFXB_TRY(gemv(s, {{&L.gate, s.gate}, {&L.up, s.up}}, batch));
+  SiluPackArgs a;
+  a.gate = s.gate;
+  a.up = s.up;
+  a.elements = s.e->shard.inter;
+  a.batch = batch;
+  a.act_codes = s.act_codes;
+  a.act_scales = s.act_scales;
+  a.act_sums = s.act_sums;
+  GFXB_TRY(launch_silu_pack(a, static_cast<int>(s.e->cfg.activation_bits), s.stream));
+  GFXB_TRY(gemv(s, {{&L.down, s.update}}, batch));
+  return all_reduce(s, s.update, static_cast<std::size_t>(batch) * s.e->cfg.hidden);
+}
+
+// Attention mixer: q/k/v GEMV, fused Q/K norm + RoPE + KV append, chunked
+// gated attention with the o_proj input pack fused in its epilogue, o_proj.
+int attention_mixer(gfxb_session& s, const Layer& L, __half* key_cache, __half* value_cache,
+                    const std::uint64_t* device_position, unsigned batch) {
+  const Shard& sh = s.e->shard;
+  GFXB_TRY(gemv(s, {{&L.q, s.proj_main}, {&L.k, s.proj_k}, {&L.v, s.proj_v}}, batch));
+  QkRopeArgs r;
+  r.q_input = s.proj_main;
+  r.q_weight = L.q_norm;
+  r.q_output = s.query;
+  r.k_input = s.proj_k;
+  r.k_weight = L.k_norm;
+  r.v_input = s.proj_v;
+  r.key_cache = key_cache;
+  r.value_cache = value_cache;
+  r.capacity = s.cfg.maximum_context_tokens;
+  r.q_heads = sh.nq;
+  r.k_heads = sh.nkv;
+  r.q_stride = 512;
+  r.k_stride = 256;
+  r.rotary = 64;
+  r.cos_table = s.rope_cos;
+  r.sin_table = s.rope_sin;
+  r.table_positions = s.cfg.maximum_context_tokens;
+  r.device_base_position = device_position;
+  GFXB_TRY(launch_qk_rope(r, batch, s.stream));
+  AttentionArgs a;
+  a.query = s.query;
+  a.gate = s.proj_main;
+  a.key_cache = key_cache;
+  a.value_cache = value_cache;
+  a.output = s.attn_out;
+  a.partials = s.attention_partials;
+  a.max_chunks = s.attention_chunks;
+  a.capacity = s.cfg.maximum_context_tokens;
+  a.device_base_position = device_position;
+  a.q_heads = sh.nq;
+  a.kv_heads = sh.nkv;
+  a.act_bits = static_cast<int>(s.e->cfg.activation_bits);
+  a.act_codes = s.act_codes;
+  a.act_scales = s.act_scales;
+  a.act_sums = s.act_sums;
+  GFXB_TRY(launch_attention(a, batch, s.stream));
+  GFXB_TRY(gemv(s, {{&L.out, s.update}}, batch));
+  return all_reduce(s, s.update, static_cast<std::size_t>(batch) * s.e->cfg.hidden);
+}
+
+// Gated-DeltaNet mixer: fused qkv/z/a/b GEMV, conv, recurrence (+ out_proj
+// pack), out_proj. With `record` the final states go to the snapshot buffers
+// and the per-token logs are written for a later rollback replay.
+int gdn_mixer(gfxb_session& s, const Layer& L, unsigned batch, bool record) {
+  const Shard& sh = s.e->shard;
+  const gfxb_model_config& c = s.e->cfg;
+  GFXB_TRY(gemv(s, {{&L.qkv, s.proj_main}, {&L.z, s.proj_z}, {&L.a, s.proj_a}, {&L.b, s.proj_b}}, batch));
+  const std::size_t conv_elems = static_cast<std::size_t>(sh.channels) * 4;
+  const std::size_t state_elems = static_cast<std::size_t>(sh.nv) * 128 * 128;
+  __half* conv_state = s.conv_states + L.state_index * conv_elems;
+  float* state = s.gdn_states + L.state_index * state_elems;
+  GdnConvArgs cv;
+  cv.projected = s.proj_main;
+  cv.weight = L.conv;
+  cv.initial_state = conv_state;
+  cv.final_state = record ? s.conv_snapshot + L.state_index * conv_elems : conv_state;
+  cv.output = s.conv_out;
+  cv.appended_log = record ? s.conv_log + static_cast<std::size_t>(L.state_index) * kMaxBlock * sh.channels : nullptr;
+  cv.channels = sh.channels;
+  cv.batch = batch;
+  GFXB_TRY(launch_gdn_conv(cv, s.stream));
+  GdnRecurrentArgs g;
+  g.qkv = s.conv_out;
+  g.z = s.proj_z;
+  g.a = s.proj_a + sh.vh0;
+  g.b = s.proj_b + sh.vh0;
+  g.ab_stride = c.gdn_value_heads;
+  g.a_log = L.a_log;
+  g.dt_bias = L.dt_bias;
+  g.norm_weight = L.gdn_norm;
+  g.initial_state = state;
+  g.final_state = record ? s.gdn_snapshot + L.state_index * state_elems : state;
+  g.output = s.gdn_out;
+  if (record) {
+    g.key_log = s.key_log + static_cast<std::size_t>(L.state_index) * kMaxBlock * sh.nk * 128;
+    g.delta_log = s.delta_log + static_cast<std::size_t>(L.state_index) * kMaxBlock * sh.nv * 128;
+    g.decay_log = s.decay_log + static_cast<std::size_t>(L.state_index) * kMaxBlock * sh.nv;
+  }
+  g.key_heads = sh.nk;
+  g.value_heads = sh.nv;
+  g.batch = batch;
+  g.act_bits = static_cast<int>(c.activation_bits);
+  g.act_codes = s.act_codes;
+  g.act_scales = s.act_scales;
+  g.act_sums = s.act_sums;
+  GFXB_TRY(launch_gdn_recurrent(g, s.stream));
+  GFXB_TRY(gemv(s, {{&L.out, s.update}}, batch));
+  return all_reduce(s, s.update, static_cast<std::size_t>(batch) * c.hidden);
+}
+
+__global__ void advance_kernel(std::uint64_t* position, std::uint32_t* tokens, const std::uint32_t* selected,
+                               unsigned batch) {
+  *position += batch;
+  tokens[0] = selected[batch - 1];
+}
+
+// TP argmax: each rank contributes (value bits, global index) per token; the
+// winner is the largest value, lowest global index on ties.
+__global__ void select_across_ranks_kernel(const std::uint32_t* gathered, unsigned ranks, unsigned batch,
+                                           std::uint32_t* tokens) {
+  const unsigned t = threadIdx.x;
+  if (t >= batch) return;
+  float best = -__int_as_float(0x7f800000);
+  std::uint32_t index = 0xffffffffu;
+  for (unsigned r = 0; r < ranks; ++r) {
+    const float value = __uint_as_float(gathered[(r * kMaxBlock + t) * 2]);
+    const std::uint32_t other = gathered[(r * kMaxBlock + t) * 2 + 1];
+    if (value > best || (value == best && other < index)) {
+      best = value;
+      index = other;
+    }
+  }
+  tokens[t] = index;
+}
+
+__global__ void exchange_kernel(const float* values, const std::uint32_t* indices, const std::uint32_t* local_tokens,
+                                std::uint32_t offset, unsigned batch, unsigned blocks, std::uint32_t* exchange) {
+  // local winner per token: recompute its value from the partials (first block carrying the index)
+  const unsigned t = threadIdx.x;
+  if (t >= batch) return;
+  const std::uint32_t local = local_tokens[t];
+  float value = -__int_as_float(0x7f800000);
+  for (unsigned b = 0; b < blocks; ++b) {
+    if (indices[t * blocks + b] == local) {
+      value = values[t * blocks + b];
+      break;
+    }
+  }
+  exchange[t * 2] = __float_as_uint(value);
+  exchange[t * 2 + 1] = local + offset;
+}
+
+int head_argmax(gfxb_session& s, const QMatrix& head_rows, std::uint32_t rows, std::uint32_t* out_tokens,
+                unsigned batch) {
+  const Shard& sh = s.e->shard;
+  QMatrix head = head_rows;
+  if (rows == 0) {
+    // this rank holds none of the requested vocabulary rows
+    if (sh.tp == 1) return fail(GFXB_INTERNAL, "empty vocabulary range");
+    // NaN value bits never win the comparison in select_across_ranks_kernel
+    GFXB_TRY(cuda_check(cudaMemsetAsync(s.exchange, 0xff, kMaxBlock * 2 * sizeof(std::uint32_t), s.stream), "memset"));
+  } else {
+    head.rows = rows;
+    GFXB_TRY(gemv(s, {{&head, s.logits}}, batch));
+    ArgmaxArgs a;
+    a.logits = s.logits;
+    a.row_stride = rows;
+    a.vocab = rows;
+    a.tokens = sh.tp == 1 ? out_tokens : s.exchange + kMaxBlock * 2;  // local winners scratch
+    a.partial_values = s.argmax_values;
+    a.partial_indices = s.argmax_indices;
+    GFXB_TRY(launch_argmax(a, batch, s.stream));
+    if (sh.tp == 1) return GFXB_OK;
+    exchange_kernel<<<1, kMaxBlock, 0, s.stream>>>(s.argmax_values, s.argmax_indices, s.exchange + kMaxBlock * 2,
+                                                   sh.v0, batch, 64, s.exchange);
+    GFXB_TRY(launch_status("argmax exchange failed"));
+  }
+  GFXB_TRY(nccl_check(nccl().all_gather(s.exchange, s.gathered, kMaxBlock * 2, ncclUint32, s.e->comm, s.stream),
+                      "NCCL all-gather failed"));
+  select_across_ranks_kernel<<<1, kMaxBlock, 0, s.stream>>>(s.gathered, sh.tp, batch, out_tokens);
+  return launch_status("argmax selection failed");
+}
+
+// The causal block forward (qwen_runtime.cpp:349-544, 1264-1392): tokens and
+// base position are read from device memory, so the same launch sequence
+// serves the eager path and captured graphs.
+int enqueue_forward(gfxb_session& s, unsigned batch, const std::uint32_t* device_tokens,
+                    const std::uint64_t* device_position, bool record) {
+  gfxb_engine& e = *s.e;
+  const gfxb_model_config& c = e.cfg;
+  __half* current = s.hidden[0];
+  __half* next = s.hidden[1];
+  GFXB_TRY(embed_norm_pack(s, device_tokens, current, e.layers[0].input_norm, batch));
+  const std::size_t kv_stride = static_cast<std::size_t>(s.cfg.maximum_context_tokens) * e.shard.nkv * 256;
+  for (std::uint32_t i = 0; i < c.layers; ++i) {
+    const Layer& L = e.layers[i];
+    if (L.attention) {
+      GFXB_TRY(attention_mixer(s, L, s.key_cache + L.state_index * kv_stride, s.value_cache + L.state_index * kv_stride,
+                               device_position, batch));
+    } else {
+      GFXB_TRY(gdn_mixer(s, L, batch, record));
+    }
+    GFXB_TRY(norm_pack(s, current, s.update, s.post_attention, L.post_norm, batch));
+    GFXB_TRY(mlp_block(s, L, batch));
+    const std::uint16_t* next_norm = i + 1 < c.layers ? e.layers[i + 1].input_norm : e.final_norm;
+    GFXB_TRY(norm_pack(s, s.post_attention, s.update, next, next_norm, batch));
+    std::swap(current, next);
+  }
+  s.last_hidden = current + static_cast<std::size_t>(batch - 1) * c.hidden;
+  return head_argmax(s, e.lm_head, e.shard.vocab, s.selected, batch);
+}
+
+// MTP proposal (qwen_runtime.cpp:715-867) for one token: embedding of
+// *device_token and the conditioning hidden state -> dual RMSNorm -> fc ->
+// one attention layer + MLP on the MTP KV cache -> draft head (first
+// draft_vocab LM-head rows) -> argmax into *output_token (or nothing when
+// output_token is null: cache advance only).
+int enqueue_mtp(gfxb_session& s, const std::uint32_t* device_token, const __half* conditioning,
+                const std::uint64_t* device_position, std::uint32_t* output_token) {
+  gfxb_engine& e = *s.e;
+  const gfxb_model_config& c = e.cfg;
+  const Shard& sh = e.shard;
+  const std::uint32_t H = c.hidden;
+  GFXB_TRY(embed_norm_pack(s, device_token, s.mtp_embed, e.pre_emb_norm, 1, 0));
+  GFXB_TRY(norm_pack(s, conditioning, nullptr, nullptr, e.pre_hidden_norm, 1, nullptr, H));
+  if (sh.tp == 1) {
+    GFXB_TRY(gemv(s, {{&e.fc, s.mtp_input}}, 1, 0, 2 * H, true));
+  } else {
+    GFXB_TRY(gemv(s, {{&e.fc, s.update}}, 1, sh.fc0, 2 * H));
+    GFXB_TRY(all_reduce(s, s.update, H));
+    GFXB_TRY(launch_float_to_half(s.update, s.mtp_input, H, s.stream));
+  }
+  GFXB_TRY(norm_pack(s, s.mtp_input, nullptr, nullptr, e.mtp.input_norm, 1));
+  if (output_token == nullptr) {
+    // advance the MTP KV cache only (qwen_runtime.cpp:826-829)
+    GFXB_TRY(gemv(s, {{&e.mtp.q, s.proj_main}, {&e.mtp.k, s.proj_k}, {&e.mtp.v, s.proj_v}}, 1));
+    QkRopeArgs r;
+    r.q_input = s.proj_main;
+    r.q_weight = e.mtp.q_norm;
+    r.q_output = s.query;
+    r.k_input = s.proj_k;
+    r.k_weight = e.mtp.k_norm;
+    r.v_input = s.proj_v;
+    r.key_cache = s.mtp_keys;
+    r.value_cache = s.mtp_values;
+    r.capacity = s.cfg.maximum_context_tokens;
+    r.q_heads = sh.nq;
+    r.k_heads = sh.nkv;
+    r.cos_table = s.rope_cos;
+    r.sin_table = s.rope_sin;
+    r.table_positions = s.cfg.maximum_context_tokens;
+    r.device_base_position = device_position;
+    return launch_qk_rope(r, 1, s.stream);
+  }
+  GFXB_TRY(attention_mixer(s, e.mtp, s.mtp_keys, s.mtp_values, device_position, 1));
+  GFXB_TRY(norm_pack(s, s.mtp_input, s.update, s.post_attention, e.mtp.post_norm, 1));
+  GFXB_TRY(mlp_block(s, e.mtp, 1));
+  GFXB_TRY(norm_pack(s, s.post_attention, s.update, s.mtp_hidden, e.mtp_final_norm, 1));
+  const std::uint32_t draft = std::min(c.draft_vocab, c.vocab);
+  const std::uint32_t local_rows = sh.v0 >= draft ? 0 : std::min(sh.vocab, draft - sh.v0);
+  return head_argmax(s, e.lm_head, local_rows, output_token, 1);
+}
+
+__global__ void set_positions_kernel(std::uint64_t* position, std::uint64_t value, std::uint64_t* mtp_positions,
+                                     std::uint64_t mtp_base, unsigned count, std::uint32_t* seed_slot,
+                                     std::uint32_t seed, std::uint32_t* tokens) {
+  *position = value;
+  for (unsigned i = 0; i < count; ++i) mtp_positions[i] = mtp_base + i;
+  *seed_slot = seed;
+  tokens[0] = seed;
+}
+
+__global__ void copy_drafts_kernel(const std::uint32_t* drafts, std::uint32_t* tokens, unsigned count) {
+  const unsigned i = threadIdx.x;
+  if (i < count) tokens[i + 1] = drafts[i];
+}
+
+int capture_greedy(gfxb_session& s) {
+  cudaGraph_t graph = nullptr;
+  GFXB_TRY(cuda_check(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal), "graph capture start failed"));
+  int status = enqueue_forward(s, 1, s.tokens, s.position, false);
+  if (status == GFXB_OK) {
+    advance_kernel<<<1, 1, 0, s.stream>>>(s.position, s.tokens, s.selected, 1);
+    status = launch_status("advance launch failed");
+  }
+  const cudaError_t end = cudaStreamEndCapture(s.stream, &graph);
+  if (status != GFXB_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return status;
+  }
+  GFXB_TRY(cuda_check(end, "graph capture end failed"));
+  const cudaError_t inst = cudaGraphInstantiate(&s.greedy_graph, graph, 0);
+  cudaGraphDestroy(graph);
+  return cuda_check(inst, "graph instantiation failed");
+}
+
+int allocate_session(gfxb_session& s, bool place) {
+  gfxb_engine& e = *s.e;
+  const gfxb_model_config& c = e.cfg;
+  const Shard& sh = e.shard;
+  Planner plan;
+  plan.base = place ? s.arena : nullptr;
+  const std::size_t B = kMaxBlock, H = c.hidden, ctx = s.cfg.maximum_context_tokens;
+  const std::size_t proj_main = std::max<std::size_t>(sh.channels, static_cast<std::size_t>(sh.nq) * 512);
+  s.act_width = static_cast<std::uint32_t>(std::max<std::size_t>({2 * H, sh.inter, sh.nv * 128ull, sh.nq * 256ull}));
+  s.hidden[0] = plan.take<__half>(B * H);
+  s.hidden[1] = plan.take<__half>(B * H);
+  s.post_attention = plan.take<__half>(B * H);
+  s.act_codes = plan.take<std::int8_t>(B * s.act_width);
+  s.act_scales = plan.take<__half>(B * s.act_width / 128);
+  s.act_sums = plan.take<std::int32_t>(B * s.act_width / 128);
+  s.proj_main = plan.take<float>(B * proj_main);
+  s.proj_z = plan.take<float>(B * sh.nv * 128);
+  s.proj_a = plan.take<float>(B * c.gdn_value_heads);
+  s.proj_b = plan.take<float>(B * c.gdn_value_heads);
+  s.proj_k = plan.take<float>(B * sh.nkv * 256);
+  s.proj_v = plan.take<float>(B * sh.nkv * 256);
+  s.update = plan.take<float>(B * H);
+  s.gate = plan.take<float>(B * sh.inter);
+  s.up = plan.take<float>(B * sh.inter);
+  s.logits = plan.take<float>(B * sh.vocab);
+  s.conv_out = plan.take<__half>(B * sh.channels);
+  s.gdn_out = plan.take<__half>(B * sh.nv * 128);
+  s.query = plan.take<__half>(B * sh.nq * 256);
+  s.attn_out = plan.take<__half>(B * sh.nq * 256);
+  s.attention_chunks = static_cast<std::uint32_t>((ctx + kAttentionChunk - 1) / kAttentionChunk);
+  s.attention_partials = plan.take<float>(attention_partial_bytes(sh.nq, ctx, kMaxBlock) / sizeof(float));
+  s.argmax_values = plan.take<float>(argmax_scratch_bytes(kMaxBlock) / 8);
+  s.argmax_indices = plan.take<std::uint32_t>(argmax_scratch_bytes(kMaxBlock) / 8);
+  s.gathered = plan.take<std::uint32_t>(static_cast<std::size_t>(sh.tp) * B * 2);
+  s.exchange = plan.take<std::uint32_t>(B * 4);
+  s.selected = plan.take<std::uint32_t>(B);
+  s.tokens = plan.take<std::uint32_t>(B);
+  s.position = plan.take<std::uint64_t>(1);
+  s.mtp_hidden = plan.take<__half>(H);
+  s.mtp_input = plan.take<__half>(H);
+  s.mtp_embed = plan.take<__half>(H);
+  s.target_snapshot = plan.take<__half>(H);
+  s.draft_tokens = plan.take<std::uint32_t>(B);
+  s.mtp_positions = plan.take<std::uint64_t>(B);
+  s.seed_token = plan.take<std::uint32_t>(1);
+  const std::size_t conv_elems = static_cast<std::size_t>(e.gdn_layers) * sh.channels * 4;
+  const std::size_t state_elems = static_cast<std::size_t>(e.gdn_layers) * sh.nv * 128 * 128;
+  s.conv_states = plan.take<__half>(conv_elems);
+  s.conv_snapshot = plan.take<__half>(conv_elems);
+  s.gdn_states = plan.take<float>(state_elems);
+  s.gdn_snapshot = plan.take<float>(state_elems);
+  s.conv_log = plan.take<__half>(static_cast<std::size_t>(e.gdn_layers) * B * sh.channels);
+  s.key_log = plan.take<float>(static_cast<std::size_t>(e.gdn_layers) * B * sh.nk * 128);
+  s.delta_log = plan.take<float>(static_cast<std::size_t>(e.gdn_layers) * B * sh.nv * 128);
+  s.decay_log = plan.take<float>(static_cast<std::size_t>(e.gdn_layers) * B * sh.nv);
+  const std::size_t kv = static_cast<std::size_t>(e.attention_layers) * ctx * sh.nkv * 256;
+  s.key_cache = plan.take<__half>(kv);
+  s.value_cache = plan.take<__half>(kv);
+  s.mtp_keys = plan.take<__half>(ctx * sh.nkv * 256);
+  s.mtp_values = plan.take<__half>(ctx * sh.nkv * 256);
+  s.rope_cos = plan.take<float>(ctx * 32);
+  s.rope_sin = plan.take<float>(ctx * 32);
+  s.arena_bytes = plan.offset;
+  return GFXB_OK;
+}
+
+}  // namespace
+}  // namespace gfxb
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+
+using namespace gfxb;
+
+extern "C" int gfxb_nccl_unique_id(void* id128) {
+  if (id128 == nullptr) return fail(GFXB_INVALID_ARGUMENT, "NCCL id buffer is null");
+  GFXB_TRY(load_nccl(nccl()));
+  ncclUniqueId id;
+  GFXB_TRY(nccl_check(nccl().get_unique_id(&id), "ncclGetUniqueId failed"));
+  std::memcpy(id128, &id, sizeof id);
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_engine_create_synthetic(const gfxb_model_config* config, int device, int tp_rank, int tp_size,
+                                            const void* nccl_id128, int include_mtp, gfxb_engine** out) {
+  if (config == nullptr || out == nullptr) return fail(GFXB_INVALID_ARGUMENT, "engine arguments are null");
+  *out = nullptr;
+  if (tp_size < 1 || tp_size > 8 || tp_rank < 0 || tp_rank >= tp_size) {
+    return fail(GFXB_INVALID_ARGUMENT, "tensor-parallel rank/size are invalid");
+  }
+  if (tp_size > 1 && nccl_id128 == nullptr) return fail(GFXB_INVALID_ARGUMENT, "TP > 1 requires an NCCL id");
+  GFXB_TRY(validate_config(*config, static_cast<std::uint32_t>(tp_size)));
+  GFXB_TRY(gfxb_require_sm100_device(device, nullptr));
+  GFXB_TRY(cuda_check(cudaSetDevice(device), "cudaSetDevice failed"));
+  auto e = std::make_unique<gfxb_engine>();
+  e->cfg = *config;
+  e->device = device;
+  e->has_mtp = include_mtp != 0;
+  e->shard = make_shard(*config, static_cast<std::uint32_t>(tp_size), static_cast<std::uint32_t>(tp_rank));
+  GFXB_TRY(cuda_check(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream creation failed"));
+  Planner plan;
+  GFXB_TRY(build_weights(*e, plan, false));
+  e->arena_bytes = plan.offset;
+  void* arena = nullptr;
+  GFXB_TRY(cuda_check(cudaMalloc(&arena, e->arena_bytes), "weight arena allocation failed"));
+  e->arena = static_cast<std::byte*>(arena);
+  Planner place;
+  place.base = e->arena;
+  int status = build_weights(*e, place, true);
+  if (status == GFXB_OK) status = cuda_check(cudaStreamSynchronize(e->stream), "weight generation failed");
+  if (status == GFXB_OK && tp_size > 1) {
+    status = load_nccl(nccl());
+    if (status == GFXB_OK) {
+      ncclUniqueId id;
+      std::memcpy(&id, nccl_id128, sizeof id);
+      status = nccl_check(nccl().comm_init_rank(&e->comm, tp_size, id, tp_rank), "ncclCommInitRank failed");
+    }
+  }
+  if (status != GFXB_OK) {
+    cudaFree(e->arena);
+    cudaStreamDestroy(e->stream);
+    return status;
+  }
+  *out = e.release();
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_engine_destroy(gfxb_engine* engine) {
+  if (engine == nullptr) return GFXB_OK;
+  cudaSetDevice(engine->device);
+  if (engine->comm != nullptr) nccl().comm_destroy(engine->comm);
+  cudaFree(engine->arena);
+  cudaStreamDestroy(engine->stream);
+  delete engine;
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_engine_weight_bytes(const gfxb_engine* engine, std::uint64_t* bytes) {
+  if (engine == nullptr || bytes == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  *bytes = engine->arena_bytes;
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_session_create(gfxb_engine* engine, const gfxb_session_config* config, gfxb_session** out) {
+  if (engine == nullptr || config == nullptr || out == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  if (config->maximum_context_tokens == 0 || config->maximum_context_tokens > engine->cfg.max_context ||
+      (config->graph_verifier_batch != 0 &&
+       (config->graph_verifier_batch < 2 || config->graph_verifier_batch > kMaxBlock))) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid decode session configuration");
+  }
+  GFXB_TRY(cuda_check(cudaSetDevice(engine->device), "cudaSetDevice failed"));
+  auto s = std::make_unique<gfxb_session>();
+  s->e = engine;
+  s->cfg = *config;
+  s->stream = engine->stream;
+  GFXB_TRY(allocate_session(*s, false));
+  void* arena = nullptr;
+  GFXB_TRY(cuda_check(cudaMalloc(&arena, s->arena_bytes), "session arena allocation failed"));
+  s->arena = static_cast<std::byte*>(arena);
+  allocate_session(*s, true);
+  int status = cuda_check(cudaMemsetAsync(s->arena, 0, s->arena_bytes, s->stream), "session arena clear failed");
+  const std::size_t ctx = config->maximum_context_tokens;
+  std::vector<float> cos_table(ctx * 32), sin_table(ctx * 32);
+  gfxb_rope_table(ctx, 64, 10000000.0f, cos_table.data(), sin_table.data());
+  if (status == GFXB_OK) {
+    status = cuda_check(cudaMemcpy(s->rope_cos, cos_table.data(), ctx * 32 * sizeof(float), cudaMemcpyHostToDevice),
+                        "RoPE table upload failed");
+  }
+  if (status == GFXB_OK) {
+    status = cuda_check(cudaMemcpy(s->rope_sin, sin_table.data(), ctx * 32 * sizeof(float), cudaMemcpyHostToDevice),
+                        "RoPE table upload failed");
+  }
+  if (status == GFXB_OK) {
+    status = cuda_check(cudaMallocHost(reinterpret_cast<void**>(&s->pinned), 256 * sizeof(std::uint32_t)),
+                        "pinned staging allocation failed");
+  }
+  if (status == GFXB_OK && config->use_graphs) status = capture_greedy(*s);
+  if (status == GFXB_OK) status = cuda_check(cudaStreamSynchronize(s->stream), "session setup failed");
+  if (status != GFXB_OK) {
+    if (s->greedy_graph) cudaGraphExecDestroy(s->greedy_graph);
+    if (s->pinned) cudaFreeHost(s->pinned);
+    cudaFree(s->arena);
+    return status;
+  }
+  *out = s.release();
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_session_destroy(gfxb_session* session) {
+  if (session == nullptr) return GFXB_OK;
+  cudaSetDevice(session->e->device);
+  cudaStreamSynchronize(session->stream);
+  if (session->greedy_graph) cudaGraphExecDestroy(session->greedy_graph);
+  if (session->pinned) cudaFreeHost(session->pinned);
+  cudaFree(session->arena);
+  delete session;
+  return GFXB_OK;
+}
+
+namespace {
+
+int upload_step(gfxb_session& s, const std::uint32_t* tokens, unsigned count) {
+  std::memcpy(s.pinned, tokens, count * sizeof(std::uint32_t));
+  std::uint64_t position = s.host_position;
+  std::memcpy(s.pinned + 64, &position, sizeof position);
+  GFXB_TRY(cuda_check(cudaMemcpyAsync(s.tokens, s.pinned, count * sizeof(std::uint32_t), cudaMemcpyHostToDevice, s.stream),
+                      "token upload failed"));
+  return cuda_check(cudaMemcpyAsync(s.position, s.pinned + 64, sizeof position, cudaMemcpyHostToDevice, s.stream),
+                    "position upload failed");
+}
+
+int download_tokens(gfxb_session& s, const std::uint32_t* device, std::uint32_t* host, unsigned count) {
+  GFXB_TRY(cuda_check(cudaMemcpyAsync(s.pinned + 128, device, count * sizeof(std::uint32_t), cudaMemcpyDeviceToHost,
+                                      s.stream),
+                      "token download failed"));
+  GFXB_TRY(cuda_check(cudaStreamSynchronize(s.stream), "decode step failed"));
+  std::memcpy(host, s.pinned + 128, count * sizeof(std::uint32_t));
+  return GFXB_OK;
+}
+
+bool valid_tokens(const gfxb_session& s, const std::uint32_t* tokens, unsigned count) {
+  for (unsigned i = 0; i < count; ++i) {
+    if (tokens[i] >= s.e->cfg.vocab) return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+extern "C" int gfxb_session_greedy_step(gfxb_session* session, std::uint32_t input_token, std::uint32_t* output) {
+  if (session == nullptr || output == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  gfxb_session& s = *session;
+  if (s.host_position >= s.cfg.maximum_context_tokens || input_token >= s.e->cfg.vocab) {
+    return fail(GFXB_INVALID_ARGUMENT, "decode token or session position is invalid");
+  }
+  GFXB_TRY(upload_step(s, &input_token, 1));
+  if (s.greedy_graph != nullptr) {
+    GFXB_TRY(cuda_check(cudaGraphLaunch(s.greedy_graph, s.stream), "graph launch failed"));
+    s.last_hidden = s.hidden[s.e->cfg.layers % 2];
+  } else {
+    GFXB_TRY(enqueue_forward(s, 1, s.tokens, s.position, false));
+  }
+  GFXB_TRY(download_tokens(s, s.selected, output, 1));
+  s.host_position += 1;
+  s.have_last_hidden = true;
+  s.mtp_chain_active = false;
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_session_enqueue_greedy(gfxb_session* session, std::uint32_t first_token, unsigned steps) {
+  if (session == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null session");
+  gfxb_session& s = *session;
+  if (s.greedy_graph == nullptr) return fail(GFXB_UNSUPPORTED, "device-resident decode needs use_graphs");
+  if (s.host_position + steps > s.cfg.maximum_context_tokens || first_token >= s.e->cfg.vocab) {
+    return fail(GFXB_INVALID_ARGUMENT, "decode loop exceeds the context or the token is invalid");
+  }
+  set_positions_kernel<<<1, 1, 0, s.stream>>>(s.position, s.host_position, s.mtp_positions, 0, 0, s.seed_token,
+                                               first_token, s.tokens);
+  GFXB_TRY(launch_status("decode loop setup failed"));
+  for (unsigned i = 0; i < steps; ++i) {
+    GFXB_TRY(cuda_check(cudaGraphLaunch(s.greedy_graph, s.stream), "graph launch failed"));
+  }
+  s.last_hidden = s.hidden[s.e->cfg.layers % 2];
+  s.host_position += steps;
+  s.have_last_hidden = steps > 0;
+  s.mtp_chain_active = false;
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_session_sync(gfxb_session* session) {
+  if (session == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null session");
+  return cuda_check(cudaStreamSynchronize(session->stream), "session synchronisation failed");
+}
+
+extern "C" int gfxb_session_last_token(gfxb_session* session, std::uint32_t* token) {
+  if (session == nullptr || token == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  return download_tokens(*session, session->selected, token, 1);
+}
+
+extern "C" void* gfxb_session_stream(gfxb_session* session) { return session != nullptr ? session->stream : nullptr; }
+
+extern "C" int gfxb_session_block_step(gfxb_session* session, const std::uint32_t* input_tokens, unsigned count,
+                                       std::uint32_t* output_tokens) {
+  if (session == nullptr || input_tokens == nullptr || output_tokens == nullptr) {
+    return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  }
+  gfxb_session& s = *session;
+  if (count == 0 || count > kMaxBlock || count > s.cfg.maximum_context_tokens - s.host_position ||
+      !valid_tokens(s, input_tokens, count)) {
+    return fail(GFXB_INVALID_ARGUMENT,
+                "decode block must contain a supported number of valid tokens within the context limit");
+  }
+  GFXB_TRY(upload_step(s, input_tokens, count));
+  GFXB_TRY(enqueue_forward(s, count, s.tokens, s.position, false));
+  GFXB_TRY(download_tokens(s, s.selected, output_tokens, count));
+  s.host_position += count;
+  s.have_last_hidden = true;
+  s.mtp_chain_active = false;
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_session_mtp_draft(gfxb_session* session, std::uint32_t next_token, std::uint32_t* draft) {
+  if (session == nullptr || draft == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  gfxb_session& s = *session;
+  if (!s.e->has_mtp) return fail(GFXB_UNSUPPORTED, "engine was created without the MTP layer");
+  if (!s.have_last_hidden || (!s.mtp_chain_active && s.mtp_position + 1 != s.host_position) ||
+      next_token >= s.e->cfg.vocab || s.mtp_position >= s.cfg.maximum_context_tokens) {
+    return fail(GFXB_INVALID_ARGUMENT, "MTP drafting is not aligned with the target state");
+  }
+  const __half* conditioning = s.mtp_chain_active ? s.mtp_hidden : s.last_hidden;
+  s.pinned[0] = next_token;
+  const std::uint64_t position = s.mtp_position;
+  std::memcpy(s.pinned + 64, &position, sizeof position);
+  GFXB_TRY(cuda_check(cudaMemcpyAsync(s.seed_token, s.pinned, 4, cudaMemcpyHostToDevice, s.stream), "upload failed"));
+  GFXB_TRY(cuda_check(cudaMemcpyAsync(s.mtp_positions, s.pinned + 64, 8, cudaMemcpyHostToDevice, s.stream),
+                      "upload failed"));
+  GFXB_TRY(enqueue_mtp(s, s.seed_token, conditioning, s.mtp_positions, s.draft_tokens));
+  GFXB_TRY(download_tokens(s, s.draft_tokens, draft, 1));
+  s.mtp_position += 1;
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_session_speculative_step(gfxb_session* session, std::uint32_t seed_token, unsigned draft_count,
+                                             std::uint32_t* tokens, unsigned* token_count, unsigned* accepted_out) {
+  if (session == nullptr || tokens == nullptr || token_count == nullptr || accepted_out == nullptr) {
+    return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  }
+  gfxb_session& s = *session;
+  if (!s.e->has_mtp) return fail(GFXB_UNSUPPORTED, "engine was created without the MTP layer");
+  if (!s.have_last_hidden || draft_count == 0 || draft_count >= kMaxBlock || seed_token >= s.e->cfg.vocab ||
+      s.mtp_position + 1 != s.host_position ||
+      draft_count + 1 > s.cfg.maximum_context_tokens - s.host_position) {
+    return fail(GFXB_INVALID_ARGUMENT, "speculative step requires 1..31 drafts and aligned target/MTP state");
+  }
+  const std::uint64_t base = s.host_position, mtp_base = s.mtp_position;
+  const gfxb_model_config& c = s.e->cfg;
+  // snapshot the conditioning hidden state (qwen_runtime.cpp:236-247)
+  GFXB_TRY(cuda_check(cudaMemcpyAsync(s.target_snapshot, s.last_hidden, c.hidden * sizeof(__half),
+                                      cudaMemcpyDeviceToDevice, s.stream),
+                      "hidden snapshot failed"));
+  set_positions_kernel<<<1, 1, 0, s.stream>>>(s.position, base, s.mtp_positions, mtp_base, draft_count, s.seed_token,
+                                               seed_token, s.tokens);
+  GFXB_TRY(launch_status("position setup failed"));
+  for (unsigned i = 0; i < draft_count; ++i) {
+    const std::uint32_t* token = i == 0 ? s.seed_token : s.draft_tokens + i - 1;
+    const __half* conditioning = i == 0 ? s.target_snapshot : s.mtp_hidden;
+    GFXB_TRY(enqueue_mtp(s, token, conditioning, s.mtp_positions + i, s.draft_tokens + i));
+  }
+  copy_drafts_kernel<<<1, kMaxBlock, 0, s.stream>>>(s.draft_tokens, s.tokens, draft_count);
+  GFXB_TRY(launch_status("draft copy failed"));
+  const unsigned batch = draft_count + 1;
+  GFXB_TRY(enqueue_forward(s, batch, s.tokens, s.position, true));
+  std::uint32_t host[2 * kMaxBlock];
+  GFXB_TRY(cuda_check(cudaMemcpyAsync(s.pinned + 128, s.draft_tokens, draft_count * 4, cudaMemcpyDeviceToHost, s.stream),
+                      "draft download failed"));
+  GFXB_TRY(cuda_check(cudaMemcpyAsync(s.pinned + 160, s.selected, batch * 4, cudaMemcpyDeviceToHost, s.stream),
+                      "verifier download failed"));
+  GFXB_TRY(cuda_check(cudaStreamSynchronize(s.stream), "speculative round failed"));
+  std::memcpy(host, s.pinned + 128, draft_count * 4);
+  std::memcpy(host + kMaxBlock, s.pinned + 160, batch * 4);
+  unsigned accepted = 0;
+  while (accepted < draft_count && host[accepted] == host[kMaxBlock + accepted]) ++accepted;
+  const std::size_t conv_elems = static_cast<std::size_t>(s.e->gdn_layers) * s.e->shard.channels * 4;
+  const std::size_t state_elems = static_cast<std::size_t>(s.e->gdn_layers) * s.e->shard.nv * 128 * 128;
+  if (accepted != draft_count) {
+    // replay the accepted prefix (+ the correction's own input) onto the untouched states
+    GdnRestoreArgs r;
+    r.conv_states = s.conv_states;
+    r.states = s.gdn_states;
+    r.conv_logs = s.conv_log;
+    r.key_logs = s.key_log;
+    r.delta_logs = s.delta_log;
+    r.decay_logs = s.decay_log;
+    r.channels = s.e->shard.channels;
+    r.key_heads = s.e->shard.nk;
+    r.value_heads = s.e->shard.nv;
+    r.layers = s.e->gdn_layers;
+    r.max_logged = kMaxBlock;
+    r.accepted = accepted + 1;
+    GFXB_TRY(launch_gdn_restore(r, s.stream));
+    s.host_position = base + accepted + 1;
+    s.mtp_position = mtp_base + accepted + 1;
+    s.last_hidden = s.hidden[c.layers % 2] + static_cast<std::size_t>(accepted) * c.hidden;
+  } else {
+    // The verifier's final states become current. Copied rather than swapped
+    // because the captured greedy graph holds the state addresses.
+    GFXB_TRY(cuda_check(cudaMemcpyAsync(s.conv_states, s.conv_snapshot, conv_elems * sizeof(__half),
+                                        cudaMemcpyDeviceToDevice, s.stream),
+                        "conv state commit failed"));
+    GFXB_TRY(cuda_check(cudaMemcpyAsync(s.gdn_states, s.gdn_snapshot, state_elems * sizeof(float),
+                                        cudaMemcpyDeviceToDevice, s.stream),
+                        "recurrent state commit failed"));
+    s.host_position = base + batch;
+    s.mtp_position = mtp_base + draft_count;
+    s.last_hidden = s.hidden[c.layers % 2] + static_cast<std::size_t>(draft_count) * c.hidden;
+    // advance only the MTP KV cache through the final draft (qwen_runtime.cpp:1520-1534)
+    const std::uint64_t position = s.mtp_position;
+    std::memcpy(s.pinned + 64, &position, sizeof position);
+    GFXB_TRY(cuda_check(cudaMemcpyAsync(s.mtp_positions, s.pinned + 64, 8, cudaMemcpyHostToDevice, s.stream),
+                        "upload failed"));
+    GFXB_TRY(enqueue_mtp(s, s.draft_tokens + draft_count - 1, s.last_hidden - c.hidden, s.mtp_positions, nullptr));
+    GFXB_TRY(cuda_check(cudaStreamSynchronize(s.stream), "MTP cache advance failed"));
+    s.mtp_position += 1;
+  }
+  s.mtp_chain_active = false;
+  for (unsigned i = 0; i < accepted; ++i) tokens[i] = host[i];
+  tokens[accepted] = host[kMaxBlock + accepted];
+  *token_count = accepted + 1;
+  *accepted_out = accepted;
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_session_position(const gfxb_session* session, std::uint64_t* position) {
+  if (session == nullptr || position == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  *position = session->host_position;
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_session_read_state(gfxb_session* session, std::uint16_t* hidden, float* logits,
+                                       std::size_t logits_count) {
+  if (session == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null session");
+  gfxb_session& s = *session;
+  GFXB_TRY(cuda_check(cudaStreamSynchronize(s.stream), "session synchronisation failed"));
+  if (hidden != nullptr && s.last_hidden != nullptr) {
+    GFXB_TRY(cuda_check(cudaMemcpy(hidden, s.last_hidden, s.e->cfg.hidden * sizeof(__half), cudaMemcpyDeviceToHost),
+                        "hidden download failed"));
+  }
+  if (logits != nullptr) {
+    const std::size_t n = std::min<std::size_t>(logits_count, s.e->shard.vocab);
+    GFXB_TRY(cuda_check(cudaMemcpy(logits, s.logits, n * sizeof(float), cudaMemcpyDeviceToHost), "logit download failed"));
+  }
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_session_enqueue_gemv(gfxb_session* session, int kind, unsigned launches, std::uint64_t* bytes) {
+  if (session == nullptr || launches == 0) return fail(GFXB_INVALID_ARGUMENT, "invalid GEMV benchmark arguments");
+  gfxb_session& s = *session;
+  gfxb_engine& e = *s.e;
+  // Cycle over the layers that carry the requested projection so every launch
+  // streams its weights from HBM (one layer's matrices fit in L2; 48 do not).
+  std::vector<const Layer*> layers;
+  for (const Layer& L : e.layers) {
+    if (kind == 0 || kind == 1 || (kind == 2 && !L.attention)) layers.push_back(&L);
+  }
+  if (layers.empty()) return fail(GFXB_INVALID_ARGUMENT, "no layer carries the requested projection");
+  std::uint64_t total = 0;
+  for (unsigned i = 0; i < launches; ++i) {
+    const Layer& L = *layers[i % layers.size()];
+    std::vector<std::pair<const QMatrix*, void*>> mats;
+    if (kind == 0) mats = {{&L.gate, s.gate}, {&L.up, s.up}};
+    else if (kind == 1) mats = {{&L.down, s.update}};
+    else mats = {{&L.qkv, s.proj_main}, {&L.z, s.proj_z}, {&L.a, s.proj_a}, {&L.b, s.proj_b}};
+    GFXB_TRY(gemv(s, mats, 1));
+    if (i == 0) {
+      const QMatrix& first = *mats[0].first;
+      const std::uint32_t bits = first.format == GFXB_W2 ? 2 : (first.format == GFXB_W3 ? 3 : 4);
+      for (const auto& m : mats) {
+        const std::uint64_t rows = m.first->rows, cols = m.first->cols;
+        total += rows * cols * bits / 8 + rows * (cols / 128) * 2 + rows * 4;  // codes + fp16 scales + fp32 out
+      }
+      const std::uint64_t cols = first.cols;
+      total += cols / 2 + cols / 128 * 2;  // A4 activation + its fp16 group scales
+    }
+  }
+  if (bytes != nullptr) *bytes = total;
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_read_device_errors(std::uint32_t* flags) {
+  if (flags == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  std::uint32_t a = 0, b = 0;
+  GFXB_TRY(read_gemv_error(&a, true));
+  GFXB_TRY(read_ops_error(&b, true));
+  *flags = a | b;
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_rope_table(std::size_t positions, unsigned rotary, float theta, float* cos_table,
+                               float* sin_table) {
+  if (cos_table == nullptr || sin_table == nullptr || rotary == 0 || (rotary & 1u) != 0 || !(theta > 1.0f)) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid RoPE table arguments");
+  }
+  const unsigned half = rotary / 2;
+  for (std::size_t p = 0; p < positions; ++p) {
+    for (unsigned f = 0; f < half; ++f) {
+      const float exponent = (2.0f * static_cast<float>(f)) / static_cast<float>(rotary);
+      const float inv_freq = static_cast<float>(std::pow(static_cast<double>(theta), -static_cast<double>(exponent)));
+      const float angle = static_cast<float>(p) * inv_freq;
+      cos_table[p * half + f] = static_cast<float>(std::cos(static_cast<double>(angle)));
+      sin_table[p * half + f] = static_cast<float>(std::sin(static_cast<double>(angle)));
+    }
+  }
+  return GFXB_OK;
+}

@@ -9,6 +9,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <utility>
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -183,5 +184,115 @@ __device__ __forceinline__ void mma_s8_16832(int (&c)[4], const std::uint32_t (&
 }
 
 inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
+
+// ---- programmatic dependent launch -------------------------------------------
+// Every kernel of the decode chain lets its successor launch early
+// (pdl_trigger) and waits for its predecessor's completion and memory
+// (pdl_wait) before it reads a predecessor's output or writes any global
+// memory. Work that depends on neither (weight prefetch) goes in between.
+
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+bool pdl_enabled();
+
+template <typename... KernelArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, std::size_t shared_bytes,
+                          cudaStream_t stream, unsigned cluster, Args&&... args) {
+  cudaLaunchConfig_t config{};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = shared_bytes;
+  config.stream = stream;
+  cudaLaunchAttribute attributes[2];
+  unsigned count = 0;
+  if (pdl_enabled()) {
+    attributes[count].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attributes[count].val.programmaticStreamSerializationAllowed = 1;
+    ++count;
+  }
+  if (cluster > 0) {
+    attributes[count].id = cudaLaunchAttributeClusterDimension;
+    attributes[count].val.clusterDim.x = cluster;
+    attributes[count].val.clusterDim.y = 1;
+    attributes[count].val.clusterDim.z = 1;
+    ++count;
+  }
+  config.attrs = attributes;
+  config.numAttrs = count;
+  return cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
+}
+
+// ---- shared-memory staging: mbarriers, bulk copies, clusters ---------------
+
+__device__ __forceinline__ std::uint32_t smem_addr(const void* pointer) {
+  return static_cast<std::uint32_t>(__cvta_generic_to_shared(pointer));
+}
+
+__device__ __forceinline__ void mbar_init(std::uint64_t* bar, std::uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(std::uint64_t* bar, std::uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+// Global -> this CTA's shared memory, completion counted on `bar` (no multicast).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, std::uint32_t bytes, std::uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(std::uint64_t* bar, std::uint32_t parity) {
+  std::uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Every wait is bounded: on expiry the kernel records kDeviceErrorTimeout in
+// `error` (when given) and the caller skips the work instead of hanging.
+constexpr std::uint32_t kDeviceErrorTimeout = 1u;
+constexpr std::uint32_t kWaitLimit = 1u << 22;
+
+__device__ __forceinline__ bool mbar_wait_bounded(std::uint64_t* bar, std::uint32_t parity,
+                                                  std::uint32_t* error) {
+  for (std::uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  if (error != nullptr) atomicOr(error, kDeviceErrorTimeout);
+  return false;
+}
+
+__device__ __forceinline__ std::uint32_t cluster_ctarank() {
+  std::uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  return rank;
+}
+
+__device__ __forceinline__ std::uint32_t map_shared_rank(std::uint32_t address, std::uint32_t rank) {
+  std::uint32_t mapped;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(mapped) : "r"(address), "r"(rank));
+  return mapped;
+}
+
+__device__ __forceinline__ void st_cluster_s32(std::uint32_t address, int value) {
+  asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(address), "r"(value) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 }  // namespace gfxb

@@ -149,6 +149,7 @@ struct GemvArgs {
   std::uint32_t columns;
   std::uint32_t groups;
   std::uint32_t batch;
+  std::uint32_t act_stride;  // elements between tokens in the activation pack (>= columns)
 };
 
 // Locate the matrix a CTA's global tile index belongs to.
@@ -170,6 +171,8 @@ __device__ __forceinline__ MatrixArg select_matrix(const GemvArgs& args, std::ui
 // groups in ascending order. Weights are prefetched two rounds ahead.
 template <int Bits, int NB>
 __global__ __launch_bounds__(256) void gemv_b200_kernel(const GemvArgs args) {
+  pdl_trigger();
+  pdl_wait();
   std::uint32_t tile = blockIdx.x;
   const MatrixArg m = select_matrix(args, tile);
   const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
@@ -207,7 +210,7 @@ __global__ __launch_bounds__(256) void gemv_b200_kernel(const GemvArgs args) {
           if (w < round_groups) {
             const std::uint32_t gg = 8u * r + w;
             scale_product[p][w] = __fmul_rn(h2f(tile_scales[gg * 16u + row]),
-                                            h2f(args.act_scales[token * G + gg]));
+                                            h2f(args.act_scales[token * (args.act_stride / kGroup) + gg]));
           }
         }
       }
@@ -220,7 +223,7 @@ __global__ __launch_bounds__(256) void gemv_b200_kernel(const GemvArgs args) {
       for (int nb = 0; nb < NB; ++nb) {
         std::uint32_t token = nb * 8u + gl;
         token = token < B ? token : B - 1u;
-        const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * K +
+        const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * args.act_stride +
                                 static_cast<std::size_t>(g) * kGroup + tq * 32u;
         const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(ap));
         const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(ap + 16));
@@ -231,12 +234,12 @@ __global__ __launch_bounds__(256) void gemv_b200_kernel(const GemvArgs args) {
         mma_s8_16832(c, a[3], b1.z, b1.w);
         const std::uint32_t t0 = nb * 8u + 2u * tq, t1 = t0 + 1u;
         if (t0 < B) {
-          const int s0 = args.act_sums[t0 * G + g];
+          const int s0 = args.act_sums[t0 * (args.act_stride / kGroup) + g];
           dots[warp][gl][t0] = kAlpha * c[0] + kBeta * s0;
           dots[warp][gl + 8][t0] = kAlpha * c[2] + kBeta * s0;
         }
         if (t1 < B) {
-          const int s1 = args.act_sums[t1 * G + g];
+          const int s1 = args.act_sums[t1 * (args.act_stride / kGroup) + g];
           dots[warp][gl][t1] = kAlpha * c[1] + kBeta * s1;
           dots[warp][gl + 8][t1] = kAlpha * c[3] + kBeta * s1;
         }
@@ -279,6 +282,212 @@ __global__ __launch_bounds__(256) void gemv_b200_kernel(const GemvArgs args) {
 }
 
 // ---------------------------------------------------------------------------
+// Streaming GEMV for batch <= 8 (the decode regime).
+//
+// A cluster of P CTAs owns one 16-row tile; CTA p owns a contiguous range of
+// its 128-column groups. One thread stages the CTA's whole weight range into
+// shared memory with bulk copies (one mbarrier per 8 groups), so every byte
+// the CTA needs is in flight from the first cycle. Warps turn staged groups
+// into exact int32 dots on the tensor cores and store them into the cluster
+// leader's shared memory (DSMEM). After a cluster barrier the leader runs the
+// reference's ordered fp32 chain over all groups of the tile.
+// ---------------------------------------------------------------------------
+
+__device__ std::uint32_t g_gemv_error;
+
+struct StreamLayout {
+  std::uint32_t per_part;     // groups per cluster rank
+  std::uint32_t weight_bytes;  // per_part * block
+  std::uint32_t scale_bytes;   // G * 32
+  std::uint32_t dot_bytes;     // G * 16 * B * 4
+  std::uint32_t act_scale_bytes;  // G * B * 2, rounded up to 16
+  std::uint32_t bar_offset;
+  std::uint32_t total;
+};
+
+__host__ __device__ inline StreamLayout stream_layout(int bits, std::uint32_t groups, std::uint32_t parts,
+                                                      std::uint32_t batch) {
+  StreamLayout s{};
+  s.per_part = (groups + parts - 1) / parts;
+  s.weight_bytes = s.per_part * static_cast<std::uint32_t>(bits) * 256u;
+  s.scale_bytes = groups * 32u;
+  s.dot_bytes = groups * 16u * batch * 4u;
+  s.act_scale_bytes = (groups * batch * 2u + 15u) & ~15u;
+  s.bar_offset = (s.weight_bytes + s.scale_bytes + s.dot_bytes + s.act_scale_bytes + 15u) & ~15u;
+  const std::uint32_t bars = (s.per_part + 7u) / 8u + 1u;
+  s.total = s.bar_offset + bars * 8u;
+  return s;
+}
+
+template <int Bits>
+__device__ __forceinline__ void load_lane_shared(const std::uint8_t* block, unsigned lane, LaneWords<Bits>& w) {
+  if constexpr (Bits == 3) {
+    w.p0 = *reinterpret_cast<const uint4*>(block + 16u * lane);
+    w.p1 = *reinterpret_cast<const uint2*>(block + 512u + 8u * lane);
+  } else if constexpr (Bits == 4) {
+    w.p0 = *reinterpret_cast<const uint4*>(block + 16u * lane);
+    w.p1 = *reinterpret_cast<const uint4*>(block + 512u + 16u * lane);
+  } else {
+    w.p0 = *reinterpret_cast<const uint4*>(block + 16u * lane);
+  }
+}
+
+template <int Bits>
+__global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, std::uint32_t parts) {
+  extern __shared__ __align__(128) std::uint8_t smem[];
+  pdl_trigger();
+  const std::uint32_t part = cluster_ctarank();
+  std::uint32_t tile = blockIdx.x / parts;
+  const MatrixArg m = select_matrix(args, tile);
+  const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const unsigned gl = lane >> 2, tq = lane & 3u;
+  const std::uint32_t G = args.groups, B = args.batch, K = args.columns;
+  constexpr std::uint32_t kBlock = Bits * 256u;
+  constexpr int kAlpha = Codec<Bits>::alpha, kBeta = Codec<Bits>::beta;
+  const StreamLayout layout = stream_layout(Bits, G, parts, B);
+  const std::uint32_t g_begin = min(G, part * layout.per_part);
+  const std::uint32_t n = min(G, g_begin + layout.per_part) - g_begin;
+  const std::uint32_t chunks = (n + 7u) / 8u;
+
+  std::uint8_t* stage = smem;
+  __half* tile_scales = reinterpret_cast<__half*>(smem + layout.weight_bytes);
+  std::int32_t* dots = reinterpret_cast<std::int32_t*>(smem + layout.weight_bytes + layout.scale_bytes);
+  __half* act_scale_stage =
+      reinterpret_cast<__half*>(smem + layout.weight_bytes + layout.scale_bytes + layout.dot_bytes);
+  std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(smem + layout.bar_offset);
+  const std::uint32_t scale_bar = (layout.per_part + 7u) / 8u;
+
+  if (threadIdx.x == 0) {
+    for (std::uint32_t c = 0; c <= scale_bar; ++c) mbar_init(&bars[c], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const std::uint8_t* source = m.codes + (static_cast<std::size_t>(tile) * G + g_begin) * kBlock;
+    for (std::uint32_t c = 0; c < chunks; ++c) {
+      const std::uint32_t bytes = min(8u, n - 8u * c) * kBlock;
+      mbar_expect_tx(&bars[c], bytes);
+      bulk_g2s(stage + 8u * c * kBlock, source + 8u * c * kBlock, bytes, &bars[c]);
+    }
+    if (part == 0) {
+      mbar_expect_tx(&bars[scale_bar], layout.scale_bytes);
+      bulk_g2s(tile_scales, m.scales + static_cast<std::size_t>(tile) * G * 16u, layout.scale_bytes,
+               &bars[scale_bar]);
+    }
+  }
+
+  // Weights and their scales never depend on the previous kernel; the
+  // activation pack does.
+  pdl_wait();
+  if (part == 0) {
+    const std::uint32_t act_groups = args.act_stride / kGroup;
+    for (std::uint32_t i = threadIdx.x; i < G * B; i += blockDim.x) {
+      const std::uint32_t tok = i / G, g = i - tok * G;
+      act_scale_stage[i] = args.act_scales[static_cast<std::size_t>(tok) * act_groups + g];
+    }
+  }
+  const std::uint32_t leader_dots = map_shared_rank(smem_addr(dots), 0);
+  const std::uint32_t token = min(gl, B - 1u);
+  for (std::uint32_t local = warp; local < n; local += 8u) {
+    const std::uint32_t g = g_begin + local;
+    const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * args.act_stride +
+                            static_cast<std::size_t>(g) * kGroup + tq * 32u;
+    const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(ap));
+    const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(ap + 16));
+    const std::uint32_t t0 = 2u * tq, t1 = t0 + 1u;
+    const std::uint32_t act_groups = args.act_stride / kGroup;
+    const int s0 = t0 < B ? __ldg(args.act_sums + t0 * act_groups + g) : 0;
+    const int s1 = t1 < B ? __ldg(args.act_sums + t1 * act_groups + g) : 0;
+    if (!mbar_wait_bounded(&bars[local / 8u], 0, &g_gemv_error)) break;
+    LaneWords<Bits> w;
+    load_lane_shared<Bits>(stage + local * kBlock, lane, w);
+    std::uint32_t a[4][4];
+    unpack(w, a);
+    int c[4] = {0, 0, 0, 0};
+    mma_s8_16832(c, a[0], b0.x, b0.y);
+    mma_s8_16832(c, a[1], b0.z, b0.w);
+    mma_s8_16832(c, a[2], b1.x, b1.y);
+    mma_s8_16832(c, a[3], b1.z, b1.w);
+    const std::uint32_t row_base = g * 16u;
+    if (t0 < B) {
+      st_cluster_s32(leader_dots + ((row_base + gl) * B + t0) * 4u, kAlpha * c[0] + kBeta * s0);
+      st_cluster_s32(leader_dots + ((row_base + gl + 8u) * B + t0) * 4u, kAlpha * c[2] + kBeta * s0);
+    }
+    if (t1 < B) {
+      st_cluster_s32(leader_dots + ((row_base + gl) * B + t1) * 4u, kAlpha * c[1] + kBeta * s1);
+      st_cluster_s32(leader_dots + ((row_base + gl + 8u) * B + t1) * 4u, kAlpha * c[3] + kBeta * s1);
+    }
+  }
+  cluster_sync_all();
+  if (part != 0) return;
+  const std::uint32_t pairs = 16u * B;
+  if (threadIdx.x >= pairs) return;
+  if (!mbar_wait_bounded(&bars[scale_bar], 0, &g_gemv_error)) return;
+  const std::uint32_t row = threadIdx.x & 15u, tok = threadIdx.x >> 4;
+  const __half* act_scales = act_scale_stage + static_cast<std::size_t>(tok) * G;
+  float accumulator = 0.0f;
+  std::uint32_t g = 0;
+  for (; g + 8u <= G; g += 8u) {
+    float product[8];
+    int dot[8];
+#pragma unroll
+    for (unsigned i = 0; i < 8; ++i) {
+      product[i] = __fmul_rn(h2f(tile_scales[(g + i) * 16u + row]), h2f(act_scales[g + i]));
+      dot[i] = dots[((g + i) * 16u + row) * B + tok];
+    }
+#pragma unroll
+    for (unsigned i = 0; i < 8; ++i) accumulator = fmaf(static_cast<float>(dot[i]), product[i], accumulator);
+  }
+  for (; g < G; ++g) {
+    const float product = __fmul_rn(h2f(tile_scales[g * 16u + row]), h2f(act_scales[g]));
+    accumulator = fmaf(static_cast<float>(dots[(g * 16u + row) * B + tok]), product, accumulator);
+  }
+  const std::size_t index = static_cast<std::size_t>(tok) * (m.tiles * 16u) + tile * 16u + row;
+  if (m.output_f16) {
+    static_cast<__half*>(m.output)[index] = f2h(accumulator);
+  } else {
+    static_cast<float*>(m.output)[index] = accumulator;
+  }
+}
+
+template <int Bits>
+int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t stream) {
+  std::uint32_t parts = total_tiles >= 1024u ? 1u : (total_tiles >= 512u ? 2u : 4u);
+  while (parts > 1u && parts > args.groups) parts >>= 1;
+  const StreamLayout layout = stream_layout(Bits, args.groups, parts, args.batch);
+  static int configured_bytes = 0;
+  if (static_cast<int>(layout.total) > configured_bytes) {
+    const cudaError_t error = cudaFuncSetAttribute(gemv_stream_kernel<Bits>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (error != cudaSuccess) {
+      set_error_cuda(error, "GEMV shared-memory configuration failed");
+      return GFXB_CUDA_ERROR;
+    }
+    configured_bytes = 200 * 1024;
+  }
+  if (layout.total > 200u * 1024u) return fail(GFXB_UNSUPPORTED, "GEMV shape exceeds shared memory");
+  cudaLaunchConfig_t config{};
+  config.gridDim = dim3(total_tiles * parts);
+  config.blockDim = dim3(256);
+  config.dynamicSmemBytes = layout.total;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeClusterDimension;
+  attribute[0].val.clusterDim.x = parts;
+  attribute[0].val.clusterDim.y = 1;
+  attribute[0].val.clusterDim.z = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  const cudaError_t error = launch_kernel(gemv_stream_kernel<Bits>, config.gridDim, config.blockDim,
+                                          config.dynamicSmemBytes, stream, parts, args, parts);
+  if (error != cudaSuccess) {
+    set_error_cuda(error, "streaming GEMV launch failed");
+    return GFXB_CUDA_ERROR;
+  }
+  return GFXB_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Reference-layout GEMM (drop-in for launch_gfx12_i4_gemm / _i8_gemm): gfx12
 // tiled weights staged per warp in shared memory, activations read in the
 // reference's packed-A4 or row-major A8 layout, group sums formed on the fly.
@@ -312,6 +521,8 @@ __global__ __launch_bounds__(256) void gemm_gfx12_kernel(
     const std::uint8_t* __restrict__ weights, const __half* __restrict__ weight_scales,
     const std::uint8_t* __restrict__ activations, const __half* __restrict__ activation_scales,
     float* __restrict__ output, std::uint32_t rows, std::uint32_t columns, std::uint32_t batch) {
+  pdl_trigger();
+  pdl_wait();
   const std::uint32_t tile = blockIdx.x;
   const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const unsigned gl = lane >> 2, tq = lane & 3u;
@@ -439,6 +650,8 @@ __global__ __launch_bounds__(128) void pack_activation_kernel(
     const __half* __restrict__ input, std::int8_t* __restrict__ codes, __half* __restrict__ scales,
     std::int32_t* __restrict__ sums, std::uint8_t* __restrict__ packed_a4,
     std::uint32_t columns, std::uint32_t groups) {
+  pdl_trigger();
+  pdl_wait();
   const std::uint32_t linear = blockIdx.x;
   const std::uint32_t token = linear / groups, group = linear - token * groups;
   const unsigned i = threadIdx.x, lane = i & 31u, warp = i >> 5;
@@ -481,6 +694,8 @@ template <int Bits>
 __global__ __launch_bounds__(128) void quantize_reference_kernel(
     const __half* __restrict__ input, std::uint8_t* __restrict__ output, __half* __restrict__ scales,
     std::uint32_t columns, std::uint32_t groups) {
+  pdl_trigger();
+  pdl_wait();
   const std::uint32_t linear = blockIdx.x;
   const std::uint32_t token = linear / groups, group = linear - token * groups;
   const unsigned i = threadIdx.x, lane = i & 31u, warp = i >> 5;
@@ -574,16 +789,40 @@ __device__ __forceinline__ std::uint64_t hash3(std::uint64_t seed, std::uint64_t
   return mix64(mix64(seed ^ (stream * 0xd1b54a32d192ed03ULL)) + index);
 }
 
-// Synthetic weights: reference code = top `bits` bits of hash(seed, 2*tensor, row*K + col).
+// Synthetic weights: the reference code of global (row, column) is the top
+// `bits` bits of hash(seed, 2*tensor, row*K + column). A shard generates its
+// local rows/columns through a row map (up to three contiguous segments of
+// global rows) and a column offset, so every tensor-parallel rank holds
+// exactly its slice of the same global model.
+struct RowMap {
+  std::uint32_t segments;
+  std::uint32_t local_begin[4];
+  std::uint32_t global_begin[3];
+  __host__ __device__ std::uint32_t operator()(std::uint32_t row) const {
+    std::uint32_t i = 0;
+    while (i + 1 < segments && row >= local_begin[i + 1]) ++i;
+    return global_begin[i] + (row - local_begin[i]);
+  }
+};
+
+// Zero-mean synthetic reference codes: W2 levels {-3,-1,1,3}, W3 q uniform on
+// {-3..3}, W4 q uniform on {-7..7} (two's-complement nibble).
+__host__ __device__ __forceinline__ std::uint32_t synthetic_code(std::uint64_t h, int bits) {
+  if (bits == 2) return static_cast<std::uint32_t>(h >> 62);
+  if (bits == 3) return static_cast<std::uint32_t>((h >> 32) % 7u + 1u);
+  return static_cast<std::uint32_t>((static_cast<int>((h >> 32) % 15u) - 7) & 0x0f);
+}
+
 struct HashSource {
   std::uint64_t seed;
   std::uint32_t tensor;
-  std::uint32_t columns;
+  std::uint32_t global_columns;
+  std::uint32_t column_offset;
+  RowMap rows;
   int bits;
   __device__ std::uint32_t operator()(std::uint32_t row, std::uint32_t column) const {
-    const std::uint64_t h = hash3(seed, 2ull * tensor, static_cast<std::uint64_t>(row) * columns + column);
-    const std::uint32_t code = static_cast<std::uint32_t>(h >> (64 - bits));
-    return bits == 4 ? (code ^ 8u) : code;
+    const std::uint64_t index = static_cast<std::uint64_t>(rows(row)) * global_columns + column + column_offset;
+    return synthetic_code(hash3(seed, 2ull * tensor, index), bits) ^ (bits == 4 ? 8u : 0u);
   }
 };
 
@@ -701,7 +940,7 @@ int validate_matrix_shape(int format, std::size_t rows, std::size_t columns) {
 
 template <int Bits, int NB>
 void launch_gemv_typed(const GemvArgs& args, unsigned grid, cudaStream_t stream) {
-  gemv_b200_kernel<Bits, NB><<<grid, 256, 0, stream>>>(args);
+  launch_kernel(gemv_b200_kernel<Bits, NB>, dim3(grid), dim3(256), 0, stream, 0, args);
 }
 
 template <int Bits>
@@ -755,14 +994,133 @@ int gfx12_gemm(int format, const std::uint8_t* w, const std::uint16_t* ws, const
 
 }  // namespace
 
-// Exposed to the host runtime (engine weight generation).
+// ---------------------------------------------------------------------------
+// synthetic weight generation for the engine (see HashSource)
+// ---------------------------------------------------------------------------
+
+namespace {
+
+__device__ __forceinline__ float unit_float(std::uint64_t h) {
+  return __fmul_rn(static_cast<float>(h >> 40), 1.0f / 16777216.0f);
+}
+
+__global__ void gen_tiled_scales_kernel(std::uint64_t seed, std::uint32_t tensor, RowMap rows,
+                                        std::uint32_t global_groups, std::uint32_t group_offset,
+                                        std::uint32_t local_rows, std::uint32_t local_groups, float lo,
+                                        float hi, __half* __restrict__ tiled) {
+  const std::uint64_t index = static_cast<std::uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= static_cast<std::uint64_t>(local_rows) * local_groups) return;
+  const std::uint32_t row = static_cast<std::uint32_t>(index / local_groups);
+  const std::uint32_t group = static_cast<std::uint32_t>(index % local_groups);
+  const std::uint64_t global = static_cast<std::uint64_t>(rows(row)) * global_groups + group + group_offset;
+  const float value = fmaf(__fsub_rn(hi, lo), unit_float(hash3(seed, 2ull * tensor + 1, global)), lo);
+  tiled[(static_cast<std::size_t>(row / 16u) * local_groups + group) * 16u + (row & 15u)] = f2h(value);
+}
+
+__global__ void gen_rowmajor_kernel(std::uint64_t seed, std::uint32_t tensor, std::uint32_t rows,
+                                    std::uint32_t columns, int bits, float lo, float hi,
+                                    std::uint8_t* __restrict__ codes, __half* __restrict__ scales) {
+  // one thread per output byte of the reference row-major layout (W2/W4)
+  const std::uint32_t per_byte = 8u / static_cast<std::uint32_t>(bits);
+  const std::uint64_t bytes = static_cast<std::uint64_t>(rows) * columns / per_byte;
+  const std::uint64_t index = static_cast<std::uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index < bytes) {
+    std::uint32_t value = 0;
+    for (std::uint32_t i = 0; i < per_byte; ++i) {
+      const std::uint64_t element = index * per_byte + i;
+      const std::uint32_t code = synthetic_code(hash3(seed, 2ull * tensor, element), bits);
+      value |= code << (i * static_cast<std::uint32_t>(bits));
+    }
+    codes[index] = static_cast<std::uint8_t>(value);
+  }
+  const std::uint64_t groups = static_cast<std::uint64_t>(rows) * (columns / kGroup);
+  if (index < groups) {
+    scales[index] = f2h(fmaf(__fsub_rn(hi, lo), unit_float(hash3(seed, 2ull * tensor + 1, index)), lo));
+  }
+}
+
+__global__ void gen_bf16_kernel(std::uint64_t seed, std::uint32_t tensor, std::uint64_t offset,
+                                std::uint64_t count, float lo, float hi, std::uint16_t* __restrict__ out) {
+  const std::uint64_t index = static_cast<std::uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= count) return;
+  const float value = fmaf(__fsub_rn(hi, lo), unit_float(hash3(seed, 2ull * tensor, index + offset)), lo);
+  std::uint32_t bits = __float_as_uint(value);
+  bits += 0x7fffu + ((bits >> 16) & 1u);
+  out[index] = static_cast<std::uint16_t>(bits >> 16);
+}
+
+}  // namespace
+
+void scale_range(int format, float* lo, float* hi) {
+  switch (format) {
+    case GFXB_W2: *lo = 0.0045f; *hi = 0.0134f; break;
+    case GFXB_W3: *lo = 0.0050f; *hi = 0.0150f; break;
+    default: *lo = 0.0023f; *hi = 0.0069f; break;
+  }
+}
+
 int generate_b200_weights(std::uint64_t seed, std::uint32_t tensor, int format, std::uint8_t* codes,
-                          std::size_t rows, std::size_t columns, cudaStream_t stream) {
+                          std::uint16_t* tiled_scales, std::size_t rows, std::size_t columns,
+                          std::size_t global_columns, std::size_t column_offset, const std::uint32_t* segment_local,
+                          const std::uint32_t* segment_global, std::uint32_t segments, cudaStream_t stream) {
   const int shape = validate_matrix_shape(format, rows, columns);
   if (shape != GFXB_OK) return shape;
+  if (segments == 0 || segments > 3 || column_offset % kGroup != 0) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid shard map");
+  }
+  RowMap map{};
+  map.segments = segments;
+  for (std::uint32_t i = 0; i < segments; ++i) {
+    map.local_begin[i] = segment_local[i];
+    map.global_begin[i] = segment_global[i];
+  }
   const int bits = bits_of(format);
-  return launch_write_b200(HashSource{seed, tensor, static_cast<std::uint32_t>(columns), bits}, codes,
-                           rows, columns, bits, stream);
+  int status = launch_write_b200(
+      HashSource{seed, tensor, static_cast<std::uint32_t>(global_columns), static_cast<std::uint32_t>(column_offset),
+                 map, bits},
+      codes, rows, columns, bits, stream);
+  if (status != GFXB_OK) return status;
+  float lo, hi;
+  scale_range(format, &lo, &hi);
+  const std::uint64_t total = rows * (columns / kGroup);
+  gen_tiled_scales_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+      seed, tensor, map, static_cast<std::uint32_t>(global_columns / kGroup),
+      static_cast<std::uint32_t>(column_offset / kGroup), static_cast<std::uint32_t>(rows),
+      static_cast<std::uint32_t>(columns / kGroup), lo, hi, reinterpret_cast<__half*>(tiled_scales));
+  return launch_status("synthetic scale generation failed");
+}
+
+int generate_rowmajor_weights(std::uint64_t seed, std::uint32_t tensor, int format, std::uint8_t* codes,
+                              std::uint16_t* scales, std::size_t rows, std::size_t columns, cudaStream_t stream) {
+  if (format != GFXB_W2 && format != GFXB_W4) return fail(GFXB_UNSUPPORTED, "row-major generation supports W2/W4");
+  const int bits = bits_of(format);
+  float lo, hi;
+  scale_range(format, &lo, &hi);
+  const std::uint64_t bytes = rows * columns * bits / 8u;
+  gen_rowmajor_kernel<<<static_cast<unsigned>((bytes + 255) / 256), 256, 0, stream>>>(
+      seed, tensor, static_cast<std::uint32_t>(rows), static_cast<std::uint32_t>(columns), bits, lo, hi, codes,
+      reinterpret_cast<__half*>(scales));
+  return launch_status("synthetic row-major generation failed");
+}
+
+int generate_bf16(std::uint64_t seed, std::uint32_t tensor, std::uint64_t offset, std::uint64_t count, float lo,
+                  float hi, std::uint16_t* out, cudaStream_t stream) {
+  gen_bf16_kernel<<<static_cast<unsigned>((count + 255) / 256), 256, 0, stream>>>(seed, tensor, offset, count, lo, hi,
+                                                                                   out);
+  return launch_status("synthetic bf16 generation failed");
+}
+
+int read_gemv_error(std::uint32_t* value, bool clear) {
+  cudaError_t error = cudaMemcpyFromSymbol(value, g_gemv_error, sizeof(std::uint32_t));
+  if (error == cudaSuccess && clear) {
+    const std::uint32_t zero = 0;
+    error = cudaMemcpyToSymbol(g_gemv_error, &zero, sizeof zero);
+  }
+  if (error != cudaSuccess) {
+    set_error_cuda(error, "device error word access failed");
+    return GFXB_CUDA_ERROR;
+  }
+  return GFXB_OK;
 }
 
 }  // namespace gfxb
@@ -816,19 +1174,19 @@ extern "C" int gfxb_pack_activation(int activation_bits, const std::uint16_t* in
   const auto* in = reinterpret_cast<const __half*>(input);
   auto* s = reinterpret_cast<__half*>(scales);
   if (activation_bits == 4) {
-    pack_activation_kernel<4><<<grid, 128, 0, as_stream(stream)>>>(
-        in, codes, s, sums, packed_a4, static_cast<std::uint32_t>(columns), groups);
+    launch_kernel(pack_activation_kernel<4>, grid, dim3(128), 0, as_stream(stream), 0, in, codes, s, sums,
+                  packed_a4, static_cast<std::uint32_t>(columns), groups);
   } else {
-    pack_activation_kernel<8><<<grid, 128, 0, as_stream(stream)>>>(
-        in, codes, s, sums, nullptr, static_cast<std::uint32_t>(columns), groups);
+    launch_kernel(pack_activation_kernel<8>, grid, dim3(128), 0, as_stream(stream), 0, in, codes, s, sums,
+                  static_cast<std::uint8_t*>(nullptr), static_cast<std::uint32_t>(columns), groups);
   }
   return launch_status("activation packing launch failed");
 }
 
-extern "C" int gfxb_lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, unsigned matrix_count,
-                                const std::int8_t* act_codes, const std::uint16_t* act_scales,
-                                const std::int32_t* act_sums, std::size_t columns, unsigned batch,
-                                void* stream) {
+namespace gfxb {
+int lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, unsigned matrix_count, const std::int8_t* act_codes,
+                const std::uint16_t* act_scales, const std::int32_t* act_sums, std::size_t columns,
+                std::size_t act_stride, unsigned batch, cudaStream_t stream) {
   GFXB_REQUIRE(matrices != nullptr && matrix_count >= 1 && matrix_count <= 4,
                "GEMV takes between one and four matrices");
   GFXB_REQUIRE(act_codes != nullptr && act_scales != nullptr && act_sums != nullptr,
@@ -857,12 +1215,28 @@ extern "C" int gfxb_lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, un
   args.columns = static_cast<std::uint32_t>(columns);
   args.groups = static_cast<std::uint32_t>(columns / kGroup);
   args.batch = batch;
+  args.act_stride = act_stride == 0 ? static_cast<std::uint32_t>(columns) : static_cast<std::uint32_t>(act_stride);
+  GFXB_REQUIRE(args.act_stride >= args.columns && args.act_stride % kGroup == 0, "activation stride is invalid");
   const int bits = bits_of(format);
   const unsigned grid = static_cast<unsigned>(total_tiles);
-  if (bits == 2) launch_gemv_bits<2>(args, grid, as_stream(stream));
-  else if (bits == 3) launch_gemv_bits<3>(args, grid, as_stream(stream));
-  else launch_gemv_bits<4>(args, grid, as_stream(stream));
+  if (batch <= 8) {
+    if (bits == 2) return launch_stream<2>(args, grid, stream);
+    if (bits == 3) return launch_stream<3>(args, grid, stream);
+    return launch_stream<4>(args, grid, stream);
+  }
+  if (bits == 2) launch_gemv_bits<2>(args, grid, stream);
+  else if (bits == 3) launch_gemv_bits<3>(args, grid, stream);
+  else launch_gemv_bits<4>(args, grid, stream);
   return launch_status("low-bit GEMV launch failed");
+}
+}  // namespace gfxb
+
+extern "C" int gfxb_lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, unsigned matrix_count,
+                                const std::int8_t* act_codes, const std::uint16_t* act_scales,
+                                const std::int32_t* act_sums, std::size_t columns, unsigned batch,
+                                void* stream) {
+  return gfxb::lowbit_gemv(format, matrices, matrix_count, act_codes, act_scales, act_sums, columns, 0, batch,
+                           as_stream(stream));
 }
 
 extern "C" int gfxb_quantize_activation_i4(const std::uint16_t* input, std::uint8_t* packed_output,

@@ -1,0 +1,882 @@
+// Decode-path operators for sm_100a: fused residual/RMSNorm/activation
+// packing, SwiGLU + packing, Gated-DeltaNet conv and recurrence with rollback
+// replay, fused Q/K RMSNorm + RoPE + KV append, chunked gated attention,
+// argmax and embedding gathers.
+//
+// Replaces the reference's qwen_ops.hip kernels. Each kernel follows the
+// reference arithmetic (file:line at each kernel) with one fixed reduction
+// order that the CPU oracle restates, so outputs compare bit for bit.
+#include <type_traits>
+
+#include "common.cuh"
+#include "ops.cuh"
+
+namespace gfxb {
+
+__device__ std::uint32_t g_ops_error;
+
+namespace {
+
+__device__ __forceinline__ std::uint32_t fragment_offset(std::uint32_t k) {
+  const std::uint32_t s = k >> 5, rest = k & 31u, half = rest >> 4, t = (rest & 15u) >> 2, j = k & 3u;
+  return t * 32u + s * 8u + half * 4u + j;
+}
+
+
+// Quantize one 128-group held by four consecutive warps (element = thread
+// index within the 128) with the reference A4/A8 rule and store it into a
+// GEMV activation pack. `slot` holds 8 floats of shared scratch per group.
+template <int ActBits>
+__device__ __forceinline__ void pack_group_128(float x, unsigned element, std::int8_t* codes, __half* scale_out,
+                                               std::int32_t* sum_out, float* max_slot, int* sum_slot) {
+  const unsigned lane = element & 31u, warp = element >> 5;
+  float amax = fabsf(x);
+#pragma unroll
+  for (unsigned offset = 16; offset != 0; offset >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
+  if (lane == 0) max_slot[warp] = amax;
+  __syncthreads();
+  amax = fmaxf(fmaxf(max_slot[0], max_slot[1]), fmaxf(max_slot[2], max_slot[3]));
+  constexpr float kDivisor = ActBits == 4 ? 7.0f : 127.0f;
+  constexpr int kLimit = ActBits == 4 ? 7 : 127;
+  const __half scale_h = f2h(amax == 0.0f ? 1.0f : __fdiv_rn(amax, kDivisor));
+  const int q = max(-kLimit, min(kLimit, f2i_rn(__fdiv_rn(x, h2f(scale_h)))));
+  codes[fragment_offset(element)] = static_cast<std::int8_t>(q);
+  int total = q;
+#pragma unroll
+  for (unsigned offset = 16; offset != 0; offset >>= 1) total += __shfl_xor_sync(0xffffffffu, total, offset);
+  if (lane == 0) sum_slot[warp] = total;
+  __syncthreads();
+  if (element == 0) {
+    *scale_out = scale_h;
+    *sum_out = sum_slot[0] + sum_slot[1] + sum_slot[2] + sum_slot[3];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// residual add + RMSNorm (+ activation pack), qwen_ops.hip:31-63, 176-217.
+// One 256-thread CTA per token; thread t owns elements t, t+256, ...; the sum
+// of squares is an fma chain per thread, the warp tree and the tree of the
+// eight warp sums. The normalized fp16 value is quantized per 128-group with
+// the reference's A4/A8 rule (lowbit_gemv.hip:373-436) into a GEMV pack.
+// ---------------------------------------------------------------------------
+
+constexpr unsigned kNormThreads = 256;
+constexpr unsigned kNormMaxIter = 64;  // H <= 16384
+
+template <int ActBits, unsigned Iterations>
+__global__ __launch_bounds__(kNormThreads) void residual_norm_pack_kernel(NormPackArgs args) {
+  pdl_trigger();
+  pdl_wait();
+  const std::uint32_t token = blockIdx.x;
+  const std::uint32_t H = args.elements;
+  const unsigned t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  constexpr unsigned iterations = Iterations;
+  const std::size_t row = static_cast<std::size_t>(token) * H;
+  __shared__ float warp_sums[8];
+  __shared__ float warp_max[Iterations][8];
+  __shared__ int warp_code_sums[Iterations][8];
+
+  float values[Iterations];
+  float square_sum = 0.0f;
+#pragma unroll
+  for (unsigned it = 0; it < iterations; ++it) {
+    const std::size_t index = row + it * kNormThreads + t;
+    float value;
+    if (args.embedding_codes != nullptr) {
+      value = 0.0f;  // replaced below
+    } else if (args.update != nullptr) {
+      const __half rounded = f2h(__fadd_rn(h2f(args.residual[index]), args.update[index]));
+      if (args.residual_out != nullptr) args.residual_out[index] = rounded;
+      value = h2f(rounded);
+    } else {
+      value = h2f(args.residual[index]);
+    }
+    values[it] = value;
+  }
+  if (args.embedding_codes != nullptr) {
+    // Embedding row gather fused as the input (lowbit_gemv.hip:158-189, W4/W2 row-major).
+    std::uint32_t id = args.device_tokens != nullptr ? args.device_tokens[token] : args.host_token;
+    const bool valid = id < args.embedding_rows;
+    const std::uint32_t groups = H / kGroup;
+#pragma unroll
+    for (unsigned it = 0; it < iterations; ++it) {
+      const std::uint32_t column = it * kNormThreads + t;
+      float value = 0.0f;
+      if (valid) {
+        int q;
+        if (args.embedding_bits == 2) {
+          const std::uint8_t packed = args.embedding_codes[static_cast<std::size_t>(id) * (H / 4u) + column / 4u];
+          q = static_cast<int>((packed >> ((column & 3u) * 2u)) & 3u) * 2 - 3;
+        } else {
+          const std::uint8_t packed = args.embedding_codes[static_cast<std::size_t>(id) * (H / 2u) + column / 2u];
+          const int code = (packed >> ((column & 1u) * 4u)) & 15;
+          q = code >= 8 ? code - 16 : code;
+        }
+        value = h2f(f2h(__fmul_rn(static_cast<float>(q),
+                                  h2f(args.embedding_scales[static_cast<std::size_t>(id) * groups + column / kGroup]))));
+      }
+      values[it] = value;
+      if (args.residual_out != nullptr) args.residual_out[row + column] = f2h(value);
+    }
+  }
+#pragma unroll
+  for (unsigned it = 0; it < iterations; ++it) square_sum = fmaf(values[it], values[it], square_sum);
+  square_sum = warp_sum_down(square_sum);
+  if (lane == 0) warp_sums[warp] = square_sum;
+  __syncthreads();
+  const float total = tree_of_eight(warp_sums, 8);
+  const float inverse = inv_sqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(H)), args.epsilon));
+#pragma unroll
+  for (unsigned it = 0; it < iterations; ++it) {
+    const std::uint32_t column = it * kNormThreads + t;
+    float scale = bf2f(args.weight[column]);
+    if (args.unit_offset) scale = __fadd_rn(scale, 1.0f);
+    const __half y = f2h(__fmul_rn(__fmul_rn(values[it], inverse), scale));
+    if (args.normalized_out != nullptr) args.normalized_out[row + column] = y;
+    values[it] = h2f(y);
+  }
+  if constexpr (ActBits != 0) {
+    // groups: element (it, t) belongs to group 2*it + (t >= 128), lane-local index t % 128
+#pragma unroll
+    for (unsigned it = 0; it < iterations; ++it) {
+      float amax = fabsf(values[it]);
+#pragma unroll
+      for (unsigned offset = 16; offset != 0; offset >>= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
+      }
+      if (lane == 0) warp_max[it][warp] = amax;
+    }
+    __syncthreads();
+    constexpr float kDivisor = ActBits == 4 ? 7.0f : 127.0f;
+    constexpr int kLimit = ActBits == 4 ? 7 : 127;
+    const unsigned half = warp >> 2;
+    const std::uint32_t groups = H / kGroup;
+#pragma unroll
+    for (unsigned it = 0; it < iterations; ++it) {
+      const float amax = fmaxf(fmaxf(warp_max[it][4 * half], warp_max[it][4 * half + 1]),
+                               fmaxf(warp_max[it][4 * half + 2], warp_max[it][4 * half + 3]));
+      const __half scale_h = f2h(amax == 0.0f ? 1.0f : __fdiv_rn(amax, kDivisor));
+      int q = f2i_rn(__fdiv_rn(values[it], h2f(scale_h)));
+      q = max(-kLimit, min(kLimit, q));
+      const std::uint32_t group = 2u * it + half;
+      const std::uint32_t local = t & 127u;
+      args.act_codes[row + group * kGroup + fragment_offset(local)] = static_cast<std::int8_t>(q);
+      if (ActBits == 4 && args.packed_a4 != nullptr) {
+        const int neighbour = __shfl_down_sync(0xffffffffu, q, 1);
+        if ((local & 1u) == 0) {
+          args.packed_a4[static_cast<std::size_t>(token) * (H / 2u) + group * 64u + local / 2u] =
+              static_cast<std::uint8_t>((q & 0x0f) | ((neighbour & 0x0f) << 4));
+        }
+      }
+      int code_sum = q;
+#pragma unroll
+      for (unsigned offset = 16; offset != 0; offset >>= 1) code_sum += __shfl_xor_sync(0xffffffffu, code_sum, offset);
+      if (lane == 0) warp_code_sums[it][warp] = code_sum;
+      if (local == 0) args.act_scales[static_cast<std::size_t>(token) * groups + group] = scale_h;
+    }
+    __syncthreads();
+    for (std::uint32_t group = t; group < groups; group += kNormThreads) {
+      const unsigned it = group >> 1, h = group & 1u;
+      args.act_sums[static_cast<std::size_t>(token) * groups + group] =
+          warp_code_sums[it][4 * h] + warp_code_sums[it][4 * h + 1] + warp_code_sums[it][4 * h + 2] +
+          warp_code_sums[it][4 * h + 3];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SiLU(gate) * up -> fp16 -> activation pack (qwen_ops.hip:108-163). One warp
+// per 128-group; lane l owns elements 4l..4l+3 (one 32-bit fragment word).
+// ---------------------------------------------------------------------------
+
+template <int ActBits>
+__global__ __launch_bounds__(256) void silu_pack_kernel(SiluPackArgs args) {
+  pdl_trigger();
+  pdl_wait();
+  const unsigned lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  const std::uint32_t groups = args.elements / kGroup;
+  const std::uint32_t linear = blockIdx.x * 8u + warp;
+  if (linear >= groups * args.batch) return;
+  const std::uint32_t token = linear / groups, group = linear - token * groups;
+  const std::size_t base = static_cast<std::size_t>(token) * args.elements + group * kGroup + 4u * lane;
+  const float4 g4 = *reinterpret_cast<const float4*>(args.gate + base);
+  const float4 u4 = *reinterpret_cast<const float4*>(args.up + base);
+  const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
+  const float us[4] = {u4.x, u4.y, u4.z, u4.w};
+  float x[4];
+  float amax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __half product = f2h(__fmul_rn(gx_silu(gs[j]), us[j]));
+    if (args.product_out != nullptr) args.product_out[base + j] = product;
+    x[j] = h2f(product);
+    amax = fmaxf(amax, fabsf(x[j]));
+  }
+  if (args.act_codes == nullptr) return;
+#pragma unroll
+  for (unsigned offset = 16; offset != 0; offset >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
+  constexpr float kDivisor = ActBits == 4 ? 7.0f : 127.0f;
+  constexpr int kLimit = ActBits == 4 ? 7 : 127;
+  const __half scale_h = f2h(amax == 0.0f ? 1.0f : __fdiv_rn(amax, kDivisor));
+  const float scale = h2f(scale_h);
+  std::uint32_t word = 0;
+  int code_sum = 0;
+  int q[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    q[j] = max(-kLimit, min(kLimit, f2i_rn(__fdiv_rn(x[j], scale))));
+    word |= (static_cast<std::uint32_t>(q[j]) & 0xffu) << (8 * j);
+    code_sum += q[j];
+  }
+  const std::size_t group_base = static_cast<std::size_t>(token) * args.elements + group * kGroup;
+  *reinterpret_cast<std::uint32_t*>(args.act_codes + group_base + fragment_offset(4u * lane)) = word;
+  if (ActBits == 4 && args.packed_a4 != nullptr) {
+    const std::uint32_t packed = static_cast<std::uint32_t>((q[0] & 15) | ((q[1] & 15) << 4)) |
+                                 (static_cast<std::uint32_t>((q[2] & 15) | ((q[3] & 15) << 4)) << 8);
+    *reinterpret_cast<std::uint16_t*>(args.packed_a4 + group_base / 2u + 2u * lane) =
+        static_cast<std::uint16_t>(packed);
+  }
+#pragma unroll
+  for (unsigned offset = 16; offset != 0; offset >>= 1) code_sum += __shfl_xor_sync(0xffffffffu, code_sum, offset);
+  if (lane == 0) {
+    args.act_scales[static_cast<std::size_t>(token) * groups + group] = scale_h;
+    args.act_sums[static_cast<std::size_t>(token) * groups + group] = code_sum;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// GDN causal conv (qwen_ops.hip:219-261): fp16 4-tap state per channel.
+// ---------------------------------------------------------------------------
+
+__global__ void gdn_conv_kernel(GdnConvArgs args) {
+  pdl_trigger();
+  pdl_wait();
+  const std::uint32_t channel = blockIdx.x * blockDim.x + threadIdx.x;
+  if (channel >= args.channels) return;
+  __half taps[4];
+  const __half* initial = args.initial_state + static_cast<std::size_t>(channel) * 4u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) taps[i] = initial[i];
+  float w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = bf2f(args.weight[static_cast<std::size_t>(channel) * 4u + i]);
+  for (std::uint32_t token = 0; token < args.batch; ++token) {
+    taps[0] = taps[1];
+    taps[1] = taps[2];
+    taps[2] = taps[3];
+    taps[3] = f2h(args.projected[static_cast<std::size_t>(token) * args.channels + channel]);
+    if (args.appended_log != nullptr) {
+      args.appended_log[static_cast<std::size_t>(token) * args.channels + channel] = taps[3];
+    }
+    float conv = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) conv = fmaf(h2f(taps[i]), w[i], conv);
+    args.output[static_cast<std::size_t>(token) * args.channels + channel] = f2h(gx_silu(conv));
+  }
+  __half* final_state = args.final_state + static_cast<std::size_t>(channel) * 4u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) final_state[i] = taps[i];
+}
+
+// ---------------------------------------------------------------------------
+// GDN recurrent step (qwen_ops.hip:263-411). One CTA of 128 threads per value
+// head; thread v keeps column S[:, v] of the 128x128 fp32 state in registers
+// across the whole token block (read once, written once). Per token: q/k
+// L2 norms (warp tree + tree of the four warp sums), decay/beta gates, the
+// delta-rule column update as two ordered fma chains over k, output RMSNorm
+// and SiLU(z) gate.
+// ---------------------------------------------------------------------------
+
+__global__ __launch_bounds__(128) void gdn_recurrent_kernel(GdnRecurrentArgs args) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr unsigned kHead = 128;
+  const unsigned vh = blockIdx.x, v = threadIdx.x, lane = v & 31u, warp = v >> 5;
+  const unsigned ratio = args.value_heads / args.key_heads;
+  const unsigned kh = vh / ratio;
+  const unsigned key_elements = args.key_heads * kHead;
+  const unsigned value_elements = args.value_heads * kHead;
+  const unsigned channels = 2u * key_elements + value_elements;
+  __shared__ float query[kHead];
+  __shared__ float key[kHead];
+  __shared__ float sums[3][4];
+  __shared__ float pack_max[4];
+  __shared__ int pack_sum[4];
+
+  float S[kHead];
+  const float* initial = args.initial_state + static_cast<std::size_t>(vh) * kHead * kHead;
+#pragma unroll
+  for (unsigned k = 0; k < kHead; ++k) S[k] = initial[k * kHead + v];
+  const float a_log = bf2f(args.a_log[vh]);
+  const float dt_bias = bf2f(args.dt_bias[vh]);
+  const float norm_weight = bf2f(args.norm_weight[v]);
+
+  for (std::uint32_t t = 0; t < args.batch; ++t) {
+    const __half* qkv = args.qkv + static_cast<std::size_t>(t) * channels;
+    const float q = h2f(qkv[kh * kHead + v]);
+    const float k = h2f(qkv[key_elements + kh * kHead + v]);
+    const float qs = warp_sum_down(__fmul_rn(q, q));
+    const float ks = warp_sum_down(__fmul_rn(k, k));
+    if (lane == 0) {
+      sums[0][warp] = qs;
+      sums[1][warp] = ks;
+    }
+    __syncthreads();
+    const float inv_q = __fmul_rn(inv_sqrt_rn(__fadd_rn(tree_of_eight(sums[0], 4), 1.0e-6f)), 0.08838834764831845f);
+    const float inv_k = inv_sqrt_rn(__fadd_rn(tree_of_eight(sums[1], 4), 1.0e-6f));
+    const std::uint32_t ab_stride = args.ab_stride != 0 ? args.ab_stride : args.value_heads;
+    const float a_value = __fadd_rn(args.a[static_cast<std::size_t>(t) * ab_stride + vh], dt_bias);
+    const float softplus = a_value > 20.0f ? a_value : gx_log1pf(gx_expf(a_value));
+    const float g = __fmul_rn(-gx_expf(a_log), softplus);
+    const float decay = gx_expf(g);
+    const float beta = gx_sigmoid(args.b[static_cast<std::size_t>(t) * ab_stride + vh]);
+    const float kn = __fmul_rn(k, inv_k);
+    query[v] = __fmul_rn(q, inv_q);
+    key[v] = kn;
+    if (args.decay_log != nullptr && v == 0) args.decay_log[static_cast<std::size_t>(t) * args.value_heads + vh] = decay;
+    if (args.key_log != nullptr && vh % ratio == 0) {
+      args.key_log[static_cast<std::size_t>(t) * key_elements + kh * kHead + v] = kn;
+    }
+    __syncthreads();
+    float memory = 0.0f;
+#pragma unroll
+    for (unsigned kk = 0; kk < kHead; ++kk) {
+      S[kk] = __fmul_rn(S[kk], decay);
+      memory = fmaf(S[kk], key[kk], memory);
+    }
+    const float value = h2f(qkv[2u * key_elements + vh * kHead + v]);
+    const float delta = __fmul_rn(__fsub_rn(value, memory), beta);
+    if (args.delta_log != nullptr) {
+      args.delta_log[static_cast<std::size_t>(t) * value_elements + vh * kHead + v] = delta;
+    }
+    float mixed = 0.0f;
+#pragma unroll
+    for (unsigned kk = 0; kk < kHead; ++kk) {
+      S[kk] = fmaf(key[kk], delta, S[kk]);
+      mixed = fmaf(S[kk], query[kk], mixed);
+    }
+    const float os = warp_sum_down(__fmul_rn(mixed, mixed));
+    if (lane == 0) sums[2][warp] = os;
+    __syncthreads();
+    const float inv_o = inv_sqrt_rn(__fadd_rn(__fdiv_rn(tree_of_eight(sums[2], 4), 128.0f), 1.0e-6f));
+    const float z = args.z[static_cast<std::size_t>(t) * value_elements + vh * kHead + v];
+    const float normalized = __fmul_rn(__fmul_rn(mixed, inv_o), norm_weight);
+    const __half y = f2h(__fmul_rn(normalized, gx_silu(z)));
+    args.output[static_cast<std::size_t>(t) * value_elements + vh * kHead + v] = y;
+    if (args.act_bits != 0) {
+      const std::size_t row = static_cast<std::size_t>(t) * value_elements + vh * kHead;
+      const std::size_t group = static_cast<std::size_t>(t) * args.value_heads + vh;
+      if (args.act_bits == 8) {
+        pack_group_128<8>(h2f(y), v, args.act_codes + row, args.act_scales + group, args.act_sums + group, pack_max, pack_sum);
+      } else {
+        pack_group_128<4>(h2f(y), v, args.act_codes + row, args.act_scales + group, args.act_sums + group, pack_max, pack_sum);
+      }
+    }
+    __syncthreads();  // query/key/sums are rewritten by the next token
+  }
+  float* final_state = args.final_state + static_cast<std::size_t>(vh) * kHead * kHead;
+#pragma unroll
+  for (unsigned k = 0; k < kHead; ++k) final_state[k * kHead + v] = S[k];
+}
+
+// Rollback replay (qwen_ops.hip:467-539): conv inputs and delta-rule updates of
+// the accepted prefix are re-applied to the untouched pre-block state, for all
+// GDN layers in one launch. Bit-identical to the forward's update order.
+__global__ void gdn_restore_conv_kernel(GdnRestoreArgs args) {
+  pdl_trigger();
+  pdl_wait();
+  const std::uint64_t linear = static_cast<std::uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const std::uint64_t total = static_cast<std::uint64_t>(args.layers) * args.channels;
+  if (linear >= total) return;
+  const std::uint64_t layer = linear / args.channels, channel = linear % args.channels;
+  __half* taps = args.conv_states + (layer * args.channels + channel) * 4u;
+  const __half* log = args.conv_logs + layer * args.max_logged * args.channels;
+  for (std::uint32_t t = 0; t < args.accepted; ++t) {
+    taps[0] = taps[1];
+    taps[1] = taps[2];
+    taps[2] = taps[3];
+    taps[3] = log[static_cast<std::size_t>(t) * args.channels + channel];
+  }
+}
+
+__global__ __launch_bounds__(128) void gdn_restore_state_kernel(GdnRestoreArgs args) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr unsigned kHead = 128;
+  const unsigned layer = blockIdx.x / args.value_heads, vh = blockIdx.x % args.value_heads;
+  const unsigned v = threadIdx.x;
+  const unsigned ratio = args.value_heads / args.key_heads, kh = vh / ratio;
+  const std::size_t key_elements = static_cast<std::size_t>(args.key_heads) * kHead;
+  const std::size_t value_elements = static_cast<std::size_t>(args.value_heads) * kHead;
+  float* S = args.states + (static_cast<std::size_t>(layer) * args.value_heads + vh) * kHead * kHead;
+  const float* key_log = args.key_logs + static_cast<std::size_t>(layer) * args.max_logged * key_elements;
+  const float* delta_log = args.delta_logs + static_cast<std::size_t>(layer) * args.max_logged * value_elements;
+  const float* decay_log = args.decay_logs + static_cast<std::size_t>(layer) * args.max_logged * args.value_heads;
+  float column[kHead];
+#pragma unroll
+  for (unsigned k = 0; k < kHead; ++k) column[k] = S[k * kHead + v];
+  for (std::uint32_t t = 0; t < args.accepted; ++t) {
+    const float decay = decay_log[static_cast<std::size_t>(t) * args.value_heads + vh];
+    const float delta = delta_log[static_cast<std::size_t>(t) * value_elements + vh * kHead + v];
+    const float* keys = key_log + static_cast<std::size_t>(t) * key_elements + kh * kHead;
+#pragma unroll
+    for (unsigned k = 0; k < kHead; ++k) column[k] = fmaf(keys[k], delta, __fmul_rn(column[k], decay));
+  }
+#pragma unroll
+  for (unsigned k = 0; k < kHead; ++k) S[k * kHead + v] = column[k];
+}
+
+// ---------------------------------------------------------------------------
+// Q/K RMSNorm(1+w) + NeoX RoPE (+ KV append), qwen_ops.hip:599-696. One
+// 256-thread CTA per (token, head); angles come from a host-built table.
+// ---------------------------------------------------------------------------
+
+__global__ __launch_bounds__(256) void qk_norm_rope_kernel(QkRopeArgs args) {
+  pdl_trigger();
+  pdl_wait();
+  const unsigned heads = args.q_heads + args.k_heads;
+  const unsigned token = blockIdx.x / heads, local = blockIdx.x % heads;
+  const bool is_key = local >= args.q_heads;
+  const unsigned head = is_key ? local - args.q_heads : local;
+  const unsigned d = threadIdx.x, lane = d & 31u, warp = d >> 5;
+  const std::uint64_t base = args.device_base_position != nullptr ? *args.device_base_position : args.base_position;
+  const std::uint64_t position = base + token;
+  const float* input = is_key ? args.k_input + (static_cast<std::size_t>(token) * args.k_heads + head) * args.k_stride
+                              : args.q_input + (static_cast<std::size_t>(token) * args.q_heads + head) * args.q_stride;
+  const std::uint16_t* weight = is_key ? args.k_weight : args.q_weight;
+  __shared__ float normalized[256];
+  __shared__ float warp_sums[8];
+  const float value = input[d];
+  const float square = warp_sum_down(__fmul_rn(value, value));
+  if (lane == 0) warp_sums[warp] = square;
+  __syncthreads();
+  const float inverse = inv_sqrt_rn(__fadd_rn(__fdiv_rn(tree_of_eight(warp_sums, 8), 256.0f), 1.0e-6f));
+  normalized[d] = __fmul_rn(value, __fmul_rn(inverse, __fadd_rn(1.0f, bf2f(weight[d]))));
+  __syncthreads();
+  float out = normalized[d];
+  const unsigned half = args.rotary / 2u;
+  if (d < args.rotary) {
+    const bool in_range = position < args.table_positions;
+    if (!in_range && d == 0) atomicOr(&g_ops_error, 2u);
+    const std::uint64_t p = in_range ? position : 0;
+    const unsigned f = d % half;
+    const float partner = d < half ? normalized[d + half] : normalized[d - half];
+    const float rotated = d < half ? -partner : partner;
+    out = fmaf(out, args.cos_table[p * half + f], __fmul_rn(rotated, args.sin_table[p * half + f]));
+  }
+  const __half result = f2h(out);
+  if (!is_key) {
+    args.q_output[(static_cast<std::size_t>(token) * args.q_heads + head) * 256u + d] = result;
+    return;
+  }
+  if (args.k_output != nullptr) args.k_output[(static_cast<std::size_t>(token) * args.k_heads + head) * 256u + d] = result;
+  if (args.key_cache != nullptr) {
+    if (position >= args.capacity) {
+      if (d == 0) atomicOr(&g_ops_error, 4u);
+      return;
+    }
+    const std::size_t slot = (static_cast<std::size_t>(position) * args.k_heads + head) * 256u + d;
+    args.key_cache[slot] = result;
+    args.value_cache[slot] = f2h(args.v_input[(static_cast<std::size_t>(token) * args.k_heads + head) * 256u + d]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Gated attention decode (qwen_ops.hip:698-766) as chunked online softmax:
+// pass 1 handles one 128-position chunk per (token, kv head) CTA with one warp
+// per query head; pass 2 merges chunks in ascending order and applies the
+// sigmoid gate. Scores: lane l owns dims 8l..8l+7 (fma chain) + xor tree,
+// times 1/16. Within a chunk the running maximum is an exact prefix max, so
+// the per-position rescale factors equal the reference's serial update.
+// ---------------------------------------------------------------------------
+
+constexpr unsigned kChunk = kAttentionChunk;
+
+__global__ __launch_bounds__(256) void attention_chunk_kernel(AttentionArgs args) {
+  pdl_trigger();
+  pdl_wait();
+  const unsigned group = args.q_heads / args.kv_heads;
+  const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const unsigned chunk = blockIdx.x, kvh = blockIdx.y, token = blockIdx.z;
+  const std::uint64_t base = args.device_base_position != nullptr ? *args.device_base_position + 1u
+                                                                  : args.base_token_count;
+  const std::uint64_t count = base + token;  // positions 0 .. count-1 are visible
+  const std::uint32_t chunks = static_cast<std::uint32_t>((count + kChunk - 1) / kChunk);
+  __shared__ float scores[8][kChunk];
+  __shared__ float alphas[8][kChunk];
+  __shared__ float betas[8][kChunk];
+  if (warp >= group) return;
+  const unsigned h = kvh * group + warp;
+  float* partial =
+      args.partials + ((static_cast<std::size_t>(token) * args.q_heads + h) * args.max_chunks + chunk) * 258u;
+  if (chunk >= chunks) return;
+  const std::uint64_t begin = static_cast<std::uint64_t>(chunk) * kChunk;
+  const std::uint64_t remaining = count - begin;
+  const std::uint32_t n = remaining < kChunk ? static_cast<std::uint32_t>(remaining) : kChunk;
+  if (count > args.capacity) {
+    if (lane == 0) atomicOr(&g_ops_error, 8u);
+    return;
+  }
+  const __half* q = args.query + (static_cast<std::size_t>(token) * args.q_heads + h) * 256u + 8u * lane;
+  float qf[8];
+  {
+    const uint4 raw = *reinterpret_cast<const uint4*>(q);
+    const __half* hv = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qf[j] = h2f(hv[j]);
+  }
+  const std::size_t row_stride = static_cast<std::size_t>(args.kv_heads) * 256u;
+  const __half* keys = args.key_cache + (begin * args.kv_heads + kvh) * 256u + 8u * lane;
+  for (std::uint32_t p = 0; p < n; ++p) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(keys + p * row_stride);
+    const __half* hv = reinterpret_cast<const __half*>(&raw);
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s = fmaf(qf[j], h2f(hv[j]), s);
+    s = warp_sum_xor(s);
+    if (lane == 0) scores[warp][p] = __fmul_rn(s, 0.0625f);
+  }
+  __syncwarp();
+  // prefix maximum: lane owns positions 4l..4l+3
+  float local_max[4];
+  float running = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const std::uint32_t p = 4u * lane + j;
+    if (p < n) running = fmaxf(running, scores[warp][p]);
+    local_max[j] = running;
+  }
+  float exclusive = __shfl_up_sync(0xffffffffu, running, 1);
+  if (lane == 0) exclusive = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (unsigned offset = 1; offset < 32; offset <<= 1) {
+    const float other = __shfl_up_sync(0xffffffffu, exclusive, offset);
+    if (lane >= offset) exclusive = fmaxf(exclusive, other);
+  }
+  float previous = exclusive;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const std::uint32_t p = 4u * lane + j;
+    const float m = fmaxf(exclusive, local_max[j]);
+    if (p < n) {
+      alphas[warp][p] = gx_expf(__fsub_rn(previous, m));
+      betas[warp][p] = gx_expf(__fsub_rn(scores[warp][p], m));
+    }
+    previous = m;
+  }
+  const float chunk_max = __shfl_sync(0xffffffffu, previous, 31);
+  __syncwarp();
+  float den = 0.0f;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const __half* values = args.value_cache + (begin * args.kv_heads + kvh) * 256u + 8u * lane;
+  for (std::uint32_t p = 0; p < n; ++p) {
+    const float alpha = alphas[warp][p], beta = betas[warp][p];
+    const uint4 raw = *reinterpret_cast<const uint4*>(values + p * row_stride);
+    const __half* hv = reinterpret_cast<const __half*>(&raw);
+    den = __fadd_rn(__fmul_rn(den, alpha), beta);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(__fmul_rn(acc[j], alpha), __fmul_rn(h2f(hv[j]), beta));
+  }
+  if (lane == 0) {
+    partial[0] = chunk_max;
+    partial[1] = den;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) partial[2 + 8 * lane + j] = acc[j];
+}
+
+__global__ __launch_bounds__(256) void attention_merge_kernel(AttentionArgs args) {
+  pdl_trigger();
+  pdl_wait();
+  const unsigned h = blockIdx.x, token = blockIdx.y, d = threadIdx.x;
+  const std::uint64_t base = args.device_base_position != nullptr ? *args.device_base_position + 1u
+                                                                  : args.base_token_count;
+  const std::uint64_t count = base + token;
+  if (count > args.capacity) return;
+  const std::uint32_t chunks = static_cast<std::uint32_t>((count + kChunk - 1) / kChunk);
+  const float* partial = args.partials + (static_cast<std::size_t>(token) * args.q_heads + h) * args.max_chunks * 258u;
+  float M = partial[0], Den = partial[1], Acc = partial[2 + d];
+  for (std::uint32_t c = 1; c < chunks; ++c) {
+    const float* p = partial + static_cast<std::size_t>(c) * 258u;
+    const float m = p[0];
+    const float next = fmaxf(M, m);
+    const float a1 = gx_expf(__fsub_rn(M, next));
+    const float a2 = gx_expf(__fsub_rn(m, next));
+    Den = __fadd_rn(__fmul_rn(Den, a1), __fmul_rn(p[1], a2));
+    Acc = __fadd_rn(__fmul_rn(Acc, a1), __fmul_rn(p[2 + d], a2));
+    M = next;
+  }
+  const float gate = args.gate[(static_cast<std::size_t>(token) * args.q_heads + h) * 512u + 256u + d];
+  const __half y = f2h(__fmul_rn(__fdiv_rn(Acc, Den), gx_sigmoid(gate)));
+  args.output[(static_cast<std::size_t>(token) * args.q_heads + h) * 256u + d] = y;
+  if (args.act_bits != 0) {
+    __shared__ float pack_max[2][4];
+    __shared__ int pack_sum[2][4];
+    const unsigned half = d >> 7, element = d & 127u;
+    const std::size_t row = (static_cast<std::size_t>(token) * args.q_heads + h) * 256u + half * 128u;
+    const std::size_t group = static_cast<std::size_t>(token) * args.q_heads * 2u + h * 2u + half;
+    if (args.act_bits == 8) {
+      pack_group_128<8>(h2f(y), element, args.act_codes + row, args.act_scales + group, args.act_sums + group,
+                        pack_max[half], pack_sum[half]);
+    } else {
+      pack_group_128<4>(h2f(y), element, args.act_codes + row, args.act_scales + group, args.act_sums + group,
+                        pack_max[half], pack_sum[half]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// argmax with the lowest index on ties (qwen_ops.hip:768-807): per-block
+// partial maxima, then one reduction per token (and an optional id map).
+// ---------------------------------------------------------------------------
+
+constexpr unsigned kArgmaxBlocks = 64;
+
+__device__ __forceinline__ void better(float& best, std::uint32_t& index, float value, std::uint32_t other) {
+  if (value > best || (value == best && other < index)) {
+    best = value;
+    index = other;
+  }
+}
+
+__global__ __launch_bounds__(256) void argmax_partial_kernel(ArgmaxArgs args) {
+  pdl_trigger();
+  pdl_wait();
+  const unsigned token = blockIdx.y;
+  const float* logits = args.logits + static_cast<std::size_t>(token) * args.row_stride;
+  float best = -__int_as_float(0x7f800000);
+  std::uint32_t index = 0xffffffffu;
+  for (std::uint32_t i = blockIdx.x * 256u + threadIdx.x; i < args.vocab; i += kArgmaxBlocks * 256u) {
+    better(best, index, logits[i], i);
+  }
+#pragma unroll
+  for (unsigned offset = 16; offset != 0; offset >>= 1) {
+    const float other_value = __shfl_xor_sync(0xffffffffu, best, offset);
+    const std::uint32_t other_index = __shfl_xor_sync(0xffffffffu, index, offset);
+    better(best, index, other_value, other_index);
+  }
+  __shared__ float values[8];
+  __shared__ std::uint32_t indices[8];
+  if ((threadIdx.x & 31u) == 0) {
+    values[threadIdx.x >> 5] = best;
+    indices[threadIdx.x >> 5] = index;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; ++w) better(best, index, values[w], indices[w]);
+    args.partial_values[token * kArgmaxBlocks + blockIdx.x] = best;
+    args.partial_indices[token * kArgmaxBlocks + blockIdx.x] = index;
+  }
+}
+
+__global__ void argmax_final_kernel(ArgmaxArgs args) {
+  pdl_trigger();
+  pdl_wait();
+  const unsigned token = blockIdx.x, lane = threadIdx.x;
+  float best = -__int_as_float(0x7f800000);
+  std::uint32_t index = 0xffffffffu;
+  for (unsigned b = lane; b < kArgmaxBlocks; b += 32) {
+    better(best, index, args.partial_values[token * kArgmaxBlocks + b], args.partial_indices[token * kArgmaxBlocks + b]);
+  }
+#pragma unroll
+  for (unsigned offset = 16; offset != 0; offset >>= 1) {
+    const float other_value = __shfl_xor_sync(0xffffffffu, best, offset);
+    const std::uint32_t other_index = __shfl_xor_sync(0xffffffffu, index, offset);
+    better(best, index, other_value, other_index);
+  }
+  if (lane == 0) {
+    if (index >= args.vocab) index = 0;  // all NaN: the reference also returns 0
+    args.tokens[token] = args.token_ids != nullptr ? args.token_ids[index] : index;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// small elementwise helpers (qwen_ops.hip:809-828)
+// ---------------------------------------------------------------------------
+
+__global__ void float_to_half_kernel(const float* __restrict__ input, __half* __restrict__ output, std::size_t n) {
+  pdl_trigger();
+  pdl_wait();
+  const std::size_t i = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) output[i] = f2h(input[i]);
+}
+
+}  // namespace
+
+// ===========================================================================
+// launchers (C++ API used by the runtime; the C ABI wraps them)
+// ===========================================================================
+
+int launch_norm_pack(const NormPackArgs& args, int act_bits, unsigned batch, cudaStream_t stream) {
+  if (args.weight == nullptr || batch == 0 || args.elements == 0 || args.elements % kNormThreads != 0 ||
+      args.elements / kNormThreads > kNormMaxIter || !(args.epsilon > 0.0f)) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid RMSNorm arguments (H must be a multiple of 256, at most 16384)");
+  }
+  if (args.embedding_codes == nullptr && args.residual == nullptr) {
+    return fail(GFXB_INVALID_ARGUMENT, "RMSNorm needs an input");
+  }
+  if (act_bits != 0 && (args.act_codes == nullptr || args.act_scales == nullptr || args.act_sums == nullptr)) {
+    return fail(GFXB_INVALID_ARGUMENT, "activation pack outputs are required");
+  }
+  if (act_bits != 0 && act_bits != 4 && act_bits != 8) {
+    return fail(GFXB_INVALID_ARGUMENT, "activation bits must be 0, 4 or 8");
+  }
+  const unsigned iterations = args.elements / kNormThreads;
+  bool launched = false;
+  auto try_launch = [&](auto iter_tag) {
+    constexpr unsigned kIter = decltype(iter_tag)::value;
+    if (iterations != kIter) return;
+    launched = true;
+    if (act_bits == 0) launch_kernel(residual_norm_pack_kernel<0, kIter>, dim3(batch), dim3(kNormThreads), 0, stream, 0, args);
+    else if (act_bits == 4) launch_kernel(residual_norm_pack_kernel<4, kIter>, dim3(batch), dim3(kNormThreads), 0, stream, 0, args);
+    else launch_kernel(residual_norm_pack_kernel<8, kIter>, dim3(batch), dim3(kNormThreads), 0, stream, 0, args);
+  };
+  try_launch(std::integral_constant<unsigned, 1>{});
+  try_launch(std::integral_constant<unsigned, 2>{});
+  try_launch(std::integral_constant<unsigned, 4>{});
+  try_launch(std::integral_constant<unsigned, 8>{});
+  try_launch(std::integral_constant<unsigned, 16>{});
+  try_launch(std::integral_constant<unsigned, 20>{});
+  try_launch(std::integral_constant<unsigned, 40>{});
+  if (!launched) return fail(GFXB_UNSUPPORTED, "RMSNorm width must be 256 x {1,2,4,8,16,20,40}");
+  return launch_status("RMSNorm launch failed");
+}
+
+int launch_silu_pack(const SiluPackArgs& args, int act_bits, cudaStream_t stream) {
+  if (args.gate == nullptr || args.up == nullptr || args.elements == 0 || args.elements % kGroup != 0 ||
+      args.batch == 0 || args.batch > 32) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid SiLU/pack arguments");
+  }
+  if (args.act_codes != nullptr && (args.act_scales == nullptr || args.act_sums == nullptr)) {
+    return fail(GFXB_INVALID_ARGUMENT, "activation pack outputs are required");
+  }
+  const std::uint32_t groups = args.elements / kGroup * args.batch;
+  const unsigned grid = (groups + 7u) / 8u;
+  if (act_bits == 8) {
+    launch_kernel(silu_pack_kernel<8>, dim3(grid), dim3(256), 0, stream, 0, args);
+  } else {
+    launch_kernel(silu_pack_kernel<4>, dim3(grid), dim3(256), 0, stream, 0, args);
+  }
+  return launch_status("SiLU/pack launch failed");
+}
+
+int launch_gdn_conv(const GdnConvArgs& args, cudaStream_t stream) {
+  if (args.projected == nullptr || args.weight == nullptr || args.initial_state == nullptr ||
+      args.final_state == nullptr || args.output == nullptr || args.channels == 0 || args.batch == 0) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid GDN convolution arguments");
+  }
+  launch_kernel(gdn_conv_kernel, dim3((args.channels + 255u) / 256u), dim3(256), 0, stream, 0, args);
+  return launch_status("GDN convolution launch failed");
+}
+
+int launch_gdn_recurrent(const GdnRecurrentArgs& args, cudaStream_t stream) {
+  if (args.qkv == nullptr || args.z == nullptr || args.a == nullptr || args.b == nullptr || args.a_log == nullptr ||
+      args.dt_bias == nullptr || args.norm_weight == nullptr || args.initial_state == nullptr ||
+      args.final_state == nullptr || args.output == nullptr || args.batch == 0 || args.key_heads == 0 ||
+      args.value_heads == 0 || args.value_heads % args.key_heads != 0) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid GDN recurrent arguments");
+  }
+  launch_kernel(gdn_recurrent_kernel, dim3(args.value_heads), dim3(128), 0, stream, 0, args);
+  return launch_status("GDN recurrent launch failed");
+}
+
+int launch_gdn_restore(const GdnRestoreArgs& args, cudaStream_t stream) {
+  if (args.conv_states == nullptr || args.states == nullptr || args.conv_logs == nullptr || args.key_logs == nullptr ||
+      args.delta_logs == nullptr || args.decay_logs == nullptr || args.channels == 0 || args.layers == 0 ||
+      args.max_logged == 0 || args.accepted == 0 || args.accepted > args.max_logged || args.key_heads == 0 ||
+      args.value_heads % args.key_heads != 0) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid GDN prefix restore arguments");
+  }
+  const std::uint64_t total = static_cast<std::uint64_t>(args.layers) * args.channels;
+  launch_kernel(gdn_restore_conv_kernel, dim3(static_cast<unsigned>((total + 255u) / 256u)), dim3(256), 0, stream, 0,
+                args);
+  int status = launch_status("GDN convolution restore launch failed");
+  if (status != GFXB_OK) return status;
+  launch_kernel(gdn_restore_state_kernel, dim3(args.layers * args.value_heads), dim3(128), 0, stream, 0, args);
+  return launch_status("GDN recurrent restore launch failed");
+}
+
+int launch_qk_rope(const QkRopeArgs& args, unsigned batch, cudaStream_t stream) {
+  if (args.q_input == nullptr || args.q_weight == nullptr || args.q_output == nullptr || args.k_input == nullptr ||
+      args.k_weight == nullptr || args.q_heads == 0 || args.k_heads == 0 || batch == 0 || args.rotary == 0 ||
+      args.rotary > 256 || (args.rotary & 1u) != 0 || args.cos_table == nullptr || args.sin_table == nullptr ||
+      args.q_stride < 256 || args.k_stride < 256) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid Q/K RMSNorm/RoPE arguments");
+  }
+  if (args.key_cache != nullptr && (args.value_cache == nullptr || args.v_input == nullptr)) {
+    return fail(GFXB_INVALID_ARGUMENT, "KV append needs value input and cache");
+  }
+  if (args.device_base_position == nullptr && args.key_cache != nullptr &&
+      args.base_position + batch > args.capacity) {
+    return fail(GFXB_INVALID_ARGUMENT, "KV append exceeds the cache capacity");
+  }
+  launch_kernel(qk_norm_rope_kernel, dim3((args.q_heads + args.k_heads) * batch), dim3(256), 0, stream, 0, args);
+  return launch_status("Q/K RMSNorm/RoPE launch failed");
+}
+
+std::size_t attention_partial_bytes(unsigned q_heads, std::size_t capacity, unsigned batch) {
+  const std::size_t chunks = (capacity + kChunk - 1) / kChunk;
+  return static_cast<std::size_t>(batch) * q_heads * chunks * 258u * sizeof(float);
+}
+
+int launch_attention(const AttentionArgs& args, unsigned batch, cudaStream_t stream) {
+  if (args.query == nullptr || args.gate == nullptr || args.key_cache == nullptr || args.value_cache == nullptr ||
+      args.output == nullptr || args.partials == nullptr || batch == 0 || batch > 32 || args.kv_heads == 0 ||
+      args.q_heads % args.kv_heads != 0 || args.q_heads / args.kv_heads > 8) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid gated attention arguments");
+  }
+  if (args.max_chunks < (args.capacity + kChunk - 1) / kChunk) {
+    return fail(GFXB_INVALID_ARGUMENT, "attention partial buffer is too small for the capacity");
+  }
+  if (args.device_base_position == nullptr &&
+      (args.base_token_count == 0 || args.base_token_count + batch - 1 > args.capacity)) {
+    return fail(GFXB_INVALID_ARGUMENT, "attention token count exceeds the cache capacity");
+  }
+  const std::uint32_t max_chunks = args.device_base_position != nullptr
+                                       ? args.max_chunks
+                                       : static_cast<std::uint32_t>((args.base_token_count + batch - 1 + kChunk - 1) / kChunk);
+  launch_kernel(attention_chunk_kernel, dim3(dim3(max_chunks, args.kv_heads, batch)), dim3(256), 0, stream, 0, args);
+  int status = launch_status("attention chunk launch failed");
+  if (status != GFXB_OK) return status;
+  launch_kernel(attention_merge_kernel, dim3(dim3(args.q_heads, batch)), dim3(256), 0, stream, 0, args);
+  return launch_status("attention merge launch failed");
+}
+
+std::size_t argmax_scratch_bytes(unsigned batch) {
+  return static_cast<std::size_t>(batch) * kArgmaxBlocks * (sizeof(float) + sizeof(std::uint32_t));
+}
+
+int launch_argmax(const ArgmaxArgs& args, unsigned batch, cudaStream_t stream) {
+  if (args.logits == nullptr || args.tokens == nullptr || args.partial_values == nullptr ||
+      args.partial_indices == nullptr || args.vocab == 0 || args.row_stride < args.vocab || batch == 0 ||
+      batch > 32) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid argmax arguments");
+  }
+  launch_kernel(argmax_partial_kernel, dim3(dim3(kArgmaxBlocks, batch)), dim3(256), 0, stream, 0, args);
+  int status = launch_status("argmax launch failed");
+  if (status != GFXB_OK) return status;
+  launch_kernel(argmax_final_kernel, dim3(batch), dim3(32), 0, stream, 0, args);
+  return launch_status("argmax launch failed");
+}
+
+int launch_float_to_half(const float* input, __half* output, std::size_t n, cudaStream_t stream) {
+  if (input == nullptr || output == nullptr || n == 0) return fail(GFXB_INVALID_ARGUMENT, "invalid float-to-half arguments");
+  launch_kernel(float_to_half_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, stream, 0, input,
+                output, n);
+  return launch_status("float-to-half launch failed");
+}
+
+int read_ops_error(std::uint32_t* value, bool clear) {
+  cudaError_t error = cudaMemcpyFromSymbol(value, g_ops_error, sizeof(std::uint32_t));
+  if (error == cudaSuccess && clear) {
+    const std::uint32_t zero = 0;
+    error = cudaMemcpyToSymbol(g_ops_error, &zero, sizeof zero);
+  }
+  if (error != cudaSuccess) {
+    set_error_cuda(error, "device error word access failed");
+    return GFXB_CUDA_ERROR;
+  }
+  return GFXB_OK;
+}
+
+}  // namespace gfxb

@@ -1,5 +1,6 @@
 // Error plumbing for the C ABI: gfxb_status codes plus a per-thread message,
 // the C counterpart of the reference's Status (include/gfxinfer/status.h).
+#include <cstdlib>
 #include <string>
 
 #include "common.cuh"
@@ -19,6 +20,14 @@ void set_error_cuda(cudaError_t error, const char* context) {
 int fail(int status, const char* message) {
   set_error(message);
   return status;
+}
+
+bool pdl_enabled() {
+  static const bool enabled = [] {
+    const char* value = std::getenv("GFXB_PDL");
+    return value == nullptr || value[0] != '0';
+  }();
+  return enabled;
 }
 
 int launch_status(const char* context) {

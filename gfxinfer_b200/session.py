@@ -1,0 +1,185 @@
+"""Engine and decode-session handles over the C ABI.
+
+Mirrors the reference's public runtime API (include/gfxinfer/engine.h:77-97,
+include/gfxinfer/qwen_runtime.h:47-77): Engine.create, QwenDecodeSession.create,
+greedy_step, block_step, mtp_draft, speculative_step, position. Failures raise
+GfxbError carrying the reference's ErrorCode value.
+"""
+from __future__ import annotations
+
+import atexit
+import ctypes
+import weakref
+from dataclasses import dataclass, field
+
+from . import abi, check, lib
+
+CONFIG2 = dict(hidden=5120, intermediate=17408, layers=64, attention_interval=4, gdn_key_heads=16,
+               gdn_value_heads=48, q_heads=24, kv_heads=4, vocab=151936, draft_vocab=98304, mlp_bits=3,
+               proj_bits=4, head_bits=4, emb_bits=4, activation_bits=4, max_context=512, seed=0x5EED)
+"""BASELINE config 2: 64-layer hybrid decoder, W3 MLP, W4 projections/head, A4, context 512."""
+
+
+def model_config(**overrides) -> abi.ModelConfig:
+    values = dict(CONFIG2)
+    values.update(overrides)
+    return abi.ModelConfig(**values)
+
+
+def nccl_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(128)
+    check(lib().gfxb_nccl_unique_id(buf))
+    return buf.raw
+
+
+class Engine:
+    """Resident weights of one model (or one tensor-parallel shard) on one GPU."""
+
+    def __init__(self, handle: int, config: abi.ModelConfig) -> None:
+        self._handle = ctypes.c_void_p(handle)
+        self.config = config
+        self._sessions: weakref.WeakSet = weakref.WeakSet()
+        _LIVE.add(self)
+
+    @classmethod
+    def create(cls, config: abi.ModelConfig | None = None, device: int = 0, tp_rank: int = 0, tp_size: int = 1,
+               nccl_id: bytes | None = None, include_mtp: bool = True) -> "Engine":
+        config = config or model_config()
+        handle = ctypes.c_void_p()
+        check(lib().gfxb_engine_create_synthetic(ctypes.byref(config), device, tp_rank, tp_size, nccl_id,
+                                                 int(include_mtp), ctypes.byref(handle)))
+        return cls(handle.value, config)
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._handle
+
+    def weight_bytes(self) -> int:
+        out = ctypes.c_uint64()
+        check(lib().gfxb_engine_weight_bytes(self._handle, ctypes.byref(out)))
+        return out.value
+
+    def close(self) -> None:
+        """Destroys the engine; sessions created from it are closed first."""
+        for session in list(self._sessions):
+            session.close()
+        if self._handle:
+            lib().gfxb_engine_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+@dataclass
+class SpeculativeStepResult:
+    tokens: list[int] = field(default_factory=list)
+    proposed_drafts: int = 0
+    accepted_drafts: int = 0
+
+
+class QwenDecodeSession:
+    """Batch-1 decode session (qwen_runtime.h:47-77)."""
+
+    def __init__(self, handle: int, engine: Engine) -> None:
+        self._handle = ctypes.c_void_p(handle)
+        self.engine = engine
+        engine._sessions.add(self)
+
+    @classmethod
+    def create(cls, engine: Engine, maximum_context_tokens: int | None = None, graph_verifier_batch: int = 0,
+               use_graphs: bool = True) -> "QwenDecodeSession":
+        ctx = maximum_context_tokens or engine.config.max_context
+        config = abi.SessionConfig(ctx, graph_verifier_batch, int(use_graphs))
+        handle = ctypes.c_void_p()
+        check(lib().gfxb_session_create(engine.handle, ctypes.byref(config), ctypes.byref(handle)))
+        return cls(handle.value, engine)
+
+    def greedy_step(self, token: int) -> int:
+        out = ctypes.c_uint32()
+        check(lib().gfxb_session_greedy_step(self._handle, token, ctypes.byref(out)))
+        return out.value
+
+    def block_step(self, tokens: list[int]) -> list[int]:
+        n = len(tokens)
+        arr = (ctypes.c_uint32 * max(n, 1))(*tokens)
+        out = (ctypes.c_uint32 * max(n, 1))()
+        check(lib().gfxb_session_block_step(self._handle, arr, n, out))
+        return list(out)[:n]
+
+    def mtp_draft(self, next_token: int) -> int:
+        out = ctypes.c_uint32()
+        check(lib().gfxb_session_mtp_draft(self._handle, next_token, ctypes.byref(out)))
+        return out.value
+
+    def speculative_step(self, seed_token: int, draft_count: int) -> SpeculativeStepResult:
+        out = (ctypes.c_uint32 * 32)()
+        count = ctypes.c_uint()
+        accepted = ctypes.c_uint()
+        check(lib().gfxb_session_speculative_step(self._handle, seed_token, draft_count, out, ctypes.byref(count),
+                                                  ctypes.byref(accepted)))
+        return SpeculativeStepResult(list(out)[:count.value], draft_count, accepted.value)
+
+    def position(self) -> int:
+        out = ctypes.c_uint64()
+        check(lib().gfxb_session_position(self._handle, ctypes.byref(out)))
+        return out.value
+
+    def enqueue_greedy(self, first_token: int, steps: int) -> None:
+        check(lib().gfxb_session_enqueue_greedy(self._handle, first_token, steps))
+
+    def sync(self) -> None:
+        check(lib().gfxb_session_sync(self._handle))
+
+    def last_token(self) -> int:
+        out = ctypes.c_uint32()
+        check(lib().gfxb_session_last_token(self._handle, ctypes.byref(out)))
+        return out.value
+
+    def stream(self) -> int:
+        return lib().gfxb_session_stream(self._handle) or 0
+
+    def enqueue_gemv(self, kind: int, launches: int) -> int:
+        """Enqueue standalone GEMV launches (0 MLP gate+up, 1 MLP down, 2 GDN in); returns bytes per launch."""
+        out = ctypes.c_uint64()
+        check(lib().gfxb_session_enqueue_gemv(self._handle, kind, launches, ctypes.byref(out)))
+        return out.value
+
+    def read_state(self, logits_count: int = 0):
+        import numpy as np
+
+        hidden = np.zeros(self.engine.config.hidden, np.uint16)
+        logits = np.zeros(max(logits_count, 1), np.float32)
+        check(lib().gfxb_session_read_state(self._handle, hidden.ctypes.data,
+                                            logits.ctypes.data if logits_count else None, logits_count))
+        return hidden, logits[:logits_count]
+
+    def close(self) -> None:
+        if self._handle:
+            lib().gfxb_session_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_LIVE: weakref.WeakSet = weakref.WeakSet()
+
+
+@atexit.register
+def _close_all() -> None:
+    # Release device objects before the CUDA runtime is torn down at exit.
+    for engine in list(_LIVE):
+        engine.close()
+
+
+def read_device_errors() -> int:
+    flags = ctypes.c_uint32()
+    check(lib().gfxb_read_device_errors(ctypes.byref(flags)))
+    return flags.value

@@ -121,6 +121,131 @@ int gfxb_gfx12_i8_gemm(int format, const uint8_t* tiled_weights,
                        const uint16_t* activation_scales, float* output, size_t rows,
                        size_t columns, unsigned batch, void* stream);
 
+/* ---- decode-path operators (qwen_ops.h) -------------------------------------
+ * Fused forms of the reference launchers; each optional output may be NULL. */
+
+/* residual add + RMSNorm (+ activation pack). Replaces launch_rms_norm(_batch),
+ * launch_residual_add_rms_norm_batch and the A4/A8 quantizer that follows
+ * them (qwen_ops.h, lowbit_gemv.h:79-95). update == NULL: plain RMSNorm of
+ * `input`. act_bits 0 (no pack), 4 or 8. */
+int gfxb_residual_rms_norm_pack(const uint16_t* input, const float* update, uint16_t* residual_out,
+                                const uint16_t* bf16_weight, uint16_t* normalized_out, size_t elements,
+                                unsigned batch, float epsilon, int add_unit_offset, int act_bits,
+                                int8_t* act_codes, uint16_t* act_scales, int32_t* act_sums,
+                                uint8_t* packed_a4, void* stream);
+/* fp16(silu(gate) * up) (+ pack). Replaces launch_silu_multiply and
+ * launch_silu_multiply_quantize_i4. */
+int gfxb_silu_multiply_pack(const float* gate, const float* up, size_t elements_per_row, unsigned batch,
+                            uint16_t* product_out, int act_bits, int8_t* act_codes, uint16_t* act_scales,
+                            int32_t* act_sums, uint8_t* packed_a4, void* stream);
+/* Replaces launch_gdn_conv_update(_block) (qwen_ops.h). */
+int gfxb_gdn_conv_update(const float* projected, const uint16_t* bf16_weight, const uint16_t* initial_state,
+                         uint16_t* final_state, uint16_t* output, uint16_t* appended_log, size_t channels,
+                         unsigned batch, void* stream);
+/* Replaces launch_gdn_recurrent_decode(_block). States [Hv][128][128] fp32. */
+int gfxb_gdn_recurrent(const uint16_t* qkv, const float* z, const float* a, const float* b,
+                       const uint16_t* a_log, const uint16_t* dt_bias, const uint16_t* norm_weight,
+                       const float* initial_state, float* final_state, uint16_t* output, float* key_log,
+                       float* delta_log, float* decay_log, unsigned key_heads, unsigned value_heads,
+                       unsigned batch, void* stream);
+/* Replaces launch_gdn_restore_prefix_all. */
+int gfxb_gdn_restore_prefix_all(uint16_t* conv_states, float* recurrent_states, const uint16_t* conv_logs,
+                                const float* key_logs, const float* delta_logs, const float* decay_logs,
+                                size_t channels, unsigned key_heads, unsigned value_heads, unsigned layers,
+                                unsigned maximum_logged_tokens, unsigned accepted_tokens, void* stream);
+/* Host helper: RoPE cos/sin table [positions][rotary/2] (theta^(-2f/rotary)). */
+int gfxb_rope_table(size_t positions, unsigned rotary, float theta, float* cos_table, float* sin_table);
+/* Replaces launch_qk_rms_norm_rope_block(_indirect_position) and, when
+ * key_cache != NULL, launch_kv_append_block(_indirect_position). */
+int gfxb_qk_rms_norm_rope(const float* q_input, const uint16_t* q_weight, uint16_t* q_output,
+                          unsigned q_heads, size_t q_stride, const float* k_input, const uint16_t* k_weight,
+                          uint16_t* k_output, unsigned k_heads, size_t k_stride, unsigned rotary,
+                          const float* cos_table, const float* sin_table, size_t table_positions,
+                          uint64_t base_position, const uint64_t* device_base_position, unsigned batch,
+                          const float* v_input, uint16_t* key_cache, uint16_t* value_cache, size_t capacity,
+                          void* stream);
+/* Scratch (bytes) needed by gfxb_gated_attention for `batch` tokens. */
+size_t gfxb_gated_attention_scratch_bytes(unsigned q_heads, size_t capacity, unsigned batch);
+/* Replaces launch_gated_attention_decode(_block)(_indirect_position). */
+int gfxb_gated_attention(const uint16_t* query, const float* gate_projection, const uint16_t* key_cache,
+                         const uint16_t* value_cache, uint16_t* output, size_t base_token_count,
+                         const uint64_t* device_base_position, size_t capacity, unsigned q_heads,
+                         unsigned kv_heads, unsigned batch, void* scratch, size_t scratch_bytes, void* stream);
+size_t gfxb_argmax_scratch_bytes(unsigned batch);
+/* Replaces launch_argmax(_batch)(_mapped). */
+int gfxb_argmax(const float* logits, const uint32_t* token_ids, uint32_t* tokens, size_t vocabulary_size,
+                size_t row_stride, unsigned batch, void* scratch, size_t scratch_bytes, void* stream);
+/* Reads (and clears) the device-side error flags set by bounded waits and
+ * range checks (1: wait timeout, 2: RoPE position beyond table, 4: KV append
+ * beyond capacity, 8: attention beyond capacity). Synchronous. */
+int gfxb_read_device_errors(uint32_t* flags);
+
+/* ---- engine and decode session (engine.h, qwen_runtime.h) ------------------- */
+
+/* Model shape and synthetic-weight recipe. Field order is shared with the CPU
+ * oracle's or_model_config. */
+typedef struct {
+  uint32_t hidden, intermediate, layers, attention_interval;
+  uint32_t gdn_key_heads, gdn_value_heads, q_heads, kv_heads;
+  uint32_t vocab, draft_vocab;
+  uint32_t mlp_bits, proj_bits, head_bits, emb_bits;
+  uint32_t activation_bits; /* 4 (A4) or 8 (A8) */
+  uint32_t max_context;
+  uint64_t seed;
+} gfxb_model_config;
+
+typedef struct gfxb_engine gfxb_engine;
+typedef struct gfxb_session gfxb_session;
+
+/* NCCL unique id for tensor parallelism (128 bytes), created on rank 0 and
+ * shared with the other ranks by the caller. */
+int gfxb_nccl_unique_id(void* id128);
+
+/* Engine::create for a seeded random-init model (replaces engine.cpp:62-216 for
+ * synthetic weights). tp_size 1 needs no NCCL id. Weights are generated on the
+ * device, shard by shard, into one arena. */
+int gfxb_engine_create_synthetic(const gfxb_model_config* config, int device, int tp_rank, int tp_size,
+                                 const void* nccl_id128, int include_mtp, gfxb_engine** engine);
+int gfxb_engine_destroy(gfxb_engine* engine);
+int gfxb_engine_weight_bytes(const gfxb_engine* engine, uint64_t* bytes);
+
+typedef struct {
+  uint32_t maximum_context_tokens;
+  uint32_t graph_verifier_batch; /* 0: no speculative graph; else drafts + 1 */
+  uint32_t use_graphs;           /* capture the greedy step in a CUDA graph */
+} gfxb_session_config;
+
+int gfxb_session_create(gfxb_engine* engine, const gfxb_session_config* config, gfxb_session** session);
+int gfxb_session_destroy(gfxb_session* session);
+/* QwenDecodeSession::greedy_step (qwen_runtime.cpp:1264-1318). */
+int gfxb_session_greedy_step(gfxb_session* session, uint32_t input_token, uint32_t* output_token);
+/* QwenDecodeSession::block_step (qwen_runtime.cpp:1320-1392), 1..32 tokens. */
+int gfxb_session_block_step(gfxb_session* session, const uint32_t* input_tokens, unsigned count,
+                            uint32_t* output_tokens);
+/* QwenDecodeSession::mtp_draft (qwen_runtime.cpp:1394-1419). */
+int gfxb_session_mtp_draft(gfxb_session* session, uint32_t next_token, uint32_t* draft_token);
+/* QwenDecodeSession::speculative_step (qwen_runtime.cpp:1421-1544): tokens
+ * receives accepted drafts + the correction (at most draft_count + 1). */
+int gfxb_session_speculative_step(gfxb_session* session, uint32_t seed_token, unsigned draft_count,
+                                  uint32_t* tokens, unsigned* token_count, unsigned* accepted_drafts);
+int gfxb_session_position(const gfxb_session* session, uint64_t* position);
+/* Device-resident decode: enqueue `steps` greedy steps on the session stream,
+ * each step's argmax feeding the next, no host synchronisation. The host
+ * position is advanced; call gfxb_session_sync before reading results. */
+int gfxb_session_enqueue_greedy(gfxb_session* session, uint32_t first_token, unsigned steps);
+int gfxb_session_sync(gfxb_session* session);
+int gfxb_session_last_token(gfxb_session* session, uint32_t* token);
+void* gfxb_session_stream(gfxb_session* session);
+/* Enqueues `launches` GEMV launches of one projection kind (0: MLP gate+up
+ * fused, 1: MLP down, 2: GDN qkv/z/a/b fused), cycling over the layers so
+ * each launch reads its weights from HBM; `bytes` receives the algorithmic
+ * bytes of one launch (codes, fp16 scales, A4 activation, fp32 outputs).
+ * Used to time the dominant kernel in isolation. */
+int gfxb_session_enqueue_gemv(gfxb_session* session, int kind, unsigned launches, uint64_t* bytes);
+/* Copies the last token's final hidden state (fp16 [hidden]) and logits of the
+ * local vocabulary shard (fp32) to host memory, for parity checks. */
+int gfxb_session_read_state(gfxb_session* session, uint16_t* hidden, float* logits, size_t logits_count);
+
 #ifdef __cplusplus
 }
 #endif

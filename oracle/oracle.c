@@ -844,8 +844,8 @@ static int format_of_bits(uint32_t bits) {
 static void scale_range(int format, float* lo, float* hi) {
   switch (format) {
     case OR_W2: *lo = 0.0045f; *hi = 0.0134f; break;
-    case OR_W3: *lo = 0.0043f; *hi = 0.0128f; break;
-    default: *lo = 0.0022f; *hi = 0.0065f; break;
+    case OR_W3: *lo = 0.0050f; *hi = 0.0150f; break;
+    default: *lo = 0.0023f; *hi = 0.0069f; break;
   }
 }
 
@@ -853,9 +853,13 @@ static inline float unit_float(uint64_t h) {
   return (float)(h >> 40) * (1.0f / 16777216.0f);
 }
 
+/* Zero-mean synthetic codes: W2 levels {-3,-1,1,3} (top two hash bits), W3 q
+ * uniform on {-3..3}, W4 q uniform on {-7..7}; returned as reference codes. */
 static inline uint8_t synthetic_code(uint64_t seed, uint32_t tensor, size_t index, int format) {
-  const unsigned bits = format == OR_W2 ? 2 : (format == OR_W3 ? 3 : 4);
-  return (uint8_t)(or_hash(seed, 2ull * tensor, index) >> (64 - bits));
+  const uint64_t h = or_hash(seed, 2ull * tensor, index);
+  if (format == OR_W2) return (uint8_t)(h >> 62);
+  if (format == OR_W3) return (uint8_t)((h >> 32) % 7u + 1u);
+  return (uint8_t)(((int)((h >> 32) % 15u) - 7) & 0x0f);
 }
 
 void or_gen_codes_rowmajor(uint64_t seed, uint32_t tensor, size_t rows, size_t columns,

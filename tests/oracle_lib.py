@@ -51,8 +51,9 @@ def model_config(**kw) -> ModelConfig:
     return ModelConfig(**defaults)
 
 
-SMALL_MODEL = dict(hidden=1024, intermediate=2048, layers=8, gdn_key_heads=2, gdn_value_heads=6,
-                   q_heads=6, kv_heads=2, vocab=4096, draft_vocab=3072, max_context=320)
+SMALL_MODEL = dict(hidden=1024, intermediate=2048, layers=8, gdn_key_heads=4, gdn_value_heads=16,
+                   q_heads=8, kv_heads=2, vocab=4096, draft_vocab=3072, max_context=320)
+"""Every dimension of BASELINE config 2 scaled down, same structure (3 GDN : 1 attention layers)."""
 
 
 class Oracle:
@@ -198,3 +199,45 @@ class Reference:
         tiled_scales = np.zeros_like(scales)
         status = self.lib.ref_tile_gfx12(_ptr(codes), _ptr(scales), rows, cols, fmt, _ptr(tiled), _ptr(tiled_scales))
         return status, tiled, tiled_scales
+
+
+class OracleModel:
+    """Scalar forward of the synthetic model (oracle.c or_model_*)."""
+
+    def __init__(self, oracle: Oracle, config: ModelConfig, include_mtp: bool = True) -> None:
+        self.oracle = oracle
+        self.config = config
+        self.handle = c_void_p(oracle.lib.or_model_create(ctypes.byref(config), int(include_mtp)))
+
+    def greedy_step(self, token: int) -> int:
+        out = c_uint32()
+        assert self.oracle.lib.or_model_greedy_step(self.handle, token, ctypes.byref(out)) == 0
+        return out.value
+
+    def mtp_draft(self, token: int, use_mtp_hidden: bool = False) -> int:
+        out = c_uint32()
+        assert self.oracle.lib.or_model_mtp_draft(self.handle, token, int(use_mtp_hidden), ctypes.byref(out)) == 0
+        return out.value
+
+    def last_hidden(self) -> np.ndarray:
+        ptr = self.oracle.lib.or_model_last_hidden(self.handle)
+        return np.ctypeslib.as_array(ctypes.cast(ptr, POINTER(ctypes.c_uint16)), (self.config.hidden,)).copy()
+
+    def logits(self) -> np.ndarray:
+        ptr = self.oracle.lib.or_model_logits(self.handle)
+        return np.ctypeslib.as_array(ctypes.cast(ptr, POINTER(ctypes.c_float)), (self.config.vocab,)).copy()
+
+    def close(self) -> None:
+        if self.handle:
+            self.oracle.lib.or_model_destroy(self.handle)
+            self.handle = c_void_p()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def prompt_tokens(oracle: Oracle, seed: int, vocab: int, count: int) -> list[int]:
+    return [oracle.lib.or_prompt_token(seed, vocab, i) for i in range(count)]

@@ -1,0 +1,162 @@
+"""End-to-end decode parity: the B200 session vs the CPU oracle's scalar forward.
+
+Bit-exact: every kernel follows the oracle's reduction order, so tokens,
+final hidden states and logits agree exactly. The reference's own
+end-to-end gates are restated too: block_step equals serial greedy steps
+(src/cli/main.cpp:866-887) and the speculative stream equals the serial
+greedy stream (src/cli/main.cpp:961-979).
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle_lib import SMALL_MODEL, OracleModel, model_config, prompt_tokens  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def small_engine():
+    from gfxinfer_b200 import build
+
+    build.build()
+    from gfxinfer_b200 import session as gs
+
+    engine = gs.Engine.create(gs.model_config(**SMALL_MODEL))
+    yield engine
+    engine.close()
+
+
+def _session(engine, graphs=True):
+    from gfxinfer_b200 import session as gs
+
+    return gs.QwenDecodeSession.create(engine, use_graphs=graphs)
+
+
+def _greedy_stream(step, prompt, steps):
+    token = None
+    for t in prompt:
+        token = step(t)
+    out = []
+    for _ in range(steps):
+        out.append(token)
+        token = step(token)
+    return out
+
+
+def test_greedy_128_steps_bit_exact_small_model(oracle, small_engine):
+    cfg = model_config(**SMALL_MODEL)
+    prompt = prompt_tokens(oracle, cfg.seed, cfg.vocab, 16)
+    ref = OracleModel(oracle, cfg, include_mtp=False)
+    want = _greedy_stream(ref.greedy_step, prompt, 128)
+    session = _session(small_engine)
+    got = _greedy_stream(session.greedy_step, prompt, 128)
+    assert got == want
+    hidden, logits = session.read_state(cfg.vocab)
+    np.testing.assert_array_equal(hidden, ref.last_hidden())
+    np.testing.assert_array_equal(logits.view(np.uint32), ref.logits().view(np.uint32))
+    assert len(set(want)) > 8  # the stream is not degenerate
+    session.close()
+
+
+def test_eager_and_graph_paths_agree(oracle, small_engine):
+    cfg = model_config(**SMALL_MODEL)
+    prompt = prompt_tokens(oracle, cfg.seed + 1, cfg.vocab, 5)
+    a, b = _session(small_engine, graphs=True), _session(small_engine, graphs=False)
+    assert _greedy_stream(a.greedy_step, prompt, 20) == _greedy_stream(b.greedy_step, prompt, 20)
+
+
+def test_device_resident_loop_matches_greedy(oracle, small_engine):
+    cfg = model_config(**SMALL_MODEL)
+    prompt = prompt_tokens(oracle, cfg.seed + 2, cfg.vocab, 4)
+    a = _session(small_engine)
+    stream = _greedy_stream(a.greedy_step, prompt, 12)
+    b = _session(small_engine)
+    for t in prompt[:-1]:
+        b.greedy_step(t)
+    b.enqueue_greedy(prompt[-1], 12)
+    b.sync()
+    # the device loop feeds each argmax back: its last output is the 12th generated token
+    assert b.last_token() == stream[11]
+    assert b.position() == len(prompt) + 11
+
+
+@pytest.mark.parametrize("width", [2, 5, 17, 32])
+def test_block_step_equals_serial_greedy(oracle, small_engine, width):
+    cfg = model_config(**SMALL_MODEL)
+    tokens = prompt_tokens(oracle, cfg.seed + width, cfg.vocab, 40)
+    serial = _session(small_engine)
+    expected = [serial.greedy_step(t) for t in tokens[:8]]
+    expected += [serial.greedy_step(t) for t in tokens[8:8 + width]]
+    block = _session(small_engine)
+    got = block.block_step(tokens[:8]) + block.block_step(tokens[8:8 + width])
+    assert got == expected
+    assert block.position() == 8 + width
+
+
+def test_mtp_draft_bit_exact(oracle, small_engine):
+    cfg = model_config(**SMALL_MODEL)
+    prompt = prompt_tokens(oracle, cfg.seed + 7, cfg.vocab, 6)
+    ref = OracleModel(oracle, cfg, include_mtp=True)
+    session = _session(small_engine)
+    want, got = [], []
+    for t in prompt:
+        nxt_ref = ref.greedy_step(t)
+        nxt = session.greedy_step(t)
+        assert nxt == nxt_ref
+        want.append(ref.mtp_draft(nxt_ref))
+        got.append(session.mtp_draft(nxt))
+    assert got == want
+
+
+@pytest.mark.parametrize("depth", [1, 4, 8])
+def test_speculative_stream_equals_greedy(oracle, small_engine, depth):
+    cfg = model_config(**SMALL_MODEL)
+    prompt = prompt_tokens(oracle, cfg.seed + 11, cfg.vocab, 8)
+    greedy = _session(small_engine)
+    reference_stream = _greedy_stream(greedy.greedy_step, prompt, 48)
+    spec = _session(small_engine)
+    token = None
+    for t in prompt:
+        token = spec.greedy_step(t)
+        spec.mtp_draft(token)
+    emitted = []
+    while len(emitted) < 40:
+        result = spec.speculative_step(token, depth)
+        emitted.append(token)
+        emitted.extend(result.tokens[:-1])
+        token = result.tokens[-1]
+        assert 0 <= result.accepted_drafts <= depth
+    assert emitted[:40] == reference_stream[:40]
+
+
+def test_invalid_arguments_are_rejected(small_engine):
+    from gfxinfer_b200 import GfxbError
+
+    session = _session(small_engine)
+    with pytest.raises(GfxbError) as error:
+        session.greedy_step(10**9)
+    assert error.value.status == 1
+    with pytest.raises(GfxbError):
+        session.block_step([])
+    with pytest.raises(GfxbError):
+        session.block_step([1] * 33)
+    with pytest.raises(GfxbError):
+        session.speculative_step(1, 4)  # no aligned MTP state yet
+
+
+def test_full_width_four_layers_matches_oracle(oracle):
+    """Config-2 widths (hidden 5120, MLP 17408 W3, 48/16 GDN heads, 24/4 attention heads, vocab 151936)."""
+    from gfxinfer_b200 import session as gs
+
+    cfg = model_config(layers=4, max_context=64)
+    engine = gs.Engine.create(gs.model_config(layers=4, max_context=64), include_mtp=False)
+    session = gs.QwenDecodeSession.create(engine)
+    ref = OracleModel(oracle, cfg, include_mtp=False)
+    prompt = prompt_tokens(oracle, cfg.seed, cfg.vocab, 3)
+    assert _greedy_stream(session.greedy_step, prompt, 2) == _greedy_stream(ref.greedy_step, prompt, 2)
+    hidden, logits = session.read_state(cfg.vocab)
+    np.testing.assert_array_equal(hidden, ref.last_hidden())
+    np.testing.assert_array_equal(logits.view(np.uint32), ref.logits().view(np.uint32))
+    session.close()
+    engine.close()
