@@ -111,23 +111,28 @@ def test_mtp_draft_bit_exact(oracle, small_engine):
 
 @pytest.mark.parametrize("depth", [1, 4, 8])
 def test_speculative_stream_equals_greedy(oracle, small_engine, depth):
+    """spec-bench (src/cli/main.cpp:917-979): one greedy step, then speculative rounds; the
+    emitted stream must equal the serial greedy stream token for token."""
     cfg = model_config(**SMALL_MODEL)
-    prompt = prompt_tokens(oracle, cfg.seed + 11, cfg.vocab, 8)
-    greedy = _session(small_engine)
-    reference_stream = _greedy_stream(greedy.greedy_step, prompt, 48)
+    start = prompt_tokens(oracle, cfg.seed + 11, cfg.vocab, 1)[0]
     spec = _session(small_engine)
-    token = None
-    for t in prompt:
-        token = spec.greedy_step(t)
-        spec.mtp_draft(token)
-    emitted = []
+    first = spec.greedy_step(start)
+    emitted, seed, proposed, accepted = [first], first, 0, 0
     while len(emitted) < 40:
-        result = spec.speculative_step(token, depth)
-        emitted.append(token)
-        emitted.extend(result.tokens[:-1])
-        token = result.tokens[-1]
-        assert 0 <= result.accepted_drafts <= depth
-    assert emitted[:40] == reference_stream[:40]
+        result = spec.speculative_step(seed, depth)
+        assert 1 <= len(result.tokens) <= depth + 1
+        proposed += result.proposed_drafts
+        accepted += result.accepted_drafts
+        emitted.extend(result.tokens)
+        seed = result.tokens[-1]
+    serial = _session(small_engine)
+    token = serial.greedy_step(start)
+    reference = [token]
+    while len(reference) < len(emitted):
+        token = serial.greedy_step(token)
+        reference.append(token)
+    assert emitted == reference
+    assert spec.position() == serial.position()
 
 
 def test_invalid_arguments_are_rejected(small_engine):
