@@ -225,6 +225,8 @@ cudaError_t launch_kernel(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, 
 
 // ---- shared-memory staging: mbarriers, bulk copies, clusters ---------------
 
+constexpr std::uint32_t kSuspendHintNs = 20000;
+
 __device__ __forceinline__ std::uint32_t smem_addr(const void* pointer) {
   return static_cast<std::uint32_t>(__cvta_generic_to_shared(pointer));
 }
@@ -251,12 +253,14 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, std::uint32
       : "memory");
 }
 
+// The waiting thread is suspended in hardware until the phase completes or
+// the hint (ns) expires, so waiting warps do not compete for issue slots.
 __device__ __forceinline__ bool mbar_try_wait(std::uint64_t* bar, std::uint32_t parity) {
   std::uint32_t done;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
       : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return done != 0;
 }
@@ -264,7 +268,7 @@ __device__ __forceinline__ bool mbar_try_wait(std::uint64_t* bar, std::uint32_t 
 // Every wait is bounded: on expiry the kernel records kDeviceErrorTimeout in
 // `error` (when given) and the caller skips the work instead of hanging.
 constexpr std::uint32_t kDeviceErrorTimeout = 1u;
-constexpr std::uint32_t kWaitLimit = 1u << 22;
+constexpr std::uint32_t kWaitLimit = 1u << 16;
 
 __device__ __forceinline__ bool mbar_wait_bounded(std::uint64_t* bar, std::uint32_t parity,
                                                   std::uint32_t* error) {

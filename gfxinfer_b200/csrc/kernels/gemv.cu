@@ -12,7 +12,9 @@
 // W4 u = q + 8, W2 u = (q + 3) / 2, and the exact correction
 // dot = alpha * mma(u, a) + beta * sum(a) uses a per-group activation sum
 // carried in the activation pack.
+#include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -306,7 +308,7 @@ struct StreamLayout {
 };
 
 __host__ __device__ inline StreamLayout stream_layout(int bits, std::uint32_t groups, std::uint32_t parts,
-                                                      std::uint32_t batch) {
+                                                      std::uint32_t batch, std::uint32_t chunk) {
   StreamLayout s{};
   s.per_part = (groups + parts - 1) / parts;
   s.weight_bytes = s.per_part * static_cast<std::uint32_t>(bits) * 256u;
@@ -314,7 +316,7 @@ __host__ __device__ inline StreamLayout stream_layout(int bits, std::uint32_t gr
   s.dot_bytes = groups * 16u * batch * 4u;
   s.act_scale_bytes = (groups * batch * 2u + 15u) & ~15u;
   s.bar_offset = (s.weight_bytes + s.scale_bytes + s.dot_bytes + s.act_scale_bytes + 15u) & ~15u;
-  const std::uint32_t bars = (s.per_part + 7u) / 8u + 1u;
+  const std::uint32_t bars = (s.per_part + chunk - 1u) / chunk + 1u;
   s.total = s.bar_offset + bars * 8u;
   return s;
 }
@@ -333,7 +335,8 @@ __device__ __forceinline__ void load_lane_shared(const std::uint8_t* block, unsi
 }
 
 template <int Bits>
-__global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, std::uint32_t parts) {
+__global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, std::uint32_t parts,
+                                                          std::uint32_t chunk) {
   extern __shared__ __align__(128) std::uint8_t smem[];
   pdl_trigger();
   const std::uint32_t part = cluster_ctarank();
@@ -344,10 +347,10 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   const std::uint32_t G = args.groups, B = args.batch, K = args.columns;
   constexpr std::uint32_t kBlock = Bits * 256u;
   constexpr int kAlpha = Codec<Bits>::alpha, kBeta = Codec<Bits>::beta;
-  const StreamLayout layout = stream_layout(Bits, G, parts, B);
+  const StreamLayout layout = stream_layout(Bits, G, parts, B, chunk);
   const std::uint32_t g_begin = min(G, part * layout.per_part);
   const std::uint32_t n = min(G, g_begin + layout.per_part) - g_begin;
-  const std::uint32_t chunks = (n + 7u) / 8u;
+  const std::uint32_t chunks = (n + chunk - 1u) / chunk;
 
   std::uint8_t* stage = smem;
   __half* tile_scales = reinterpret_cast<__half*>(smem + layout.weight_bytes);
@@ -355,7 +358,7 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   __half* act_scale_stage =
       reinterpret_cast<__half*>(smem + layout.weight_bytes + layout.scale_bytes + layout.dot_bytes);
   std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(smem + layout.bar_offset);
-  const std::uint32_t scale_bar = (layout.per_part + 7u) / 8u;
+  const std::uint32_t scale_bar = (layout.per_part + chunk - 1u) / chunk;
 
   if (threadIdx.x == 0) {
     for (std::uint32_t c = 0; c <= scale_bar; ++c) mbar_init(&bars[c], 1);
@@ -365,9 +368,9 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   if (threadIdx.x == 0) {
     const std::uint8_t* source = m.codes + (static_cast<std::size_t>(tile) * G + g_begin) * kBlock;
     for (std::uint32_t c = 0; c < chunks; ++c) {
-      const std::uint32_t bytes = min(8u, n - 8u * c) * kBlock;
+      const std::uint32_t bytes = min(chunk, n - chunk * c) * kBlock;
       mbar_expect_tx(&bars[c], bytes);
-      bulk_g2s(stage + 8u * c * kBlock, source + 8u * c * kBlock, bytes, &bars[c]);
+      bulk_g2s(stage + chunk * c * kBlock, source + chunk * c * kBlock, bytes, &bars[c]);
     }
     if (part == 0) {
       mbar_expect_tx(&bars[scale_bar], layout.scale_bytes);
@@ -398,7 +401,7 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
     const std::uint32_t act_groups = args.act_stride / kGroup;
     const int s0 = t0 < B ? __ldg(args.act_sums + t0 * act_groups + g) : 0;
     const int s1 = t1 < B ? __ldg(args.act_sums + t1 * act_groups + g) : 0;
-    if (!mbar_wait_bounded(&bars[local / 8u], 0, &g_gemv_error)) break;
+    if (!mbar_wait_bounded(&bars[local / chunk], 0, &g_gemv_error)) break;
     LaneWords<Bits> w;
     load_lane_shared<Bits>(stage + local * kBlock, lane, w);
     std::uint32_t a[4][4];
@@ -450,11 +453,31 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   }
 }
 
+std::uint32_t env_value(const char* name, std::uint32_t fallback) {
+  const char* value = std::getenv(name);
+  return value != nullptr && value[0] != '\0' ? static_cast<std::uint32_t>(std::strtoul(value, nullptr, 10)) : fallback;
+}
+
+// Tuning knobs (read once): cluster split override and groups per bulk copy.
+struct StreamTuning {
+  std::uint32_t parts = env_value("GFXB_GEMV_PARTS", 0);
+  std::uint32_t chunk = std::max<std::uint32_t>(1u, env_value("GFXB_GEMV_CHUNK", 8));
+  std::uint32_t min_tiles_p1 = env_value("GFXB_GEMV_P1_TILES", 1024);
+};
+
+const StreamTuning& tuning() {
+  static const StreamTuning t;
+  return t;
+}
+
 template <int Bits>
 int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t stream) {
-  std::uint32_t parts = total_tiles >= 1024u ? 1u : (total_tiles >= 512u ? 2u : 4u);
+  const StreamTuning& tune = tuning();
+  std::uint32_t parts = total_tiles >= tune.min_tiles_p1 ? 1u : (total_tiles >= tune.min_tiles_p1 / 2 ? 2u : 4u);
+  if (tune.parts != 0) parts = tune.parts;
   while (parts > 1u && parts > args.groups) parts >>= 1;
-  const StreamLayout layout = stream_layout(Bits, args.groups, parts, args.batch);
+  const std::uint32_t chunk = tune.chunk;
+  const StreamLayout layout = stream_layout(Bits, args.groups, parts, args.batch, chunk);
   static int configured_bytes = 0;
   if (static_cast<int>(layout.total) > configured_bytes) {
     const cudaError_t error = cudaFuncSetAttribute(gemv_stream_kernel<Bits>,
@@ -479,7 +502,7 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
   config.attrs = attribute;
   config.numAttrs = 1;
   const cudaError_t error = launch_kernel(gemv_stream_kernel<Bits>, config.gridDim, config.blockDim,
-                                          config.dynamicSmemBytes, stream, parts, args, parts);
+                                          config.dynamicSmemBytes, stream, parts, args, parts, chunk);
   if (error != cudaSuccess) {
     set_error_cuda(error, "streaming GEMV launch failed");
     return GFXB_CUDA_ERROR;
@@ -1219,7 +1242,8 @@ int lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, unsigned matrix_co
   GFXB_REQUIRE(args.act_stride >= args.columns && args.act_stride % kGroup == 0, "activation stride is invalid");
   const int bits = bits_of(format);
   const unsigned grid = static_cast<unsigned>(total_tiles);
-  if (batch <= 8) {
+  static const bool force_v1 = env_value("GFXB_GEMV_V1", 0) != 0;
+  if (batch <= 8 && !force_v1) {
     if (bits == 2) return launch_stream<2>(args, grid, stream);
     if (bits == 3) return launch_stream<3>(args, grid, stream);
     return launch_stream<4>(args, grid, stream);

@@ -77,25 +77,21 @@ __global__ __launch_bounds__(kNormThreads) void residual_norm_pack_kernel(NormPa
   __shared__ int warp_code_sums[Iterations][8];
 
   float values[Iterations];
+  float weights[Iterations];
   float square_sum = 0.0f;
+  // Every global load is issued before any store: the outputs may alias the
+  // inputs as far as the compiler knows, so interleaving them would serialise
+  // one memory round trip per element.
 #pragma unroll
   for (unsigned it = 0; it < iterations; ++it) {
-    const std::size_t index = row + it * kNormThreads + t;
-    float value;
-    if (args.embedding_codes != nullptr) {
-      value = 0.0f;  // replaced below
-    } else if (args.update != nullptr) {
-      const __half rounded = f2h(__fadd_rn(h2f(args.residual[index]), args.update[index]));
-      if (args.residual_out != nullptr) args.residual_out[index] = rounded;
-      value = h2f(rounded);
-    } else {
-      value = h2f(args.residual[index]);
-    }
-    values[it] = value;
+    const std::uint32_t column = it * kNormThreads + t;
+    float scale = bf2f(args.weight[column]);
+    if (args.unit_offset) scale = __fadd_rn(scale, 1.0f);
+    weights[it] = scale;
   }
   if (args.embedding_codes != nullptr) {
     // Embedding row gather fused as the input (lowbit_gemv.hip:158-189, W4/W2 row-major).
-    std::uint32_t id = args.device_tokens != nullptr ? args.device_tokens[token] : args.host_token;
+    const std::uint32_t id = args.device_tokens != nullptr ? args.device_tokens[token] : args.host_token;
     const bool valid = id < args.embedding_rows;
     const std::uint32_t groups = H / kGroup;
 #pragma unroll
@@ -116,8 +112,28 @@ __global__ __launch_bounds__(kNormThreads) void residual_norm_pack_kernel(NormPa
                                   h2f(args.embedding_scales[static_cast<std::size_t>(id) * groups + column / kGroup]))));
       }
       values[it] = value;
-      if (args.residual_out != nullptr) args.residual_out[row + column] = f2h(value);
     }
+    if (args.residual_out != nullptr) {
+#pragma unroll
+      for (unsigned it = 0; it < iterations; ++it) args.residual_out[row + it * kNormThreads + t] = f2h(values[it]);
+    }
+  } else if (args.update != nullptr) {
+    float updates[Iterations];
+#pragma unroll
+    for (unsigned it = 0; it < iterations; ++it) {
+      const std::size_t index = row + it * kNormThreads + t;
+      values[it] = h2f(args.residual[index]);
+      updates[it] = args.update[index];
+    }
+#pragma unroll
+    for (unsigned it = 0; it < iterations; ++it) {
+      const __half rounded = f2h(__fadd_rn(values[it], updates[it]));
+      values[it] = h2f(rounded);
+      if (args.residual_out != nullptr) args.residual_out[row + it * kNormThreads + t] = rounded;
+    }
+  } else {
+#pragma unroll
+    for (unsigned it = 0; it < iterations; ++it) values[it] = h2f(args.residual[row + it * kNormThreads + t]);
   }
 #pragma unroll
   for (unsigned it = 0; it < iterations; ++it) square_sum = fmaf(values[it], values[it], square_sum);
@@ -129,9 +145,7 @@ __global__ __launch_bounds__(kNormThreads) void residual_norm_pack_kernel(NormPa
 #pragma unroll
   for (unsigned it = 0; it < iterations; ++it) {
     const std::uint32_t column = it * kNormThreads + t;
-    float scale = bf2f(args.weight[column]);
-    if (args.unit_offset) scale = __fadd_rn(scale, 1.0f);
-    const __half y = f2h(__fmul_rn(__fmul_rn(values[it], inverse), scale));
+    const __half y = f2h(__fmul_rn(__fmul_rn(values[it], inverse), weights[it]));
     if (args.normalized_out != nullptr) args.normalized_out[row + column] = y;
     values[it] = h2f(y);
   }
@@ -527,14 +541,23 @@ __global__ __launch_bounds__(256) void attention_chunk_kernel(AttentionArgs args
   }
   const std::size_t row_stride = static_cast<std::size_t>(args.kv_heads) * 256u;
   const __half* keys = args.key_cache + (begin * args.kv_heads + kvh) * 256u + 8u * lane;
-  for (std::uint32_t p = 0; p < n; ++p) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(keys + p * row_stride);
-    const __half* hv = reinterpret_cast<const __half*>(&raw);
-    float s = 0.0f;
+  // eight key rows in flight per step; positions past n read row 0 (valid) and are dropped
+  for (std::uint32_t p0 = 0; p0 < n; p0 += 8) {
+    uint4 raw[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) s = fmaf(qf[j], h2f(hv[j]), s);
-    s = warp_sum_xor(s);
-    if (lane == 0) scores[warp][p] = __fmul_rn(s, 0.0625f);
+    for (int i = 0; i < 8; ++i) {
+      const std::uint32_t p = p0 + i < n ? p0 + i : 0u;
+      raw[i] = *reinterpret_cast<const uint4*>(keys + p * row_stride);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const __half* hv = reinterpret_cast<const __half*>(&raw[i]);
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s = fmaf(qf[j], h2f(hv[j]), s);
+      s = warp_sum_xor(s);
+      if (lane == 0 && p0 + i < n) scores[warp][p0 + i] = __fmul_rn(s, 0.0625f);
+    }
   }
   __syncwarp();
   // prefix maximum: lane owns positions 4l..4l+3
@@ -569,13 +592,23 @@ __global__ __launch_bounds__(256) void attention_chunk_kernel(AttentionArgs args
   float den = 0.0f;
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   const __half* values = args.value_cache + (begin * args.kv_heads + kvh) * 256u + 8u * lane;
-  for (std::uint32_t p = 0; p < n; ++p) {
-    const float alpha = alphas[warp][p], beta = betas[warp][p];
-    const uint4 raw = *reinterpret_cast<const uint4*>(values + p * row_stride);
-    const __half* hv = reinterpret_cast<const __half*>(&raw);
-    den = __fadd_rn(__fmul_rn(den, alpha), beta);
+  for (std::uint32_t p0 = 0; p0 < n; p0 += 8) {
+    uint4 raw[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(__fmul_rn(acc[j], alpha), __fmul_rn(h2f(hv[j]), beta));
+    for (int i = 0; i < 8; ++i) {
+      const std::uint32_t p = p0 + i < n ? p0 + i : 0u;
+      raw[i] = *reinterpret_cast<const uint4*>(values + p * row_stride);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (p0 + i < n) {
+        const float alpha = alphas[warp][p0 + i], beta = betas[warp][p0 + i];
+        const __half* hv = reinterpret_cast<const __half*>(&raw[i]);
+        den = __fadd_rn(__fmul_rn(den, alpha), beta);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(__fmul_rn(acc[j], alpha), __fmul_rn(h2f(hv[j]), beta));
+      }
+    }
   }
   if (lane == 0) {
     partial[0] = chunk_max;
