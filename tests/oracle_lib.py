@@ -80,7 +80,7 @@ class Oracle:
             "or_residual_add_rms_norm": (None, [c_void_p, c_void_p, c_void_p, c_size_t, c_float, c_int, c_void_p, c_void_p]),
             "or_silu_multiply_f16": (None, [c_void_p, c_void_p, c_size_t, c_void_p]),
             "or_gdn_conv_update": (None, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_uint]),
-            "or_gdn_recurrent": (None, [c_void_p] * 13 + [c_uint, c_uint, c_uint]),
+            "or_gdn_recurrent": (None, [c_void_p] * 12 + [c_uint, c_uint, c_uint]),
             "or_gdn_restore": (None, [c_void_p] * 6 + [c_size_t, c_uint, c_uint, c_uint]),
             "or_rope_table": (None, [c_size_t, c_uint, c_float, c_void_p, c_void_p]),
             "or_qk_norm_rope": (None, [c_void_p, c_size_t, c_void_p, c_uint, c_size_t, c_void_p, c_void_p, c_uint, c_void_p]),
