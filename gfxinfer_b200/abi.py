@@ -52,6 +52,7 @@ SIGNATURES: dict[str, tuple] = {
                                       c_uint64, P, c_uint, P, P, P, c_size_t, P]),
     "gfxb_gated_attention_scratch_bytes": (c_size_t, [c_uint, c_size_t, c_uint]),
     "gfxb_gated_attention": (c_int, [P, P, P, P, P, c_size_t, P, c_size_t, c_uint, c_uint, c_uint, P, c_size_t, P]),
+    "gfxb_gated_attention_static_scratch": (c_int, [P, P, P, P, P, c_size_t, P, c_size_t, c_uint, c_uint, c_uint, P]),
     "gfxb_argmax_scratch_bytes": (c_size_t, [c_uint]),
     "gfxb_argmax": (c_int, [P, P, P, c_size_t, c_size_t, c_uint, P, c_size_t, P]),
     "gfxb_read_device_errors": (c_int, [POINTER(c_uint32)]),

@@ -197,3 +197,75 @@ extern "C" int gfxb_argmax(const float* logits, const std::uint32_t* token_ids, 
   a.partial_indices = reinterpret_cast<std::uint32_t*>(static_cast<float*>(scratch) + static_cast<std::size_t>(batch) * 64);
   return launch_argmax(a, batch, as_stream(stream));
 }
+
+// ---------------------------------------------------------------------------
+// Gated attention without allocation.
+//
+// Some callers cannot call cudaMalloc: code that runs inside another
+// framework's memory budget (an inference server or plugin host that owns
+// all device memory), latency-critical loops that cannot afford the implicit
+// device synchronisation an allocation may cause, or embedded deployments that
+// fix their memory map at start-up. For them this entry point keeps the
+// attention chunk partials in a fixed array compiled into the library, so it
+// allocates nothing. The array is 4 MiB; every GPU that loads the library
+// holds it until the process exits.
+// ---------------------------------------------------------------------------
+
+#include <mutex>
+
+namespace {
+
+constexpr std::size_t kStaticAttentionScratchBytes = std::size_t{4} << 20;
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) float g_static_attention_scratch[kStaticAttentionScratchBytes / sizeof(float)];
+
+std::mutex g_static_scratch_mutex;
+void* g_static_scratch_address[kMaxDevices] = {};
+
+// Host code cannot pass the array's name to a kernel (it is a host-side
+// stand-in, not a device address), so the device address is looked up once
+// per device, with that device current, and cached.
+int static_scratch_address(void** address) {
+  int device = 0;
+  cudaError_t error = cudaGetDevice(&device);
+  if (error != cudaSuccess) {
+    set_error_cuda(error, "cudaGetDevice failed");
+    return GFXB_CUDA_ERROR;
+  }
+  if (device < 0 || device >= kMaxDevices) return fail(GFXB_UNSUPPORTED, "device index beyond the static scratch table");
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (g_static_scratch_address[device] == nullptr) {
+    void* pointer = nullptr;
+    error = cudaGetSymbolAddress(&pointer, g_static_attention_scratch);
+    if (error != cudaSuccess) {
+      set_error_cuda(error, "cudaGetSymbolAddress of the static attention scratch failed");
+      return GFXB_CUDA_ERROR;
+    }
+    g_static_scratch_address[device] = pointer;
+  }
+  *address = g_static_scratch_address[device];
+  return GFXB_OK;
+}
+
+}  // namespace
+
+extern "C" int gfxb_gated_attention_static_scratch(const std::uint16_t* query, const float* gate_projection,
+                                                   const std::uint16_t* key_cache, const std::uint16_t* value_cache,
+                                                   std::uint16_t* output, std::size_t base_token_count,
+                                                   const std::uint64_t* device_base_position, std::size_t capacity,
+                                                   unsigned q_heads, unsigned kv_heads, unsigned batch,
+                                                   void* stream) {
+  const std::size_t needed = attention_partial_bytes(q_heads, capacity, batch);
+  if (needed > kStaticAttentionScratchBytes) {
+    return fail(GFXB_INVALID_ARGUMENT,
+                "attention scratch (batch x q_heads x ceil(capacity / 128) x 258 floats) exceeds the 4 MiB "
+                "static array of gfxb_gated_attention_static_scratch; use gfxb_gated_attention with a caller buffer");
+  }
+  void* scratch = nullptr;
+  const int status = static_scratch_address(&scratch);
+  if (status != GFXB_OK) return status;
+  return gfxb_gated_attention(query, gate_projection, key_cache, value_cache, output, base_token_count,
+                              device_base_position, capacity, q_heads, kv_heads, batch, scratch,
+                              kStaticAttentionScratchBytes, stream);
+}

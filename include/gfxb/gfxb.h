@@ -171,6 +171,22 @@ int gfxb_gated_attention(const uint16_t* query, const float* gate_projection, co
                          const uint16_t* value_cache, uint16_t* output, size_t base_token_count,
                          const uint64_t* device_base_position, size_t capacity, unsigned q_heads,
                          unsigned kv_heads, unsigned batch, void* scratch, size_t scratch_bytes, void* stream);
+/* Allocation-free variant of gfxb_gated_attention, with no counterpart in the
+ * reference. For callers that cannot allocate device memory (a host framework
+ * that owns the memory budget, loops that cannot afford an allocation's
+ * implicit synchronisation, fixed memory maps): the chunk partials live in a
+ * 4 MiB array compiled into the library, held by every GPU that loads it
+ * until exit. Limit: batch x q_heads x ceil(capacity / 128) x 258 x 4 bytes
+ * <= 4 MiB, else GFXB_INVALID_ARGUMENT. The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress, device current); make
+ * that first call before any stream capture. All calls share the array:
+ * calls that overlap on the GPU (other streams, other threads) race. Nothing
+ * needs clearing between calls; each call writes every partial it reads. */
+int gfxb_gated_attention_static_scratch(const uint16_t* query, const float* gate_projection,
+                                        const uint16_t* key_cache, const uint16_t* value_cache, uint16_t* output,
+                                        size_t base_token_count, const uint64_t* device_base_position,
+                                        size_t capacity, unsigned q_heads, unsigned kv_heads, unsigned batch,
+                                        void* stream);
 size_t gfxb_argmax_scratch_bytes(unsigned batch);
 /* Replaces launch_argmax(_batch)(_mapped). */
 int gfxb_argmax(const float* logits, const uint32_t* token_ids, uint32_t* tokens, size_t vocabulary_size,
