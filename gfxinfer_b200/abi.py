@@ -28,6 +28,13 @@ class SessionConfig(ctypes.Structure):
     _fields_ = [("maximum_context_tokens", c_uint32), ("graph_verifier_batch", c_uint32), ("use_graphs", c_uint32)]
 
 
+class TpShardInfo(ctypes.Structure):
+    _fields_ = [(name, c_uint32) for name in (
+        "gdn_key_heads", "gdn_key_head0", "gdn_value_heads", "gdn_value_head0", "q_heads", "q_head0",
+        "kv_heads", "kv_head0", "intermediate", "intermediate0", "vocab", "vocab0", "fc_columns", "fc_column0",
+        "gdn_channels")]
+
+
 # name -> (restype, argtypes); kept in declaration order of include/gfxb/gfxb.h.
 SIGNATURES: dict[str, tuple] = {
     "gfxb_last_error_message": (c_char_p, []),
@@ -57,6 +64,7 @@ SIGNATURES: dict[str, tuple] = {
     "gfxb_argmax": (c_int, [P, P, P, c_size_t, c_size_t, c_uint, P, c_size_t, P]),
     "gfxb_read_device_errors": (c_int, [POINTER(c_uint32)]),
     "gfxb_nccl_unique_id": (c_int, [P]),
+    "gfxb_tp_shard": (c_int, [POINTER(ModelConfig), c_int, c_int, POINTER(TpShardInfo)]),
     "gfxb_engine_create_synthetic": (c_int, [POINTER(ModelConfig), c_int, c_int, c_int, P, c_int, POINTER(c_void_p)]),
     "gfxb_engine_destroy": (c_int, [P]),
     "gfxb_engine_weight_bytes": (c_int, [P, POINTER(c_uint64)]),

@@ -837,6 +837,18 @@ extern "C" int gfxb_nccl_unique_id(void* id128) {
   return GFXB_OK;
 }
 
+extern "C" int gfxb_tp_shard(const gfxb_model_config* config, int tp_rank, int tp_size, gfxb_tp_shard_info* out) {
+  if (config == nullptr || out == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  if (tp_size < 1 || tp_size > 8 || tp_rank < 0 || tp_rank >= tp_size) {
+    return fail(GFXB_INVALID_ARGUMENT, "tensor-parallel rank/size are invalid");
+  }
+  GFXB_TRY(validate_config(*config, static_cast<std::uint32_t>(tp_size)));
+  const Shard s = make_shard(*config, static_cast<std::uint32_t>(tp_size), static_cast<std::uint32_t>(tp_rank));
+  *out = gfxb_tp_shard_info{s.nk, s.kh0, s.nv, s.vh0, s.nq, s.qh0, s.nkv, s.kv0, s.inter, s.i0,
+                            s.vocab, s.v0, s.fc_cols, s.fc0, s.channels};
+  return GFXB_OK;
+}
+
 extern "C" int gfxb_engine_create_synthetic(const gfxb_model_config* config, int device, int tp_rank, int tp_size,
                                             const void* nccl_id128, int include_mtp, gfxb_engine** out) {
   if (config == nullptr || out == nullptr) return fail(GFXB_INVALID_ARGUMENT, "engine arguments are null");

@@ -32,6 +32,13 @@ def nccl_unique_id() -> bytes:
     return buf.raw
 
 
+def tp_shard(config: abi.ModelConfig, tp_rank: int, tp_size: int) -> abi.TpShardInfo:
+    """This rank's slice of every tensor-parallel dimension (host-side; no GPU needed)."""
+    out = abi.TpShardInfo()
+    check(lib().gfxb_tp_shard(ctypes.byref(config), tp_rank, tp_size, ctypes.byref(out)))
+    return out
+
+
 class Engine:
     """Resident weights of one model (or one tensor-parallel shard) on one GPU."""
 

@@ -217,6 +217,19 @@ typedef struct gfxb_session gfxb_session;
  * shared with the other ranks by the caller. */
 int gfxb_nccl_unique_id(void* id128);
 
+/* This rank's slice of every sharded dimension (heads, rows, columns): first
+ * index and count. Column-parallel: GDN key/value heads (qkv, z), attention
+ * query heads (q) and the KV heads they read, MLP rows, LM-head vocabulary
+ * rows. Row-parallel: GDN out, attention o, MLP down (K = the slices above),
+ * MTP fc (K slice of the 2*hidden input). Host-only; validates the config. */
+typedef struct {
+  uint32_t gdn_key_heads, gdn_key_head0, gdn_value_heads, gdn_value_head0;
+  uint32_t q_heads, q_head0, kv_heads, kv_head0;
+  uint32_t intermediate, intermediate0, vocab, vocab0, fc_columns, fc_column0;
+  uint32_t gdn_channels;
+} gfxb_tp_shard_info;
+int gfxb_tp_shard(const gfxb_model_config* config, int tp_rank, int tp_size, gfxb_tp_shard_info* shard);
+
 /* Engine::create for a seeded random-init model (replaces engine.cpp:62-216 for
  * synthetic weights). tp_size 1 needs no NCCL id. Weights are generated on the
  * device, shard by shard, into one arena. */

@@ -1,0 +1,76 @@
+"""Tensor parallelism on 2 GPUs: the sharded model equals the unsharded one.
+
+Each rank holds its slice of the same global synthetic model; row-parallel
+outputs are summed with an NCCL all-reduce, which changes the fp32 summation
+order, so TP=2 is compared to the (bit-exact) TP=1 oracle with a tolerance:
+first-step logits within 2 % of their spread, the same first token, and both
+ranks emitting identical token streams. Skipped with fewer than two GPUs.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from oracle_lib import SMALL_MODEL, OracleModel, model_config, prompt_tokens  # noqa: E402
+
+
+def _rank(rank, world, id_queue, result_queue, prompt):
+    import torch as t
+
+    t.cuda.set_device(rank)
+    from gfxinfer_b200 import session as gs
+
+    if rank == 0:
+        nccl_id = gs.nccl_unique_id()
+        for _ in range(world - 1):
+            id_queue.put(nccl_id)
+    else:
+        nccl_id = id_queue.get(timeout=120)
+    engine = gs.Engine.create(gs.model_config(**SMALL_MODEL), device=rank, tp_rank=rank, tp_size=world,
+                              nccl_id=nccl_id)
+    session = gs.QwenDecodeSession.create(engine)
+    first = session.greedy_step(prompt[0])
+    shard = gs.tp_shard(gs.model_config(**SMALL_MODEL), rank, world)
+    _, logits = session.read_state(shard.vocab)
+    token = first
+    stream = [first]
+    for tok in prompt[1:]:
+        token = session.greedy_step(tok)
+    for _ in range(12):
+        stream.append(token)
+        token = session.greedy_step(token)
+    block = session.block_step(prompt[:5])
+    result_queue.put((rank, logits, stream, block))
+    session.close()
+    engine.close()
+
+
+def test_tp2_matches_tp1(oracle):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from gfxinfer_b200 import build
+
+    build.build()
+    import torch.multiprocessing as mp
+
+    cfg = model_config(**SMALL_MODEL)
+    prompt = prompt_tokens(oracle, cfg.seed + 99, cfg.vocab, 6)
+    ctx = mp.get_context("spawn")
+    id_queue, result_queue = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, 2, id_queue, result_queue, prompt)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict((r, (l, s, b)) for r, l, s, b in [result_queue.get(timeout=300) for _ in procs])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    ref = OracleModel(oracle, cfg, include_mtp=False)
+    first = ref.greedy_step(prompt[0])
+    want = ref.logits()
+    got = np.concatenate([results[0][0], results[1][0]])
+    spread = float(want.max() - want.min())
+    assert np.abs(got - want).max() <= 0.02 * spread
+    assert results[0][1][0] == first
+    assert results[0][1] == results[1][1]  # both ranks select the same tokens
+    assert results[0][2] == results[1][2]
