@@ -103,6 +103,42 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+class _PeerWatchdog:
+    """Aborts the engine's NCCL communicator when another rank reports a failure through the
+    torch.distributed store, so this rank's pending collectives end with an error instead of
+    waiting for a peer that is gone."""
+
+    def __init__(self, engine) -> None:
+        import torch.distributed as dist
+
+        self.engine = engine
+        self.store = dist.distributed_c10d._get_default_store()
+        self.done = threading.Event()
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+
+    def _run(self) -> None:
+        while not self.done.wait(1.0):
+            try:
+                if self.store.add("gfxb_failures", 0) > 0:
+                    self.engine.abort()
+                    return
+            except Exception:
+                return
+
+    def stop(self) -> None:
+        self.done.set()
+
+    @staticmethod
+    def report_failure() -> None:
+        try:
+            import torch.distributed as dist
+
+            dist.distributed_c10d._get_default_store().add("gfxb_failures", 1)
+        except Exception:
+            pass
+
+
 def _dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -110,53 +146,67 @@ def _dist():
     return world, rank, local
 
 
-def cpu_baseline(steps_tokens: int = 2) -> dict:
-    """The oracle's scalar forward (C, OpenMP) on this host: 4 of the 64 layers (3 GDN + 1 attention)
-    and the LM head at full config-2 width; layer time scaled x16 to the full depth."""
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
-    from oracle_lib import Oracle, model_config
+class CpuSample:
+    """The reference path's CPU implementation on this host: the oracle's scalar forward (C, OpenMP over
+    all host cores). The model holds 4 of the 64 config-2 layers (3 GDN + 1 attention, the repeating unit)
+    and the full LM head at full width; per token, layer time is scaled x16 to the full depth."""
 
-    oracle = Oracle()
-    cfg = model_config(max_context=64)
-    start = time.perf_counter()
-    seconds_per_token = oracle.lib.or_time_layers(cfg, 3, 1, 1, steps_tokens)
-    wall = time.perf_counter() - start
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return {"value": round(1.0 / seconds_per_token, 4), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": (f"{steps_tokens} greedy tokens through 4 of 64 config-2 layers (3 GDN + 1 attention) "
-                       f"and the full LM head at full width; layer time x16 + head time per token "
-                       f"(sample wall {wall:.1f}s incl. weight generation)")}
+    def __init__(self) -> None:
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        from oracle_lib import Oracle, OracleModel, model_config
+
+        self.oracle = Oracle()
+        self.cores = int(self.oracle.lib.or_set_threads(os.cpu_count() or 1))
+        cfg = model_config(layers=4, max_context=64)
+        start = time.perf_counter()
+        self.model = OracleModel(self.oracle, cfg, include_mtp=False)
+        self.build_seconds = time.perf_counter() - start
+        self.token = 1
+        self.scale = 64 / 4
+
+    def step(self) -> float:
+        """One sampled token; returns the extrapolated seconds per full 64-layer token."""
+        layer0, head0, _ = self.model.timing()
+        self.token = self.model.greedy_step(self.token)
+        layer1, head1, _ = self.model.timing()
+        return (layer1 - layer0) * self.scale + (head1 - head0)
+
+    def describe(self, tokens: int) -> str:
+        return (f"{tokens} greedy tokens through 4 of 64 config-2 layers (3 GDN + 1 attention) and the full "
+                f"LM head (vocab 151936) at full width, scalar C forward on {self.cores} threads; layer time "
+                f"x16 + head time per token")
+
+
+def cpu_baseline(tokens: int = 2) -> dict:
+    sample = CpuSample()
+    seconds = [sample.step() for _ in range(tokens)]
+    value = 1.0 / statistics.mean(seconds)
+    return {"value": round(value, 4), "unit": UNIT, "cores": sample.cores, "kind": "port",
+            "sample": sample.describe(tokens)}
 
 
 def run_reference(args) -> None:
     world, rank, _ = _dist()
     if rank != 0:
         return
-    base = cpu_baseline(1)
-    per_step = 1.0 / base["value"]
-    # W warm-up + K timed "steps": each step is one bounded sample token of the CPU forward.
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
-    from oracle_lib import Oracle, model_config
-
-    oracle = Oracle()
-    cfg = model_config(max_context=64)
-    samples = []
+    sample = CpuSample()
+    seconds = []
     for i in range(args.warmup + args.steps):
-        t = oracle.lib.or_time_layers(cfg, 3, 1, 1, 1)
+        t = sample.step()
         if i >= args.warmup:
-            samples.append(t)
-    tokens_per_s = 1.0 / statistics.mean(samples)
+            seconds.append(t)
+    per_token = statistics.mean(seconds)
+    tokens_per_s = 1.0 / per_token
     line = {"impl": "reference", "metric": METRIC, "value": round(tokens_per_s, 4), "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(1000.0 * statistics.mean(samples), 3), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp32", "data": "synthetic",
-            "config": {"workload": "config-2 decode: 64-layer hybrid GDN/attention, hidden 5120, MLP 17408 W3, "
-                                   "W4 projections and LM head (vocab 151936), A4, ctx 512",
-                       "seq_len": 512, "global_batch": 1, "parallelism": "cpu"},
-            "cpu_baseline": {"value": round(tokens_per_s, 4), "unit": UNIT, "cores": base["cores"], "kind": "port",
-                             "sample": base["sample"]},
+            "ms_per_step": round(1000.0 * per_token, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "config-2 decode: 64-layer hybrid (48 GDN + 16 gated GQA), hidden 5120, "
+                                   "MLP 17408 W3, GDN/attention W4, W4 LM head vocab 151936, A4, batch 1, ctx 512",
+                       "global_batch": 1, "seq_len": 512, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(tokens_per_s, 4), "unit": UNIT, "cores": sample.cores, "kind": "port",
+                             "sample": sample.describe(args.steps)},
             "e2e": {"value": round(tokens_per_s, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    del per_step
     print(json.dumps(line), flush=True)
 
 
@@ -171,7 +221,9 @@ def run_b200(args) -> None:
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        # gloo carries only host-side plumbing (NCCL id, barriers, timing max); the data path is the
+        # engine's own NCCL communicator.
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     from gfxinfer_b200 import build
 
     if rank == 0 and not os.path.exists(os.path.join(ROOT, "gfxinfer_b200", "libgfxb200.so")):
@@ -192,6 +244,7 @@ def run_b200(args) -> None:
         nccl_id = holder[0]
     engine = gs.Engine.create(gs.model_config(**cfg), device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id,
                               include_mtp=False)
+    watchdog = _PeerWatchdog(engine) if world > 1 else None
     session = gs.QwenDecodeSession.create(engine, maximum_context_tokens=cfg["max_context"])
     stream = torch.cuda.ExternalStream(session.stream(), device=torch.device("cuda", local))
     rng = np.random.default_rng(cfg["seed"])
@@ -245,7 +298,7 @@ def run_b200(args) -> None:
     gemv_stop.synchronize()
     gemv_us = gemv_start.elapsed_time(gemv_stop) * 1000.0 / launches
 
-    times = torch.tensor([device_ms, e2e_ms, gemv_us], dtype=torch.float64, device="cuda")
+    times = torch.tensor([device_ms, e2e_ms, gemv_us], dtype=torch.float64)
     if world > 1:
         import torch.distributed as dist
 
@@ -284,6 +337,8 @@ def run_b200(args) -> None:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(2)
         print(json.dumps(line), flush=True)
+    if watchdog is not None:
+        watchdog.stop()
     session.close()
     engine.close()
     if world > 1:
@@ -306,8 +361,13 @@ def main() -> None:
         parser.error("prompt + warm-up + timed steps exceed the 512-token context")
     if args.impl == "reference":
         run_reference(args)
-    else:
+        return
+    try:
         run_b200(args)
+    except BaseException:
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            _PeerWatchdog.report_failure()
+        raise
 
 
 if __name__ == "__main__":

@@ -67,6 +67,7 @@ SIGNATURES: dict[str, tuple] = {
     "gfxb_tp_shard": (c_int, [POINTER(ModelConfig), c_int, c_int, POINTER(TpShardInfo)]),
     "gfxb_engine_create_synthetic": (c_int, [POINTER(ModelConfig), c_int, c_int, c_int, P, c_int, POINTER(c_void_p)]),
     "gfxb_engine_destroy": (c_int, [P]),
+    "gfxb_engine_abort": (c_int, [P]),
     "gfxb_engine_weight_bytes": (c_int, [P, POINTER(c_uint64)]),
     "gfxb_session_create": (c_int, [P, POINTER(SessionConfig), POINTER(c_void_p)]),
     "gfxb_session_destroy": (c_int, [P]),

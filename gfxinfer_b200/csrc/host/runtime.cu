@@ -64,6 +64,7 @@ struct NcclApi {
   ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
   ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
   ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
@@ -81,6 +82,7 @@ int load_nccl(NcclApi& api) {
   api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(api.handle, "ncclGetUniqueId"));
   api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(api.handle, "ncclCommInitRank"));
   api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(api.handle, "ncclCommDestroy"));
+  api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(dlsym(api.handle, "ncclCommAbort"));
   api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(api.handle, "ncclAllReduce"));
   api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(api.handle, "ncclAllGather"));
   api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(api.handle, "ncclGetErrorString"));
@@ -901,6 +903,14 @@ extern "C" int gfxb_engine_destroy(gfxb_engine* engine) {
   cudaStreamDestroy(engine->stream);
   delete engine;
   return GFXB_OK;
+}
+
+extern "C" int gfxb_engine_abort(gfxb_engine* engine) {
+  if (engine == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null engine");
+  if (engine->comm == nullptr || nccl().comm_abort == nullptr) return GFXB_OK;
+  const ncclComm_t comm = engine->comm;
+  engine->comm = nullptr;
+  return nccl_check(nccl().comm_abort(comm), "ncclCommAbort failed");
 }
 
 extern "C" int gfxb_engine_weight_bytes(const gfxb_engine* engine, std::uint64_t* bytes) {

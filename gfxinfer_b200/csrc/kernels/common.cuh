@@ -285,6 +285,18 @@ __device__ __forceinline__ std::uint32_t cluster_ctarank() {
   return rank;
 }
 
+__device__ __forceinline__ std::uint32_t cluster_nctarank() {
+  std::uint32_t count;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(count));
+  return count;
+}
+
+__device__ __forceinline__ std::uint32_t dynamic_smem_bytes() {
+  std::uint32_t bytes;
+  asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(bytes));
+  return bytes;
+}
+
 __device__ __forceinline__ std::uint32_t map_shared_rank(std::uint32_t address, std::uint32_t rank) {
   std::uint32_t mapped;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(mapped) : "r"(address), "r"(rank));
@@ -293,6 +305,15 @@ __device__ __forceinline__ std::uint32_t map_shared_rank(std::uint32_t address, 
 
 __device__ __forceinline__ void st_cluster_s32(std::uint32_t address, int value) {
   asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(address), "r"(value) : "memory");
+}
+
+// Split cluster barrier. A CTA must not touch another CTA's shared memory
+// before a cluster barrier has shown that every CTA of the cluster is running.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void cluster_sync_all() {

@@ -296,6 +296,9 @@ __global__ __launch_bounds__(256) void gemv_b200_kernel(const GemvArgs args) {
 // ---------------------------------------------------------------------------
 
 __device__ std::uint32_t g_gemv_error;
+constexpr std::uint32_t kGemvErrorCluster = 16u;  // cluster size differs from the split the host chose
+constexpr std::uint32_t kGemvErrorSmem = 32u;     // shared-memory layout exceeds the launch's dynamic size
+constexpr std::uint32_t kGemvErrorTile = 64u;     // CTA maps past the last tile of its matrix
 
 struct StreamLayout {
   std::uint32_t per_part;     // groups per cluster rank
@@ -360,6 +363,19 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(smem + layout.bar_offset);
   const std::uint32_t scale_bar = (layout.per_part + chunk - 1u) / chunk;
 
+  // Self-check of the launch geometry: every CTA of the grid sees the same
+  // values, so all of them return together, before any barrier or copy.
+  {
+    std::uint32_t bad = 0;
+    if (cluster_nctarank() != parts || part >= parts) bad |= kGemvErrorCluster;
+    if (layout.total > dynamic_smem_bytes()) bad |= kGemvErrorSmem;
+    if (tile >= m.tiles) bad |= kGemvErrorTile;
+    if (bad != 0) {
+      if (threadIdx.x == 0) atomicOr(&g_gemv_error, bad);
+      return;
+    }
+  }
+
   if (threadIdx.x == 0) {
     for (std::uint32_t c = 0; c <= scale_bar; ++c) mbar_init(&bars[c], 1);
     fence_mbar_init();
@@ -379,6 +395,9 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
     }
   }
 
+  // Every CTA of the cluster announces it is running; the wait below (before
+  // the first store into the leader's shared memory) completes this phase.
+  cluster_arrive();
   // Weights and their scales never depend on the previous kernel; the
   // activation pack does.
   pdl_wait();
@@ -391,6 +410,7 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   }
   const std::uint32_t leader_dots = map_shared_rank(smem_addr(dots), 0);
   const std::uint32_t token = min(gl, B - 1u);
+  cluster_wait();
   for (std::uint32_t local = warp; local < n; local += 8u) {
     const std::uint32_t g = g_begin + local;
     const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * args.act_stride +

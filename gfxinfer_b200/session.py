@@ -61,6 +61,11 @@ class Engine:
     def handle(self) -> ctypes.c_void_p:
         return self._handle
 
+    def abort(self) -> None:
+        """Abort the NCCL communicator so a step blocked on a failed peer returns an error."""
+        if self._handle:
+            check(lib().gfxb_engine_abort(self._handle))
+
     def weight_bytes(self) -> int:
         out = ctypes.c_uint64()
         check(lib().gfxb_engine_weight_bytes(self._handle, ctypes.byref(out)))

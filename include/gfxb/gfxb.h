@@ -236,6 +236,11 @@ int gfxb_tp_shard(const gfxb_model_config* config, int tp_rank, int tp_size, gfx
 int gfxb_engine_create_synthetic(const gfxb_model_config* config, int device, int tp_rank, int tp_size,
                                  const void* nccl_id128, int include_mtp, gfxb_engine** engine);
 int gfxb_engine_destroy(gfxb_engine* engine);
+/* Aborts the engine's NCCL communicator (callable from another thread while a
+ * step is blocked on a peer that failed): pending collectives end with an
+ * error instead of waiting for the lost rank. The engine can only be
+ * destroyed afterwards. */
+int gfxb_engine_abort(gfxb_engine* engine);
 int gfxb_engine_weight_bytes(const gfxb_engine* engine, uint64_t* bytes);
 
 typedef struct {

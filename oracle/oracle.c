@@ -1277,6 +1277,23 @@ int or_model_mtp_draft(or_model* m, uint32_t token, int use_mtp_hidden, uint32_t
 }
 
 size_t or_model_position(const or_model* m) { return m->position; }
+
+/* Cumulative seconds spent in the decoder layers and in the LM head + argmax. */
+void or_model_timing(const or_model* m, double* layer_seconds, double* head_seconds, size_t* tokens) {
+  *layer_seconds = m->layer_seconds;
+  *head_seconds = m->head_seconds;
+  *tokens = m->tokens;
+}
+
+int or_set_threads(int threads) {
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+  return omp_get_max_threads();
+#else
+  (void)threads;
+  return 1;
+#endif
+}
 const uint16_t* or_model_last_hidden(const or_model* m) { return m->last_hidden; }
 const float* or_model_logits(const or_model* m) { return m->logits; }
 

@@ -119,6 +119,8 @@ int or_model_block_step(or_model* model, const uint32_t* tokens, unsigned count,
 int or_model_mtp_draft(or_model* model, uint32_t token, int use_mtp_hidden,
                        uint32_t* draft);
 size_t or_model_position(const or_model* model);
+void or_model_timing(const or_model* model, double* layer_seconds, double* head_seconds, size_t* tokens);
+int or_set_threads(int threads);
 const uint16_t* or_model_last_hidden(const or_model* model);
 const float* or_model_logits(const or_model* model);
 double or_time_layers(const or_model_config* config, unsigned gdn_layers,

@@ -91,6 +91,8 @@ class Oracle:
             "or_model_greedy_step": (c_int, [c_void_p, c_uint32, POINTER(c_uint32)]),
             "or_model_mtp_draft": (c_int, [c_void_p, c_uint32, c_int, POINTER(c_uint32)]),
             "or_model_position": (c_size_t, [c_void_p]),
+            "or_model_timing": (None, [c_void_p, POINTER(c_double), POINTER(c_double), POINTER(c_size_t)]),
+            "or_set_threads": (c_int, [c_int]),
             "or_model_last_hidden": (c_void_p, [c_void_p]),
             "or_model_logits": (c_void_p, [c_void_p]),
             "or_time_layers": (c_double, [POINTER(ModelConfig), c_uint, c_uint, c_uint, c_uint]),
@@ -218,6 +220,11 @@ class OracleModel:
         out = c_uint32()
         assert self.oracle.lib.or_model_mtp_draft(self.handle, token, int(use_mtp_hidden), ctypes.byref(out)) == 0
         return out.value
+
+    def timing(self):
+        layer, head, tokens = c_double(), c_double(), c_size_t()
+        self.oracle.lib.or_model_timing(self.handle, ctypes.byref(layer), ctypes.byref(head), ctypes.byref(tokens))
+        return layer.value, head.value, tokens.value
 
     def last_hidden(self) -> np.ndarray:
         ptr = self.oracle.lib.or_model_last_hidden(self.handle)
