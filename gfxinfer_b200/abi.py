@@ -25,7 +25,11 @@ class ModelConfig(ctypes.Structure):
 
 
 class SessionConfig(ctypes.Structure):
-    _fields_ = [("maximum_context_tokens", c_uint32), ("graph_verifier_batch", c_uint32), ("use_graphs", c_uint32)]
+    _fields_ = [("maximum_context_tokens", c_uint32), ("graph_verifier_batch", c_uint32), ("use_graphs", c_uint32),
+                ("step_kernel", c_uint32)]
+
+
+STEP_AUTO, STEP_LAUNCHES, STEP_PERSISTENT = 0, 1, 2
 
 
 class TpShardInfo(ctypes.Structure):

@@ -25,6 +25,7 @@
 #include "gfxb/gfxb.h"
 #include "kernels/common.cuh"
 #include "kernels/ops.cuh"
+#include "kernels/token_loop.cuh"
 
 namespace gfxb {
 
@@ -42,12 +43,6 @@ int generate_bf16(std::uint64_t seed, std::uint32_t tensor, std::uint64_t offset
 int read_gemv_error(std::uint32_t* value, bool clear);
 
 namespace {
-
-#define GFXB_TRY(expression)              \
-  do {                                    \
-    const int status_ = (expression);     \
-    if (status_ != GFXB_OK) return status_; \
-  } while (0)
 
 int cuda_check(cudaError_t error, const char* context) {
   if (error == cudaSuccess) return GFXB_OK;
@@ -121,6 +116,7 @@ constexpr unsigned kMaxBlock = 32;
 
 std::uint32_t tensor_id(std::uint32_t layer, std::uint32_t kind) { return layer * 32u + kind; }
 int format_of(std::uint32_t bits) { return bits == 2 ? GFXB_W2 : (bits == 3 ? GFXB_W3 : GFXB_W4); }
+int bits_of_format(int format) { return format == GFXB_W2 ? 2 : (format == GFXB_W3 ? 3 : 4); }
 
 struct QMatrix {
   std::uint8_t* codes = nullptr;
@@ -385,6 +381,12 @@ struct gfxb_session {
   const __half* last_hidden = nullptr;
   std::uint32_t* pinned = nullptr;  // host staging
   cudaGraphExec_t greedy_graph = nullptr;
+  // persistent token kernel
+  __half* mlp_product = nullptr;  // fp16 SiLU(gate) * up of the token kernel's MLP
+  gfxb::LoopOp* loop_ops = nullptr;
+  gfxb::LoopControl* loop_control = nullptr;
+  gfxb::LoopLaunch loop{};
+  bool loop_ready = false;
 };
 
 namespace gfxb {
@@ -736,14 +738,238 @@ __global__ void copy_drafts_kernel(const std::uint32_t* drafts, std::uint32_t* t
   if (i < count) tokens[i + 1] = drafts[i];
 }
 
+// The batch-1 greedy step as one token-kernel operation list. Operation i
+// reads only outputs of operations before it (the kernel puts a grid barrier
+// in front of each); buffers follow enqueue_forward so both paths leave the
+// same state behind (hidden[0/1], post_attention, update, caches, logits).
+int build_token_loop(gfxb_session& s) {
+  gfxb_engine& e = *s.e;
+  const gfxb_model_config& c = e.cfg;
+  const Shard& sh = e.shard;
+  if (sh.tp != 1) return fail(GFXB_UNSUPPORTED, "token kernel: tensor-parallel sessions use per-operation launches");
+  if (!token_loop_supported_hidden(c.hidden)) return fail(GFXB_UNSUPPORTED, "token kernel: unsupported hidden size");
+  if (sh.nkv > kLoopMaxKvHeads) return fail(GFXB_UNSUPPORTED, "token kernel: too many KV heads");
+  std::uint32_t ctas = 0;
+  GFXB_TRY(token_loop_grid(e.device, &ctas));
+  const std::size_t ctx = s.cfg.maximum_context_tokens;
+  std::vector<LoopOp> ops;
+  std::uint32_t rotation = 0, max_groups = 0, dots_half = 0;
+  auto matrix = [](const QMatrix& q, void* output, std::uint32_t epilogue) {
+    LoopMatrix m{};
+    m.codes = q.codes;
+    m.scales = reinterpret_cast<const __half*>(q.scales);
+    m.output = output;
+    m.tiles = q.rows / 16u;
+    m.epilogue = epilogue;
+    return m;
+  };
+  auto add_op = [&](LoopOp& op, std::uint32_t units) {
+    op.rotation = rotation;
+    rotation = (rotation + units) % ctas;
+    ops.push_back(op);
+  };
+  auto add_gemv = [&](LoopGemv g, const std::vector<LoopMatrix>& mats, std::uint32_t columns, std::uint32_t bits) {
+    g.bits = bits;
+    g.groups = columns / 128u;
+    g.count = static_cast<std::uint32_t>(mats.size());
+    g.units = 0;
+    for (std::size_t i = 0; i < mats.size(); ++i) {
+      g.m[i] = mats[i];
+      g.units += mats[i].tiles;
+    }
+    if (g.paired) g.units = mats[0].tiles;
+    max_groups = std::max(max_groups, g.groups);
+    dots_half = std::max(dots_half, (g.paired ? 2u : 1u) * g.groups * 16u);
+    LoopOp op{};
+    op.kind = kLoopGemv;
+    op.gemv = g;
+    add_op(op, g.units);
+  };
+  auto residual_norm = [&](const __half* residual, __half* residual_out, const std::uint16_t* weight) {
+    LoopGemv g{};
+    g.act_source = kActResidualNorm;
+    g.residual = residual;
+    g.update = s.update;
+    g.residual_out = residual_out;
+    g.norm_weight = weight;
+    return g;
+  };
+  auto global_pack = [&]() {
+    LoopGemv g{};
+    g.act_source = kActGlobalPack;
+    g.pack_codes = s.act_codes;
+    g.pack_scales = s.act_scales;
+    g.pack_sums = s.act_sums;
+    return g;
+  };
+  const std::size_t kv_stride = ctx * sh.nkv * 256;
+  const std::size_t conv_elems = static_cast<std::size_t>(sh.channels) * 4;
+  const std::size_t state_elems = static_cast<std::size_t>(sh.nv) * 128 * 128;
+  const int act_bits = static_cast<int>(c.activation_bits);
+  for (std::uint32_t i = 0; i < c.layers; ++i) {
+    const Layer& L = e.layers[i];
+    __half* current = s.hidden[i % 2];
+    // input RMSNorm + mixer projections
+    LoopGemv in{};
+    if (i == 0) {
+      in.act_source = kActEmbedNorm;
+      in.embedding_codes = e.emb_codes;
+      in.embedding_scales = reinterpret_cast<const __half*>(e.emb_scales);
+      in.embedding_rows = c.vocab;
+      in.embedding_bits = c.emb_bits;
+      in.tokens = s.tokens;
+      in.residual_out = current;
+      in.norm_weight = L.input_norm;
+    } else {
+      in = residual_norm(s.post_attention, current, L.input_norm);
+    }
+    if (L.attention) {
+      add_gemv(in, {matrix(L.q, s.proj_main, kEpiF32), matrix(L.k, s.proj_k, kEpiF32), matrix(L.v, s.proj_v, kEpiF32)},
+               c.hidden, static_cast<std::uint32_t>(bits_of_format(L.q.format)));
+      LoopOp op{};
+      op.kind = kLoopAttention;
+      QkRopeArgs& r = op.rope;
+      r.q_input = s.proj_main;
+      r.q_weight = L.q_norm;
+      r.k_input = s.proj_k;
+      r.k_weight = L.k_norm;
+      r.v_input = s.proj_v;
+      r.key_cache = s.key_cache + L.state_index * kv_stride;
+      r.value_cache = s.value_cache + L.state_index * kv_stride;
+      r.capacity = ctx;
+      r.q_heads = sh.nq;
+      r.k_heads = sh.nkv;
+      r.q_stride = 512;
+      r.k_stride = 256;
+      r.rotary = 64;
+      r.cos_table = s.rope_cos;
+      r.sin_table = s.rope_sin;
+      r.table_positions = ctx;
+      r.device_base_position = s.position;
+      AttentionArgs& a = op.attention;
+      a.gate = s.proj_main;
+      a.key_cache = r.key_cache;
+      a.value_cache = r.value_cache;
+      a.output = s.attn_out;
+      a.partials = s.attention_partials;
+      a.max_chunks = s.attention_chunks;
+      a.capacity = ctx;
+      a.device_base_position = s.position;
+      a.q_heads = sh.nq;
+      a.kv_heads = sh.nkv;
+      a.act_bits = act_bits;
+      a.act_codes = s.act_codes;
+      a.act_scales = s.act_scales;
+      a.act_sums = s.act_sums;
+      add_op(op, sh.nkv * s.attention_chunks);
+      add_gemv(global_pack(), {matrix(L.out, s.update, kEpiF32)}, sh.nq * 256,
+               static_cast<std::uint32_t>(bits_of_format(L.out.format)));
+    } else {
+      LoopMatrix qkv = matrix(L.qkv, s.conv_out, kEpiConv);
+      qkv.conv_state = s.conv_states + L.state_index * conv_elems;
+      qkv.conv_weight = L.conv;
+      add_gemv(in, {qkv, matrix(L.z, s.proj_z, kEpiF32), matrix(L.a, s.proj_a, kEpiF32), matrix(L.b, s.proj_b, kEpiF32)},
+               c.hidden, static_cast<std::uint32_t>(bits_of_format(L.qkv.format)));
+      LoopOp op{};
+      op.kind = kLoopGdn;
+      GdnRecurrentArgs& g = op.gdn;
+      g.qkv = s.conv_out;
+      g.z = s.proj_z;
+      g.a = s.proj_a;
+      g.b = s.proj_b;
+      g.ab_stride = c.gdn_value_heads;
+      g.a_log = L.a_log;
+      g.dt_bias = L.dt_bias;
+      g.norm_weight = L.gdn_norm;
+      g.initial_state = s.gdn_states + L.state_index * state_elems;
+      g.final_state = s.gdn_states + L.state_index * state_elems;
+      g.output = s.gdn_out;
+      g.key_heads = sh.nk;
+      g.value_heads = sh.nv;
+      g.batch = 1;
+      g.act_bits = act_bits;
+      g.act_codes = s.act_codes;
+      g.act_scales = s.act_scales;
+      g.act_sums = s.act_sums;
+      add_op(op, sh.nv);
+      add_gemv(global_pack(), {matrix(L.out, s.update, kEpiF32)}, sh.nv * 128,
+               static_cast<std::uint32_t>(bits_of_format(L.out.format)));
+    }
+    // post-mixer RMSNorm + SwiGLU gate/up (fused SiLU product), then down
+    LoopGemv gate_up = residual_norm(current, s.post_attention, L.post_norm);
+    gate_up.paired = 1;
+    add_gemv(gate_up, {matrix(L.gate, s.mlp_product, kEpiSiluPair), matrix(L.up, nullptr, kEpiSiluPair)}, c.hidden,
+             static_cast<std::uint32_t>(bits_of_format(L.gate.format)));
+    LoopGemv down{};
+    down.act_source = kActPackF16;
+    down.f16_input = s.mlp_product;
+    add_gemv(down, {matrix(L.down, s.update, kEpiF32)}, sh.inter, static_cast<std::uint32_t>(bits_of_format(L.down.format)));
+  }
+  // final RMSNorm + LM head + argmax
+  add_gemv(residual_norm(s.post_attention, s.hidden[c.layers % 2], e.final_norm), {matrix(e.lm_head, s.logits, kEpiLogits)},
+           c.hidden, static_cast<std::uint32_t>(bits_of_format(e.lm_head.format)));
+  LoopOp argmax{};
+  argmax.kind = kLoopArgmax;
+  add_op(argmax, 0);
+  if (ops.size() > 5ull * c.layers + 4) return fail(GFXB_INTERNAL, "token kernel operation list overflow");
+
+  LoopLaunch& launch = s.loop;
+  launch = LoopLaunch{};
+  launch.ops = s.loop_ops;
+  launch.op_count = static_cast<std::uint32_t>(ops.size());
+  launch.control = s.loop_control;
+  launch.hidden = c.hidden;
+  launch.vocab = sh.vocab;
+  launch.selected = s.selected;
+  launch.tokens = s.tokens;
+  launch.position = s.position;
+  launch.act_bits = c.activation_bits;
+  GFXB_TRY(plan_token_loop(launch, max_groups, dots_half, e.device));
+  if (launch.ctas != ctas) return fail(GFXB_INTERNAL, "token kernel grid changed");
+  for (const LoopOp& op : ops) {
+    if (op.kind != kLoopGemv) continue;
+    if (token_loop_unit_slots(op.gemv.bits, op.gemv.groups, op.gemv.paired != 0) > launch.slots) {
+      return fail(GFXB_UNSUPPORTED, "token kernel: a weight tile does not fit the ring");
+    }
+  }
+  GFXB_TRY(cuda_check(cudaMemcpyAsync(s.loop_ops, ops.data(), ops.size() * sizeof(LoopOp), cudaMemcpyHostToDevice,
+                                      s.stream),
+                      "token kernel operation upload failed"));
+  GFXB_TRY(cuda_check(cudaMemsetAsync(s.loop_control, 0, sizeof(LoopControl), s.stream), "token kernel control reset failed"));
+  GFXB_TRY(cuda_check(cudaStreamSynchronize(s.stream), "token kernel setup failed"));
+  s.loop_ready = true;
+  return GFXB_OK;
+}
+
+// Error bits the token kernel left in the control block (0: none).
+int check_token_loop(gfxb_session& s) {
+  if (!s.loop_ready) return GFXB_OK;
+  std::uint32_t error = 0;
+  GFXB_TRY(cuda_check(cudaMemcpy(&error, &s.loop_control->error, sizeof error, cudaMemcpyDeviceToHost),
+                      "token kernel status read failed"));
+  if (error == 0) return GFXB_OK;
+  // clear the abort state so later steps run (their results follow the failed step's state)
+  GFXB_TRY(cuda_check(cudaMemset(s.loop_control, 0, sizeof(LoopControl)), "token kernel control reset failed"));
+  std::string message = "token kernel failed:";
+  if (error & kLoopErrorBarrier) message += " grid barrier wait expired;";
+  if (error & kLoopErrorRing) message += " weight ring wait expired;";
+  if (error & kLoopErrorContext) message += " position outside the KV cache or RoPE table;";
+  return fail((error & kLoopErrorContext) && !(error & (kLoopErrorBarrier | kLoopErrorRing)) ? GFXB_INVALID_ARGUMENT
+                                                                                             : GFXB_INTERNAL,
+              message.c_str());
+}
+
+int enqueue_greedy_step(gfxb_session& s) {
+  if (s.loop_ready) return launch_token_loop(s.loop, s.stream);
+  GFXB_TRY(enqueue_forward(s, 1, s.tokens, s.position, false));
+  advance_kernel<<<1, 1, 0, s.stream>>>(s.position, s.tokens, s.selected, 1);
+  return launch_status("advance launch failed");
+}
+
 int capture_greedy(gfxb_session& s) {
   cudaGraph_t graph = nullptr;
   GFXB_TRY(cuda_check(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal), "graph capture start failed"));
-  int status = enqueue_forward(s, 1, s.tokens, s.position, false);
-  if (status == GFXB_OK) {
-    advance_kernel<<<1, 1, 0, s.stream>>>(s.position, s.tokens, s.selected, 1);
-    status = launch_status("advance launch failed");
-  }
+  const int status = enqueue_greedy_step(s);
   const cudaError_t end = cudaStreamEndCapture(s.stream, &graph);
   if (status != GFXB_OK) {
     if (graph) cudaGraphDestroy(graph);
@@ -817,6 +1043,9 @@ int allocate_session(gfxb_session& s, bool place) {
   s.mtp_values = plan.take<__half>(ctx * sh.nkv * 256);
   s.rope_cos = plan.take<float>(ctx * 32);
   s.rope_sin = plan.take<float>(ctx * 32);
+  s.mlp_product = plan.take<__half>(B * sh.inter);
+  s.loop_control = plan.take<LoopControl>(1);
+  s.loop_ops = plan.take<LoopOp>(5ull * c.layers + 4);
   s.arena_bytes = plan.offset;
   return GFXB_OK;
 }
@@ -953,6 +1182,13 @@ extern "C" int gfxb_session_create(gfxb_engine* engine, const gfxb_session_confi
     status = cuda_check(cudaMallocHost(reinterpret_cast<void**>(&s->pinned), 256 * sizeof(std::uint32_t)),
                         "pinned staging allocation failed");
   }
+  if (status == GFXB_OK && config->step_kernel > GFXB_STEP_PERSISTENT) {
+    status = fail(GFXB_INVALID_ARGUMENT, "unknown step kernel");
+  }
+  if (status == GFXB_OK && config->step_kernel != GFXB_STEP_LAUNCHES) {
+    status = build_token_loop(*s);
+    if (status != GFXB_OK && config->step_kernel == GFXB_STEP_AUTO) status = GFXB_OK;  // per-operation launches
+  }
   if (status == GFXB_OK && config->use_graphs) status = capture_greedy(*s);
   if (status == GFXB_OK) status = cuda_check(cudaStreamSynchronize(s->stream), "session setup failed");
   if (status != GFXB_OK) {
@@ -1015,11 +1251,14 @@ extern "C" int gfxb_session_greedy_step(gfxb_session* session, std::uint32_t inp
   GFXB_TRY(upload_step(s, &input_token, 1));
   if (s.greedy_graph != nullptr) {
     GFXB_TRY(cuda_check(cudaGraphLaunch(s.greedy_graph, s.stream), "graph launch failed"));
-    s.last_hidden = s.hidden[s.e->cfg.layers % 2];
+  } else if (s.loop_ready) {
+    GFXB_TRY(launch_token_loop(s.loop, s.stream));
   } else {
     GFXB_TRY(enqueue_forward(s, 1, s.tokens, s.position, false));
   }
+  s.last_hidden = s.hidden[s.e->cfg.layers % 2];
   GFXB_TRY(download_tokens(s, s.selected, output, 1));
+  GFXB_TRY(check_token_loop(s));
   s.host_position += 1;
   s.have_last_hidden = true;
   s.mtp_chain_active = false;
@@ -1048,7 +1287,8 @@ extern "C" int gfxb_session_enqueue_greedy(gfxb_session* session, std::uint32_t 
 
 extern "C" int gfxb_session_sync(gfxb_session* session) {
   if (session == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null session");
-  return cuda_check(cudaStreamSynchronize(session->stream), "session synchronisation failed");
+  GFXB_TRY(cuda_check(cudaStreamSynchronize(session->stream), "session synchronisation failed"));
+  return check_token_loop(*session);
 }
 
 extern "C" int gfxb_session_last_token(gfxb_session* session, std::uint32_t* token) {

@@ -28,6 +28,12 @@ void set_error_cuda(cudaError_t error, const char* context);
 int fail(int status, const char* message);
 int launch_status(const char* context);
 
+#define GFXB_TRY(expression)                \
+  do {                                      \
+    const int status_ = (expression);       \
+    if (status_ != GFXB_OK) return status_; \
+  } while (0)
+
 #define GFXB_REQUIRE(condition, message) \
   do {                                   \
     if (!(condition)) return ::gfxb::fail(GFXB_INVALID_ARGUMENT, message); \

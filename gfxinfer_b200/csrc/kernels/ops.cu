@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "ops.cuh"
+#include "ops_device.cuh"
 
 namespace gfxb {
 
@@ -17,185 +18,15 @@ __device__ std::uint32_t g_ops_error;
 
 namespace {
 
-__device__ __forceinline__ std::uint32_t fragment_offset(std::uint32_t k) {
-  const std::uint32_t s = k >> 5, rest = k & 31u, half = rest >> 4, t = (rest & 15u) >> 2, j = k & 3u;
-  return t * 32u + s * 8u + half * 4u + j;
-}
-
-
-// Quantize one 128-group held by four consecutive warps (element = thread
-// index within the 128) with the reference A4/A8 rule and store it into a
-// GEMV activation pack. `slot` holds 8 floats of shared scratch per group.
-template <int ActBits>
-__device__ __forceinline__ void pack_group_128(float x, unsigned element, std::int8_t* codes, __half* scale_out,
-                                               std::int32_t* sum_out, float* max_slot, int* sum_slot) {
-  const unsigned lane = element & 31u, warp = element >> 5;
-  float amax = fabsf(x);
-#pragma unroll
-  for (unsigned offset = 16; offset != 0; offset >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
-  if (lane == 0) max_slot[warp] = amax;
-  __syncthreads();
-  amax = fmaxf(fmaxf(max_slot[0], max_slot[1]), fmaxf(max_slot[2], max_slot[3]));
-  constexpr float kDivisor = ActBits == 4 ? 7.0f : 127.0f;
-  constexpr int kLimit = ActBits == 4 ? 7 : 127;
-  const __half scale_h = f2h(amax == 0.0f ? 1.0f : __fdiv_rn(amax, kDivisor));
-  const int q = max(-kLimit, min(kLimit, f2i_rn(__fdiv_rn(x, h2f(scale_h)))));
-  codes[fragment_offset(element)] = static_cast<std::int8_t>(q);
-  int total = q;
-#pragma unroll
-  for (unsigned offset = 16; offset != 0; offset >>= 1) total += __shfl_xor_sync(0xffffffffu, total, offset);
-  if (lane == 0) sum_slot[warp] = total;
-  __syncthreads();
-  if (element == 0) {
-    *scale_out = scale_h;
-    *sum_out = sum_slot[0] + sum_slot[1] + sum_slot[2] + sum_slot[3];
-  }
-}
-
-// ---------------------------------------------------------------------------
-// residual add + RMSNorm (+ activation pack), qwen_ops.hip:31-63, 176-217.
-// One 256-thread CTA per token; thread t owns elements t, t+256, ...; the sum
-// of squares is an fma chain per thread, the warp tree and the tree of the
-// eight warp sums. The normalized fp16 value is quantized per 128-group with
-// the reference's A4/A8 rule (lowbit_gemv.hip:373-436) into a GEMV pack.
-// ---------------------------------------------------------------------------
-
-constexpr unsigned kNormThreads = 256;
-constexpr unsigned kNormMaxIter = 64;  // H <= 16384
-
+// residual add + RMSNorm (+ activation pack): one 256-thread CTA per token.
 template <int ActBits, unsigned Iterations>
 __global__ __launch_bounds__(kNormThreads) void residual_norm_pack_kernel(NormPackArgs args) {
   pdl_trigger();
   pdl_wait();
-  const std::uint32_t token = blockIdx.x;
-  const std::uint32_t H = args.elements;
-  const unsigned t = threadIdx.x, lane = t & 31u, warp = t >> 5;
-  constexpr unsigned iterations = Iterations;
-  const std::size_t row = static_cast<std::size_t>(token) * H;
   __shared__ float warp_sums[8];
   __shared__ float warp_max[Iterations][8];
   __shared__ int warp_code_sums[Iterations][8];
-
-  float values[Iterations];
-  float weights[Iterations];
-  float square_sum = 0.0f;
-  // Every global load is issued before any store: the outputs may alias the
-  // inputs as far as the compiler knows, so interleaving them would serialise
-  // one memory round trip per element.
-#pragma unroll
-  for (unsigned it = 0; it < iterations; ++it) {
-    const std::uint32_t column = it * kNormThreads + t;
-    float scale = bf2f(args.weight[column]);
-    if (args.unit_offset) scale = __fadd_rn(scale, 1.0f);
-    weights[it] = scale;
-  }
-  if (args.embedding_codes != nullptr) {
-    // Embedding row gather fused as the input (lowbit_gemv.hip:158-189, W4/W2 row-major).
-    const std::uint32_t id = args.device_tokens != nullptr ? args.device_tokens[token] : args.host_token;
-    const bool valid = id < args.embedding_rows;
-    const std::uint32_t groups = H / kGroup;
-#pragma unroll
-    for (unsigned it = 0; it < iterations; ++it) {
-      const std::uint32_t column = it * kNormThreads + t;
-      float value = 0.0f;
-      if (valid) {
-        int q;
-        if (args.embedding_bits == 2) {
-          const std::uint8_t packed = args.embedding_codes[static_cast<std::size_t>(id) * (H / 4u) + column / 4u];
-          q = static_cast<int>((packed >> ((column & 3u) * 2u)) & 3u) * 2 - 3;
-        } else {
-          const std::uint8_t packed = args.embedding_codes[static_cast<std::size_t>(id) * (H / 2u) + column / 2u];
-          const int code = (packed >> ((column & 1u) * 4u)) & 15;
-          q = code >= 8 ? code - 16 : code;
-        }
-        value = h2f(f2h(__fmul_rn(static_cast<float>(q),
-                                  h2f(args.embedding_scales[static_cast<std::size_t>(id) * groups + column / kGroup]))));
-      }
-      values[it] = value;
-    }
-    if (args.residual_out != nullptr) {
-#pragma unroll
-      for (unsigned it = 0; it < iterations; ++it) args.residual_out[row + it * kNormThreads + t] = f2h(values[it]);
-    }
-  } else if (args.update != nullptr) {
-    float updates[Iterations];
-#pragma unroll
-    for (unsigned it = 0; it < iterations; ++it) {
-      const std::size_t index = row + it * kNormThreads + t;
-      values[it] = h2f(args.residual[index]);
-      updates[it] = args.update[index];
-    }
-#pragma unroll
-    for (unsigned it = 0; it < iterations; ++it) {
-      const __half rounded = f2h(__fadd_rn(values[it], updates[it]));
-      values[it] = h2f(rounded);
-      if (args.residual_out != nullptr) args.residual_out[row + it * kNormThreads + t] = rounded;
-    }
-  } else {
-#pragma unroll
-    for (unsigned it = 0; it < iterations; ++it) values[it] = h2f(args.residual[row + it * kNormThreads + t]);
-  }
-#pragma unroll
-  for (unsigned it = 0; it < iterations; ++it) square_sum = fmaf(values[it], values[it], square_sum);
-  square_sum = warp_sum_down(square_sum);
-  if (lane == 0) warp_sums[warp] = square_sum;
-  __syncthreads();
-  const float total = tree_of_eight(warp_sums, 8);
-  const float inverse = inv_sqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(H)), args.epsilon));
-#pragma unroll
-  for (unsigned it = 0; it < iterations; ++it) {
-    const std::uint32_t column = it * kNormThreads + t;
-    const __half y = f2h(__fmul_rn(__fmul_rn(values[it], inverse), weights[it]));
-    if (args.normalized_out != nullptr) args.normalized_out[row + column] = y;
-    values[it] = h2f(y);
-  }
-  if constexpr (ActBits != 0) {
-    // groups: element (it, t) belongs to group 2*it + (t >= 128), lane-local index t % 128
-#pragma unroll
-    for (unsigned it = 0; it < iterations; ++it) {
-      float amax = fabsf(values[it]);
-#pragma unroll
-      for (unsigned offset = 16; offset != 0; offset >>= 1) {
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
-      }
-      if (lane == 0) warp_max[it][warp] = amax;
-    }
-    __syncthreads();
-    constexpr float kDivisor = ActBits == 4 ? 7.0f : 127.0f;
-    constexpr int kLimit = ActBits == 4 ? 7 : 127;
-    const unsigned half = warp >> 2;
-    const std::uint32_t groups = H / kGroup;
-#pragma unroll
-    for (unsigned it = 0; it < iterations; ++it) {
-      const float amax = fmaxf(fmaxf(warp_max[it][4 * half], warp_max[it][4 * half + 1]),
-                               fmaxf(warp_max[it][4 * half + 2], warp_max[it][4 * half + 3]));
-      const __half scale_h = f2h(amax == 0.0f ? 1.0f : __fdiv_rn(amax, kDivisor));
-      int q = f2i_rn(__fdiv_rn(values[it], h2f(scale_h)));
-      q = max(-kLimit, min(kLimit, q));
-      const std::uint32_t group = 2u * it + half;
-      const std::uint32_t local = t & 127u;
-      args.act_codes[row + group * kGroup + fragment_offset(local)] = static_cast<std::int8_t>(q);
-      if (ActBits == 4 && args.packed_a4 != nullptr) {
-        const int neighbour = __shfl_down_sync(0xffffffffu, q, 1);
-        if ((local & 1u) == 0) {
-          args.packed_a4[static_cast<std::size_t>(token) * (H / 2u) + group * 64u + local / 2u] =
-              static_cast<std::uint8_t>((q & 0x0f) | ((neighbour & 0x0f) << 4));
-        }
-      }
-      int code_sum = q;
-#pragma unroll
-      for (unsigned offset = 16; offset != 0; offset >>= 1) code_sum += __shfl_xor_sync(0xffffffffu, code_sum, offset);
-      if (lane == 0) warp_code_sums[it][warp] = code_sum;
-      if (local == 0) args.act_scales[static_cast<std::size_t>(token) * groups + group] = scale_h;
-    }
-    __syncthreads();
-    for (std::uint32_t group = t; group < groups; group += kNormThreads) {
-      const unsigned it = group >> 1, h = group & 1u;
-      args.act_sums[static_cast<std::size_t>(token) * groups + group] =
-          warp_code_sums[it][4 * h] + warp_code_sums[it][4 * h + 1] + warp_code_sums[it][4 * h + 2] +
-          warp_code_sums[it][4 * h + 3];
-    }
-  }
+  norm_pack_body<ActBits, Iterations>(args, blockIdx.x, threadIdx.x, BlockSync{}, warp_sums, warp_max, warp_code_sums);
 }
 
 // ---------------------------------------------------------------------------
@@ -213,15 +44,15 @@ __global__ __launch_bounds__(256) void silu_pack_kernel(SiluPackArgs args) {
   if (linear >= groups * args.batch) return;
   const std::uint32_t token = linear / groups, group = linear - token * groups;
   const std::size_t base = static_cast<std::size_t>(token) * args.elements + group * kGroup + 4u * lane;
-  const float4 g4 = *reinterpret_cast<const float4*>(args.gate + base);
-  const float4 u4 = *reinterpret_cast<const float4*>(args.up + base);
+  const float4 g4 = ld_cg_f4(args.gate + base);
+  const float4 u4 = ld_cg_f4(args.up + base);
   const float gs[4] = {g4.x, g4.y, g4.z, g4.w};
   const float us[4] = {u4.x, u4.y, u4.z, u4.w};
   float x[4];
   float amax = 0.0f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const __half product = f2h(__fmul_rn(gx_silu(gs[j]), us[j]));
+    const __half product = silu_product(gs[j], us[j]);
     if (args.product_out != nullptr) args.product_out[base + j] = product;
     x[j] = h2f(product);
     amax = fmaxf(amax, fabsf(x[j]));
@@ -229,16 +60,14 @@ __global__ __launch_bounds__(256) void silu_pack_kernel(SiluPackArgs args) {
   if (args.act_codes == nullptr) return;
 #pragma unroll
   for (unsigned offset = 16; offset != 0; offset >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
-  constexpr float kDivisor = ActBits == 4 ? 7.0f : 127.0f;
-  constexpr int kLimit = ActBits == 4 ? 7 : 127;
-  const __half scale_h = f2h(amax == 0.0f ? 1.0f : __fdiv_rn(amax, kDivisor));
+  const __half scale_h = act_scale_of<ActBits>(amax);
   const float scale = h2f(scale_h);
   std::uint32_t word = 0;
   int code_sum = 0;
   int q[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    q[j] = max(-kLimit, min(kLimit, f2i_rn(__fdiv_rn(x[j], scale))));
+    q[j] = act_code_of<ActBits>(x[j], scale);
     word |= (static_cast<std::uint32_t>(q[j]) & 0xffu) << (8 * j);
     code_sum += q[j];
   }
@@ -275,17 +104,9 @@ __global__ void gdn_conv_kernel(GdnConvArgs args) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) w[i] = bf2f(args.weight[static_cast<std::size_t>(channel) * 4u + i]);
   for (std::uint32_t token = 0; token < args.batch; ++token) {
-    taps[0] = taps[1];
-    taps[1] = taps[2];
-    taps[2] = taps[3];
-    taps[3] = f2h(args.projected[static_cast<std::size_t>(token) * args.channels + channel]);
-    if (args.appended_log != nullptr) {
-      args.appended_log[static_cast<std::size_t>(token) * args.channels + channel] = taps[3];
-    }
-    float conv = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) conv = fmaf(h2f(taps[i]), w[i], conv);
-    args.output[static_cast<std::size_t>(token) * args.channels + channel] = f2h(gx_silu(conv));
+    const std::size_t index = static_cast<std::size_t>(token) * args.channels + channel;
+    args.output[index] = gdn_conv_step(taps, w, ld_cg(args.projected + index));
+    if (args.appended_log != nullptr) args.appended_log[index] = taps[3];
   }
   __half* final_state = args.final_state + static_cast<std::size_t>(channel) * 4u;
 #pragma unroll
@@ -301,96 +122,15 @@ __global__ void gdn_conv_kernel(GdnConvArgs args) {
 // and SiLU(z) gate.
 // ---------------------------------------------------------------------------
 
-__global__ __launch_bounds__(128) void gdn_recurrent_kernel(GdnRecurrentArgs args) {
+__global__ __launch_bounds__(kGdnThreads) void gdn_recurrent_kernel(GdnRecurrentArgs args) {
   pdl_trigger();
   pdl_wait();
-  constexpr unsigned kHead = 128;
-  const unsigned vh = blockIdx.x, v = threadIdx.x, lane = v & 31u, warp = v >> 5;
-  const unsigned ratio = args.value_heads / args.key_heads;
-  const unsigned kh = vh / ratio;
-  const unsigned key_elements = args.key_heads * kHead;
-  const unsigned value_elements = args.value_heads * kHead;
-  const unsigned channels = 2u * key_elements + value_elements;
-  __shared__ float query[kHead];
-  __shared__ float key[kHead];
-  __shared__ float sums[3][4];
-  __shared__ float pack_max[4];
-  __shared__ int pack_sum[4];
-
-  float S[kHead];
-  const float* initial = args.initial_state + static_cast<std::size_t>(vh) * kHead * kHead;
-#pragma unroll
-  for (unsigned k = 0; k < kHead; ++k) S[k] = initial[k * kHead + v];
-  const float a_log = bf2f(args.a_log[vh]);
-  const float dt_bias = bf2f(args.dt_bias[vh]);
-  const float norm_weight = bf2f(args.norm_weight[v]);
-
-  for (std::uint32_t t = 0; t < args.batch; ++t) {
-    const __half* qkv = args.qkv + static_cast<std::size_t>(t) * channels;
-    const float q = h2f(qkv[kh * kHead + v]);
-    const float k = h2f(qkv[key_elements + kh * kHead + v]);
-    const float qs = warp_sum_down(__fmul_rn(q, q));
-    const float ks = warp_sum_down(__fmul_rn(k, k));
-    if (lane == 0) {
-      sums[0][warp] = qs;
-      sums[1][warp] = ks;
-    }
-    __syncthreads();
-    const float inv_q = __fmul_rn(inv_sqrt_rn(__fadd_rn(tree_of_eight(sums[0], 4), 1.0e-6f)), 0.08838834764831845f);
-    const float inv_k = inv_sqrt_rn(__fadd_rn(tree_of_eight(sums[1], 4), 1.0e-6f));
-    const std::uint32_t ab_stride = args.ab_stride != 0 ? args.ab_stride : args.value_heads;
-    const float a_value = __fadd_rn(args.a[static_cast<std::size_t>(t) * ab_stride + vh], dt_bias);
-    const float softplus = a_value > 20.0f ? a_value : gx_log1pf(gx_expf(a_value));
-    const float g = __fmul_rn(-gx_expf(a_log), softplus);
-    const float decay = gx_expf(g);
-    const float beta = gx_sigmoid(args.b[static_cast<std::size_t>(t) * ab_stride + vh]);
-    const float kn = __fmul_rn(k, inv_k);
-    query[v] = __fmul_rn(q, inv_q);
-    key[v] = kn;
-    if (args.decay_log != nullptr && v == 0) args.decay_log[static_cast<std::size_t>(t) * args.value_heads + vh] = decay;
-    if (args.key_log != nullptr && vh % ratio == 0) {
-      args.key_log[static_cast<std::size_t>(t) * key_elements + kh * kHead + v] = kn;
-    }
-    __syncthreads();
-    float memory = 0.0f;
-#pragma unroll
-    for (unsigned kk = 0; kk < kHead; ++kk) {
-      S[kk] = __fmul_rn(S[kk], decay);
-      memory = fmaf(S[kk], key[kk], memory);
-    }
-    const float value = h2f(qkv[2u * key_elements + vh * kHead + v]);
-    const float delta = __fmul_rn(__fsub_rn(value, memory), beta);
-    if (args.delta_log != nullptr) {
-      args.delta_log[static_cast<std::size_t>(t) * value_elements + vh * kHead + v] = delta;
-    }
-    float mixed = 0.0f;
-#pragma unroll
-    for (unsigned kk = 0; kk < kHead; ++kk) {
-      S[kk] = fmaf(key[kk], delta, S[kk]);
-      mixed = fmaf(S[kk], query[kk], mixed);
-    }
-    const float os = warp_sum_down(__fmul_rn(mixed, mixed));
-    if (lane == 0) sums[2][warp] = os;
-    __syncthreads();
-    const float inv_o = inv_sqrt_rn(__fadd_rn(__fdiv_rn(tree_of_eight(sums[2], 4), 128.0f), 1.0e-6f));
-    const float z = args.z[static_cast<std::size_t>(t) * value_elements + vh * kHead + v];
-    const float normalized = __fmul_rn(__fmul_rn(mixed, inv_o), norm_weight);
-    const __half y = f2h(__fmul_rn(normalized, gx_silu(z)));
-    args.output[static_cast<std::size_t>(t) * value_elements + vh * kHead + v] = y;
-    if (args.act_bits != 0) {
-      const std::size_t row = static_cast<std::size_t>(t) * value_elements + vh * kHead;
-      const std::size_t group = static_cast<std::size_t>(t) * args.value_heads + vh;
-      if (args.act_bits == 8) {
-        pack_group_128<8>(h2f(y), v, args.act_codes + row, args.act_scales + group, args.act_sums + group, pack_max, pack_sum);
-      } else {
-        pack_group_128<4>(h2f(y), v, args.act_codes + row, args.act_scales + group, args.act_sums + group, pack_max, pack_sum);
-      }
-    }
-    __syncthreads();  // query/key/sums are rewritten by the next token
-  }
-  float* final_state = args.final_state + static_cast<std::size_t>(vh) * kHead * kHead;
-#pragma unroll
-  for (unsigned k = 0; k < kHead; ++k) final_state[k * kHead + v] = S[k];
+  __shared__ GdnScratch scratch;
+  const unsigned vh = blockIdx.x, t = threadIdx.x;
+  float S[kGdnRows];
+  gdn_load_state(args, vh, t, S);
+  gdn_recurrent_tokens(args, vh, t, S, BlockSync{}, scratch);
+  gdn_store_state(args, vh, t, S);
 }
 
 // Rollback replay (qwen_ops.hip:467-539): conv inputs and delta-rule updates of
@@ -452,33 +192,17 @@ __global__ __launch_bounds__(256) void qk_norm_rope_kernel(QkRopeArgs args) {
   const unsigned token = blockIdx.x / heads, local = blockIdx.x % heads;
   const bool is_key = local >= args.q_heads;
   const unsigned head = is_key ? local - args.q_heads : local;
-  const unsigned d = threadIdx.x, lane = d & 31u, warp = d >> 5;
+  const unsigned d = threadIdx.x;
   const std::uint64_t base = args.device_base_position != nullptr ? *args.device_base_position : args.base_position;
   const std::uint64_t position = base + token;
   const float* input = is_key ? args.k_input + (static_cast<std::size_t>(token) * args.k_heads + head) * args.k_stride
                               : args.q_input + (static_cast<std::size_t>(token) * args.q_heads + head) * args.q_stride;
-  const std::uint16_t* weight = is_key ? args.k_weight : args.q_weight;
   __shared__ float normalized[256];
   __shared__ float warp_sums[8];
-  const float value = input[d];
-  const float square = warp_sum_down(__fmul_rn(value, value));
-  if (lane == 0) warp_sums[warp] = square;
-  __syncthreads();
-  const float inverse = inv_sqrt_rn(__fadd_rn(__fdiv_rn(tree_of_eight(warp_sums, 8), 256.0f), 1.0e-6f));
-  normalized[d] = __fmul_rn(value, __fmul_rn(inverse, __fadd_rn(1.0f, bf2f(weight[d]))));
-  __syncthreads();
-  float out = normalized[d];
-  const unsigned half = args.rotary / 2u;
-  if (d < args.rotary) {
-    const bool in_range = position < args.table_positions;
-    if (!in_range && d == 0) atomicOr(&g_ops_error, 2u);
-    const std::uint64_t p = in_range ? position : 0;
-    const unsigned f = d % half;
-    const float partner = d < half ? normalized[d + half] : normalized[d - half];
-    const float rotated = d < half ? -partner : partner;
-    out = fmaf(out, args.cos_table[p * half + f], __fmul_rn(rotated, args.sin_table[p * half + f]));
-  }
-  const __half result = f2h(out);
+  bool out_of_range = false;
+  const __half result = qk_norm_rope_value(ld_cg(input + d), is_key ? args.k_weight : args.q_weight, position, args, d,
+                                           BlockSync{}, normalized, warp_sums, out_of_range);
+  if (out_of_range && d == 0) atomicOr(&g_ops_error, 2u);
   if (!is_key) {
     args.q_output[(static_cast<std::size_t>(token) * args.q_heads + head) * 256u + d] = result;
     return;
@@ -491,7 +215,7 @@ __global__ __launch_bounds__(256) void qk_norm_rope_kernel(QkRopeArgs args) {
     }
     const std::size_t slot = (static_cast<std::size_t>(position) * args.k_heads + head) * 256u + d;
     args.key_cache[slot] = result;
-    args.value_cache[slot] = f2h(args.v_input[(static_cast<std::size_t>(token) * args.k_heads + head) * 256u + d]);
+    args.value_cache[slot] = f2h(ld_cg(args.v_input + (static_cast<std::size_t>(token) * args.k_heads + head) * 256u + d));
   }
 }
 
@@ -531,91 +255,11 @@ __global__ __launch_bounds__(256) void attention_chunk_kernel(AttentionArgs args
     if (lane == 0) atomicOr(&g_ops_error, 8u);
     return;
   }
-  const __half* q = args.query + (static_cast<std::size_t>(token) * args.q_heads + h) * 256u + 8u * lane;
-  float qf[8];
-  {
-    const uint4 raw = *reinterpret_cast<const uint4*>(q);
-    const __half* hv = reinterpret_cast<const __half*>(&raw);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) qf[j] = h2f(hv[j]);
-  }
   const std::size_t row_stride = static_cast<std::size_t>(args.kv_heads) * 256u;
-  const __half* keys = args.key_cache + (begin * args.kv_heads + kvh) * 256u + 8u * lane;
-  // eight key rows in flight per step; positions past n read row 0 (valid) and are dropped
-  for (std::uint32_t p0 = 0; p0 < n; p0 += 8) {
-    uint4 raw[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const std::uint32_t p = p0 + i < n ? p0 + i : 0u;
-      raw[i] = *reinterpret_cast<const uint4*>(keys + p * row_stride);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const __half* hv = reinterpret_cast<const __half*>(&raw[i]);
-      float s = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) s = fmaf(qf[j], h2f(hv[j]), s);
-      s = warp_sum_xor(s);
-      if (lane == 0 && p0 + i < n) scores[warp][p0 + i] = __fmul_rn(s, 0.0625f);
-    }
-  }
-  __syncwarp();
-  // prefix maximum: lane owns positions 4l..4l+3
-  float local_max[4];
-  float running = -__int_as_float(0x7f800000);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const std::uint32_t p = 4u * lane + j;
-    if (p < n) running = fmaxf(running, scores[warp][p]);
-    local_max[j] = running;
-  }
-  float exclusive = __shfl_up_sync(0xffffffffu, running, 1);
-  if (lane == 0) exclusive = -__int_as_float(0x7f800000);
-#pragma unroll
-  for (unsigned offset = 1; offset < 32; offset <<= 1) {
-    const float other = __shfl_up_sync(0xffffffffu, exclusive, offset);
-    if (lane >= offset) exclusive = fmaxf(exclusive, other);
-  }
-  float previous = exclusive;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const std::uint32_t p = 4u * lane + j;
-    const float m = fmaxf(exclusive, local_max[j]);
-    if (p < n) {
-      alphas[warp][p] = gx_expf(__fsub_rn(previous, m));
-      betas[warp][p] = gx_expf(__fsub_rn(scores[warp][p], m));
-    }
-    previous = m;
-  }
-  const float chunk_max = __shfl_sync(0xffffffffu, previous, 31);
-  __syncwarp();
-  float den = 0.0f;
-  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  const __half* values = args.value_cache + (begin * args.kv_heads + kvh) * 256u + 8u * lane;
-  for (std::uint32_t p0 = 0; p0 < n; p0 += 8) {
-    uint4 raw[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const std::uint32_t p = p0 + i < n ? p0 + i : 0u;
-      raw[i] = *reinterpret_cast<const uint4*>(values + p * row_stride);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (p0 + i < n) {
-        const float alpha = alphas[warp][p0 + i], beta = betas[warp][p0 + i];
-        const __half* hv = reinterpret_cast<const __half*>(&raw[i]);
-        den = __fadd_rn(__fmul_rn(den, alpha), beta);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(__fmul_rn(acc[j], alpha), __fmul_rn(h2f(hv[j]), beta));
-      }
-    }
-  }
-  if (lane == 0) {
-    partial[0] = chunk_max;
-    partial[1] = den;
-  }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) partial[2 + 8 * lane + j] = acc[j];
+  attention_chunk_warp(args.query + (static_cast<std::size_t>(token) * args.q_heads + h) * 256u,
+                       args.key_cache + (begin * args.kv_heads + kvh) * 256u,
+                       args.value_cache + (begin * args.kv_heads + kvh) * 256u, row_stride, n, lane, scores[warp],
+                       alphas[warp], betas[warp], partial);
 }
 
 __global__ __launch_bounds__(256) void attention_merge_kernel(AttentionArgs args) {
@@ -627,35 +271,9 @@ __global__ __launch_bounds__(256) void attention_merge_kernel(AttentionArgs args
   const std::uint64_t count = base + token;
   if (count > args.capacity) return;
   const std::uint32_t chunks = static_cast<std::uint32_t>((count + kChunk - 1) / kChunk);
-  const float* partial = args.partials + (static_cast<std::size_t>(token) * args.q_heads + h) * args.max_chunks * 258u;
-  float M = partial[0], Den = partial[1], Acc = partial[2 + d];
-  for (std::uint32_t c = 1; c < chunks; ++c) {
-    const float* p = partial + static_cast<std::size_t>(c) * 258u;
-    const float m = p[0];
-    const float next = fmaxf(M, m);
-    const float a1 = gx_expf(__fsub_rn(M, next));
-    const float a2 = gx_expf(__fsub_rn(m, next));
-    Den = __fadd_rn(__fmul_rn(Den, a1), __fmul_rn(p[1], a2));
-    Acc = __fadd_rn(__fmul_rn(Acc, a1), __fmul_rn(p[2 + d], a2));
-    M = next;
-  }
-  const float gate = args.gate[(static_cast<std::size_t>(token) * args.q_heads + h) * 512u + 256u + d];
-  const __half y = f2h(__fmul_rn(__fdiv_rn(Acc, Den), gx_sigmoid(gate)));
-  args.output[(static_cast<std::size_t>(token) * args.q_heads + h) * 256u + d] = y;
-  if (args.act_bits != 0) {
-    __shared__ float pack_max[2][4];
-    __shared__ int pack_sum[2][4];
-    const unsigned half = d >> 7, element = d & 127u;
-    const std::size_t row = (static_cast<std::size_t>(token) * args.q_heads + h) * 256u + half * 128u;
-    const std::size_t group = static_cast<std::size_t>(token) * args.q_heads * 2u + h * 2u + half;
-    if (args.act_bits == 8) {
-      pack_group_128<8>(h2f(y), element, args.act_codes + row, args.act_scales + group, args.act_sums + group,
-                        pack_max[half], pack_sum[half]);
-    } else {
-      pack_group_128<4>(h2f(y), element, args.act_codes + row, args.act_scales + group, args.act_sums + group,
-                        pack_max[half], pack_sum[half]);
-    }
-  }
+  __shared__ float pack_max[2][4];
+  __shared__ int pack_sum[2][4];
+  attention_merge_head(args, h, token, d, chunks, BlockSync{}, pack_max, pack_sum);
 }
 
 // ---------------------------------------------------------------------------
@@ -665,12 +283,6 @@ __global__ __launch_bounds__(256) void attention_merge_kernel(AttentionArgs args
 
 constexpr unsigned kArgmaxBlocks = 64;
 
-__device__ __forceinline__ void better(float& best, std::uint32_t& index, float value, std::uint32_t other) {
-  if (value > best || (value == best && other < index)) {
-    best = value;
-    index = other;
-  }
-}
 
 __global__ __launch_bounds__(256) void argmax_partial_kernel(ArgmaxArgs args) {
   pdl_trigger();
@@ -809,7 +421,7 @@ int launch_gdn_recurrent(const GdnRecurrentArgs& args, cudaStream_t stream) {
       args.value_heads == 0 || args.value_heads % args.key_heads != 0) {
     return fail(GFXB_INVALID_ARGUMENT, "invalid GDN recurrent arguments");
   }
-  launch_kernel(gdn_recurrent_kernel, dim3(args.value_heads), dim3(128), 0, stream, 0, args);
+  launch_kernel(gdn_recurrent_kernel, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, 0, args);
   return launch_status("GDN recurrent launch failed");
 }
 

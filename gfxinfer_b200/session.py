@@ -103,9 +103,11 @@ class QwenDecodeSession:
 
     @classmethod
     def create(cls, engine: Engine, maximum_context_tokens: int | None = None, graph_verifier_batch: int = 0,
-               use_graphs: bool = True) -> "QwenDecodeSession":
+               use_graphs: bool = True, step_kernel: int = abi.STEP_AUTO) -> "QwenDecodeSession":
+        """step_kernel: abi.STEP_AUTO (persistent token kernel where supported), abi.STEP_LAUNCHES
+        (per-operation kernels) or abi.STEP_PERSISTENT (token kernel or GFXB_UNSUPPORTED)."""
         ctx = maximum_context_tokens or engine.config.max_context
-        config = abi.SessionConfig(ctx, graph_verifier_batch, int(use_graphs))
+        config = abi.SessionConfig(ctx, graph_verifier_batch, int(use_graphs), step_kernel)
         handle = ctypes.c_void_p()
         check(lib().gfxb_session_create(engine.handle, ctypes.byref(config), ctypes.byref(handle)))
         return cls(handle.value, engine)

@@ -247,7 +247,17 @@ typedef struct {
   uint32_t maximum_context_tokens;
   uint32_t graph_verifier_batch; /* 0: no speculative graph; else drafts + 1 */
   uint32_t use_graphs;           /* capture the greedy step in a CUDA graph */
+  uint32_t step_kernel;          /* GFXB_STEP_*: how a batch-1 greedy step runs */
 } gfxb_session_config;
+
+/* Batch-1 greedy step execution. AUTO uses the persistent token kernel (one
+ * launch per token: every layer, the LM head and the argmax, with the weight
+ * stream running ahead across layers) where the session supports it (one
+ * GPU, hidden size 256 x {4, 8, 16, 20}) and the per-operation launches
+ * otherwise; LAUNCHES always uses the per-operation kernels; PERSISTENT fails
+ * session creation with GFXB_UNSUPPORTED where the token kernel cannot run.
+ * Both paths produce identical bits. */
+enum { GFXB_STEP_AUTO = 0, GFXB_STEP_LAUNCHES = 1, GFXB_STEP_PERSISTENT = 2 };
 
 int gfxb_session_create(gfxb_engine* engine, const gfxb_session_config* config, gfxb_session** session);
 int gfxb_session_destroy(gfxb_session* session);
