@@ -387,6 +387,7 @@ struct gfxb_session {
   gfxb::LoopControl* loop_control = nullptr;
   gfxb::LoopLaunch loop{};
   bool loop_ready = false;
+  std::uint64_t* loop_trace = nullptr;  // timeline buffer, allocated on the first traced step
 };
 
 namespace gfxb {
@@ -926,12 +927,6 @@ int build_token_loop(gfxb_session& s) {
   launch.act_bits = c.activation_bits;
   GFXB_TRY(plan_token_loop(launch, max_groups, dots_half, e.device));
   if (launch.ctas != ctas) return fail(GFXB_INTERNAL, "token kernel grid changed");
-  for (const LoopOp& op : ops) {
-    if (op.kind != kLoopGemv) continue;
-    if (token_loop_unit_slots(op.gemv.bits, op.gemv.groups, op.gemv.paired != 0) > launch.slots) {
-      return fail(GFXB_UNSUPPORTED, "token kernel: a weight tile does not fit the ring");
-    }
-  }
   GFXB_TRY(cuda_check(cudaMemcpyAsync(s.loop_ops, ops.data(), ops.size() * sizeof(LoopOp), cudaMemcpyHostToDevice,
                                       s.stream),
                       "token kernel operation upload failed"));
@@ -1185,10 +1180,7 @@ extern "C" int gfxb_session_create(gfxb_engine* engine, const gfxb_session_confi
   if (status == GFXB_OK && config->step_kernel > GFXB_STEP_PERSISTENT) {
     status = fail(GFXB_INVALID_ARGUMENT, "unknown step kernel");
   }
-  if (status == GFXB_OK && config->step_kernel != GFXB_STEP_LAUNCHES) {
-    status = build_token_loop(*s);
-    if (status != GFXB_OK && config->step_kernel == GFXB_STEP_AUTO) status = GFXB_OK;  // per-operation launches
-  }
+  if (status == GFXB_OK && config->step_kernel == GFXB_STEP_PERSISTENT) status = build_token_loop(*s);
   if (status == GFXB_OK && config->use_graphs) status = capture_greedy(*s);
   if (status == GFXB_OK) status = cuda_check(cudaStreamSynchronize(s->stream), "session setup failed");
   if (status != GFXB_OK) {
@@ -1207,6 +1199,7 @@ extern "C" int gfxb_session_destroy(gfxb_session* session) {
   cudaStreamSynchronize(session->stream);
   if (session->greedy_graph) cudaGraphExecDestroy(session->greedy_graph);
   if (session->pinned) cudaFreeHost(session->pinned);
+  if (session->loop_trace) cudaFree(session->loop_trace);
   cudaFree(session->arena);
   delete session;
   return GFXB_OK;
@@ -1482,6 +1475,53 @@ extern "C" int gfxb_session_enqueue_gemv(gfxb_session* session, int kind, unsign
     }
   }
   if (bytes != nullptr) *bytes = total;
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_session_trace_step(gfxb_session* session, std::uint32_t input_token, std::uint32_t* output_token,
+                                       std::uint64_t* timeline, std::size_t timeline_entries, unsigned* op_count,
+                                       unsigned* ctas, std::uint32_t* op_kinds) {
+  if (session == nullptr || output_token == nullptr || op_count == nullptr || ctas == nullptr) {
+    return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  }
+  gfxb_session& s = *session;
+  if (!s.loop_ready) return fail(GFXB_UNSUPPORTED, "the session does not run the persistent token kernel");
+  *op_count = s.loop.op_count;
+  *ctas = s.loop.ctas;
+  const std::size_t entries = (static_cast<std::size_t>(s.loop.op_count) + 1u) * 2u * s.loop.ctas;
+  if (timeline == nullptr || timeline_entries < entries) {
+    return fail(GFXB_INVALID_ARGUMENT, "timeline buffer must hold (op_count + 1) * 2 * ctas entries");
+  }
+  if (s.host_position >= s.cfg.maximum_context_tokens || input_token >= s.e->cfg.vocab) {
+    return fail(GFXB_INVALID_ARGUMENT, "decode token or session position is invalid");
+  }
+  cudaSetDevice(s.e->device);
+  if (s.loop_trace == nullptr) {
+    GFXB_TRY(cuda_check(cudaMalloc(reinterpret_cast<void**>(&s.loop_trace), entries * sizeof(std::uint64_t)),
+                        "timeline allocation failed"));
+  }
+  GFXB_TRY(cuda_check(cudaMemsetAsync(s.loop_trace, 0, entries * sizeof(std::uint64_t), s.stream), "timeline reset failed"));
+  GFXB_TRY(upload_step(s, &input_token, 1));
+  LoopLaunch traced = s.loop;
+  traced.trace = s.loop_trace;
+  GFXB_TRY(launch_token_loop(traced, s.stream));
+  s.last_hidden = s.hidden[s.e->cfg.layers % 2];
+  GFXB_TRY(download_tokens(s, s.selected, output_token, 1));
+  GFXB_TRY(check_token_loop(s));
+  s.host_position += 1;
+  s.have_last_hidden = true;
+  s.mtp_chain_active = false;
+  GFXB_TRY(cuda_check(cudaMemcpy(timeline, s.loop_trace, entries * sizeof(std::uint64_t), cudaMemcpyDeviceToHost),
+                      "timeline download failed"));
+  if (op_kinds != nullptr) {
+    std::vector<LoopOp> ops(s.loop.op_count);
+    GFXB_TRY(cuda_check(cudaMemcpy(ops.data(), s.loop_ops, ops.size() * sizeof(LoopOp), cudaMemcpyDeviceToHost),
+                        "operation list download failed"));
+    for (std::size_t i = 0; i < ops.size(); ++i) {
+      op_kinds[i] = ops[i].kind == kLoopGemv ? (ops[i].gemv.bits << 8) | (ops[i].gemv.act_source << 4) | kLoopGemv
+                                             : ops[i].kind;
+    }
+  }
   return GFXB_OK;
 }
 

@@ -1,15 +1,16 @@
 // Persistent token kernel (see token_loop.cuh for the design).
 //
-// Ring protocol. Slot s of the shared-memory ring carries a `full` mbarrier
-// (producer arrival + bulk-copy bytes) and an `empty` mbarrier (one arrival
-// per compute warp). Producer and compute warps walk the same sequence of
-// slot uses: for every GEMV operation, for each of this CTA's units, for
-// each matrix tile of the unit, one slot with the tile's fp16 scales and
-// then ceil(G / groups-per-slot) slots of weight codes. A compute warp waits
-// for `full` before it reads a slot and arrives on `empty` after, even when
-// the slot holds none of its groups, so a slot is refilled only after every
-// warp is done with it. The scale slot is released by the warp that runs the
-// tile's fp32 chain.
+// Ring protocol. Slot s of the code ring carries a `full` mbarrier (issuing
+// lane's arrival + bulk-copy bytes) and an `empty` mbarrier (one arrival per
+// compute warp). Producer lanes and compute warps walk the same sequence of
+// slot uses: for every GEMV operation, for each of this CTA's units, for each
+// matrix tile of the unit, ceil(G / groups-per-slot) slots of weight codes;
+// use n is issued by producer n % kLoopProducerLanes. A compute warp
+// waits for `full` before it reads a slot and arrives on `empty` after, even
+// when the slot holds none of its groups, so a slot is refilled only after
+// every warp is done with it. Each tile's fp16 scales travel through the
+// scale ring (same protocol, one `empty` arrival: the warp that runs the
+// tile's fp32 chain releases it).
 //
 // Every wait is bounded by the global timer. A wait that expires sets the
 // control block's abort word; every later wait of every CTA then returns at
@@ -27,6 +28,7 @@ namespace gfxb {
 namespace {
 
 constexpr std::uint64_t kLoopWaitNs = 1000000000ull;  // 1 s, far above any legitimate wait
+
 
 using ComputeSync = NamedSync<1, kLoopComputeThreads>;
 
@@ -75,15 +77,17 @@ __device__ __forceinline__ uint2 ld_cg8(const void* p) {
 __device__ __forceinline__ void mbar_arrive(std::uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive_count(std::uint64_t* bar, std::uint32_t count) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
 
 struct Ctx {
   LoopControl* ctl;
   std::uint8_t* ring;
   std::uint64_t* full;
   std::uint64_t* empty;
+  std::uint8_t* scale_ring;
+  std::uint64_t* scale_full;
+  std::uint64_t* scale_empty;
+  std::uint32_t scale_slot_bytes;
+  std::uint32_t sn;            // scale-ring position
   std::int8_t* act_codes;
   __half* act_scales;
   std::int32_t* act_sums;
@@ -94,7 +98,13 @@ struct Ctx {
   std::uint32_t n;             // ring position
   std::uint32_t unit_counter;  // GEMV units done by this CTA
   volatile std::uint32_t* abort;
+  std::uint64_t* trace;        // LoopLaunch::trace
 };
+
+// Timeline entry (see LoopLaunch::trace); thread 0 only.
+__device__ __forceinline__ void trace_mark(const Ctx& c, std::uint32_t op, std::uint32_t which) {
+  if (c.trace != nullptr) c.trace[(2ull * op + which) * c.ctas + c.cta] = global_ns();
+}
 
 __device__ __forceinline__ std::uint32_t first_unit(const Ctx& c, std::uint32_t rotation) {
   return (c.cta + c.ctas - rotation % c.ctas) % c.ctas;
@@ -122,25 +132,37 @@ __device__ __forceinline__ void raise_abort(Ctx& c, std::uint32_t error) {
   *c.abort = 1u;
 }
 
-// Warp-uniform bounded wait for a ring slot's `full` phase.
-__device__ __forceinline__ bool ring_wait(Ctx& c, std::uint32_t slot, std::uint32_t round, unsigned lane) {
+// Another CTA's abort is polled from global memory at most every
+// kLoopAbortPollNs while a wait lasts: a global load on every spin would
+// delay each wake-up by an L2 round trip.
+constexpr std::uint64_t kLoopAbortPollNs = 20000;
+
+// Warp-uniform bounded wait for a ring slot's `full` phase (`round`: the slot's use count).
+__device__ __forceinline__ bool ring_wait(Ctx& c, std::uint64_t* bar, std::uint32_t round, unsigned lane) {
   if (*c.abort != 0) return false;
-  std::uint64_t* bar = &c.full[slot];
   const std::uint32_t parity = round & 1u;
-  std::uint64_t start = 0;
+  std::uint64_t start = 0, next_poll = 0;
   for (std::uint32_t spin = 0;; ++spin) {
     const bool done = mbar_try_wait(bar, parity);
     if (__all_sync(0xffffffffu, done)) return true;
     std::uint32_t stop = 0;
     if (lane == 0) {
       const std::uint64_t now = global_ns();
-      if (spin == 0) start = now;
-      if (*c.abort != 0 || ld_volatile(&c.ctl->abort) != 0) {
-        *c.abort = 1u;
+      if (spin == 0) {
+        start = now;
+        next_poll = now + kLoopAbortPollNs;
+      }
+      if (*c.abort != 0) {
         stop = 1;
-      } else if (now - start > kLoopWaitNs) {
-        raise_abort(c, kLoopErrorRing);
-        stop = 1;
+      } else if (now >= next_poll) {
+        next_poll = now + kLoopAbortPollNs;
+        if (ld_volatile(&c.ctl->abort) != 0) {
+          *c.abort = 1u;
+          stop = 1;
+        } else if (now - start > kLoopWaitNs) {
+          raise_abort(c, kLoopErrorRing);
+          stop = 1;
+        }
       }
     }
     if (__shfl_sync(0xffffffffu, stop, 0) != 0) return false;
@@ -149,80 +171,105 @@ __device__ __forceinline__ bool ring_wait(Ctx& c, std::uint32_t slot, std::uint3
 
 // Grid barrier over all CTAs (compute warps only). Returns false once the
 // step is aborted.
-__device__ __forceinline__ bool grid_barrier(Ctx& c, std::uint32_t target) {
+__device__ __forceinline__ bool grid_barrier(Ctx& c, std::uint32_t target, std::uint32_t op) {
   ComputeSync{}();
+  if (threadIdx.x == 0) trace_mark(c, op, 0);
   if (threadIdx.x == 0 && *c.abort == 0) {
     __threadfence();
     atomicAdd(&c.ctl->arrive, 1u);
     const std::uint64_t start = global_ns();
+    std::uint64_t next_poll = start + kLoopAbortPollNs;
     while (true) {
       const std::uint32_t v = ld_acquire(&c.ctl->arrive);
       if (static_cast<std::int32_t>(v - target) >= 0) break;
-      if (ld_volatile(&c.ctl->abort) != 0) {
-        *c.abort = 1u;
-        break;
-      }
-      if (global_ns() - start > kLoopWaitNs) {
-        raise_abort(c, kLoopErrorBarrier);
-        break;
+      const std::uint64_t now = global_ns();
+      if (now >= next_poll) {
+        next_poll = now + kLoopAbortPollNs;
+        if (ld_volatile(&c.ctl->abort) != 0) {
+          *c.abort = 1u;
+          break;
+        }
+        if (now - start > kLoopWaitNs) {
+          raise_abort(c, kLoopErrorBarrier);
+          break;
+        }
       }
     }
     __threadfence();
   }
+  if (threadIdx.x == 0) trace_mark(c, op, 1);
   ComputeSync{}();
   return *c.abort == 0;
 }
 
 // ---------------------------------------------------------------------------
-// producer: lane 0 of the last warp
+// producers: lane 0 of each of the last kLoopProducerLanes warps
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ bool producer_wait(Ctx& c, std::uint64_t* bar, std::uint32_t parity, bool honour_abort) {
   const std::uint64_t start = global_ns();
+  std::uint64_t next_poll = start + kLoopAbortPollNs;
   while (!mbar_try_wait(bar, parity)) {
-    if (honour_abort && (*c.abort != 0 || ld_volatile(&c.ctl->abort) != 0)) return false;
-    if (global_ns() - start > kLoopWaitNs) {
-      raise_abort(c, kLoopErrorRing);
-      return false;
+    if (honour_abort && *c.abort != 0) return false;
+    const std::uint64_t now = global_ns();
+    if (now >= next_poll) {
+      next_poll = now + kLoopAbortPollNs;
+      if (honour_abort && ld_volatile(&c.ctl->abort) != 0) return false;
+      if (now - start > kLoopWaitNs) {
+        raise_abort(c, kLoopErrorRing);
+        return false;
+      }
     }
   }
   return true;
 }
 
-__device__ __forceinline__ void produce(const LoopLaunch& L, Ctx& c) {
-  std::uint32_t issued = 0;
+// Groups of weight codes one code slot carries.
+__device__ __forceinline__ std::uint32_t groups_per_slot(std::uint32_t bits) { return kLoopSlotBytes / (bits * 256u); }
+
+// Every producer walks the whole copy sequence and issues the copies it owns
+// (sequence position % kLoopProducerLanes == lane, `lane` = producer index).
+__device__ __forceinline__ void produce(const LoopLaunch& L, Ctx& c, unsigned lane) {
+  std::uint32_t code_n = 0, scale_n = 0;
   bool ok = true;
-  auto issue = [&](const void* source, std::uint32_t bytes) {
-    const std::uint32_t slot = issued % c.slots, round = issued / c.slots;
-    if (round > 0 && !producer_wait(c, &c.empty[slot], (round - 1u) & 1u, true)) {
+  auto issue = [&](std::uint32_t n, std::uint32_t slots, std::uint64_t* full, std::uint64_t* empty,
+                   std::uint8_t* ring, std::uint32_t slot_bytes, const void* source, std::uint32_t bytes) {
+    if (!ok || n % kLoopProducerLanes != lane) return;
+    const std::uint32_t slot = n % slots, round = n / slots;
+    if (round > 0 && !producer_wait(c, &empty[slot], (round - 1u) & 1u, true)) {
       ok = false;
       return;
     }
-    mbar_expect_tx(&c.full[slot], bytes);
-    bulk_g2s(c.ring + static_cast<std::size_t>(slot) * kLoopSlotBytes, source, bytes, &c.full[slot]);
-    ++issued;
+    mbar_expect_tx(&full[slot], bytes);
+    bulk_g2s(ring + static_cast<std::size_t>(slot) * slot_bytes, source, bytes, &full[slot]);
   };
   for (std::uint32_t i = 0; ok && i < L.op_count; ++i) {
     const LoopOp& op = L.ops[i];
     if (op.kind != kLoopGemv) continue;
     const LoopGemv& g = op.gemv;
-    const std::uint32_t block = g.bits * 256u, G = g.groups, per_slot = kLoopSlotBytes / block;
+    const std::uint32_t block = g.bits * 256u, G = g.groups, per_slot = groups_per_slot(g.bits);
     const std::uint32_t parts = g.paired ? 2u : 1u;
     for (std::uint32_t u = first_unit(c, op.rotation); ok && u < g.units; u += c.ctas) {
       for (std::uint32_t p = 0; ok && p < parts; ++p) {
         std::uint32_t tile;
         const LoopMatrix& m = g.m[locate(g, u, p, tile)];
-        issue(m.scales + static_cast<std::size_t>(tile) * G * 16u, G * 32u);
-        for (std::uint32_t g0 = 0; ok && g0 < G; g0 += per_slot) {
-          issue(m.codes + (static_cast<std::size_t>(tile) * G + g0) * block, min(per_slot, G - g0) * block);
+        issue(scale_n++, kLoopScaleSlots, c.scale_full, c.scale_empty, c.scale_ring, c.scale_slot_bytes,
+              m.scales + static_cast<std::size_t>(tile) * G * 16u, G * 32u);
+        for (std::uint32_t g0 = 0; g0 < G; g0 += per_slot) {
+          issue(code_n++, c.slots, c.full, c.empty, c.ring, kLoopSlotBytes,
+                m.codes + (static_cast<std::size_t>(tile) * G + g0) * block, min(per_slot, G - g0) * block);
         }
       }
     }
   }
   // No copy may still be landing in shared memory when the CTA exits.
-  const std::uint32_t first = issued > c.slots ? issued - c.slots : 0u;
-  for (std::uint32_t k = first; k < issued; ++k) {
-    producer_wait(c, &c.full[k % c.slots], (k / c.slots) & 1u, false);
+  for (std::uint32_t k = code_n > c.slots ? code_n - c.slots : 0u; k < code_n; ++k) {
+    if (k % kLoopProducerLanes == lane) producer_wait(c, &c.full[k % c.slots], (k / c.slots) & 1u, false);
+  }
+  for (std::uint32_t k = scale_n > kLoopScaleSlots ? scale_n - kLoopScaleSlots : 0u; k < scale_n; ++k) {
+    if (k % kLoopProducerLanes == lane) {
+      producer_wait(c, &c.scale_full[k % kLoopScaleSlots], (k / kLoopScaleSlots) & 1u, false);
+    }
   }
 }
 
@@ -230,27 +277,55 @@ __device__ __forceinline__ void produce(const LoopLaunch& L, Ctx& c) {
 // GEMV
 // ---------------------------------------------------------------------------
 
-// int32 dots of one 128-column group for the 16 rows of a tile, token 0:
-// lanes with t = lane % 4 == 0 hold rows lane/4 and lane/4 + 8.
+// int32 dots of this warp's groups of one code slot (groups g0..g1-1 of the
+// tile; warp w takes first = g0 + (w - g0) mod 8, first + 8, ...), token 0:
+// lanes with t = lane % 4 == 0 hold rows lane/4 and lane/4 + 8. All of the
+// warp's groups are loaded, unpacked and multiplied together (indices past
+// g1 repeat the last group and are not stored), and each group's four mma
+// run as two independent chains, so the tensor-core latency overlaps.
 template <int Bits>
-__device__ __forceinline__ void group_dots(const std::uint8_t* block, const std::int8_t* act, std::int32_t sum,
-                                           unsigned lane, std::int32_t* out) {
+__device__ __forceinline__ void slot_dots(const std::uint8_t* base, std::uint32_t g0, std::uint32_t g1,
+                                          const std::int8_t* act_codes, const std::int32_t* act_sums,
+                                          unsigned warp, unsigned lane, std::int32_t* out) {
   constexpr int kAlpha = Codec<Bits>::alpha, kBeta = Codec<Bits>::beta;
-  LaneWords<Bits> w;
-  load_lane_shared<Bits>(block, lane, w);
-  std::uint32_t a[4][4];
-  unpack(w, a);
+  constexpr std::uint32_t kBlock = Bits * 256u;
+  constexpr std::uint32_t kPerWarp = (kLoopSlotBytes / kBlock + kLoopComputeWarps - 1u) / kLoopComputeWarps;
   const unsigned tq = lane & 3u, gl = lane >> 2;
-  const uint4 b0 = *reinterpret_cast<const uint4*>(act + tq * 32u);
-  const uint4 b1 = *reinterpret_cast<const uint4*>(act + tq * 32u + 16u);
-  int acc[4] = {0, 0, 0, 0};
-  mma_s8_16832(acc, a[0], b0.x, b0.y);
-  mma_s8_16832(acc, a[1], b0.z, b0.w);
-  mma_s8_16832(acc, a[2], b1.x, b1.y);
-  mma_s8_16832(acc, a[3], b1.z, b1.w);
-  if (tq == 0) {
-    out[gl] = kAlpha * acc[0] + kBeta * sum;
-    out[gl + 8u] = kAlpha * acc[2] + kBeta * sum;
+  const std::uint32_t first = g0 + ((warp + kLoopComputeWarps - g0 % kLoopComputeWarps) % kLoopComputeWarps);
+  if (first >= g1) return;
+  std::uint32_t group[kPerWarp];
+  LaneWords<Bits> w[kPerWarp];
+  uint4 b0[kPerWarp], b1[kPerWarp];
+#pragma unroll
+  for (std::uint32_t j = 0; j < kPerWarp; ++j) {
+    group[j] = min(first + kLoopComputeWarps * j, g1 - 1u);
+    load_lane_shared<Bits>(base + (group[j] - g0) * kBlock, lane, w[j]);
+    const std::int8_t* act = act_codes + group[j] * kGroup + tq * 32u;
+    b0[j] = *reinterpret_cast<const uint4*>(act);
+    b1[j] = *reinterpret_cast<const uint4*>(act + 16u);
+  }
+  int acc[kPerWarp][2][4];
+#pragma unroll
+  for (std::uint32_t j = 0; j < kPerWarp; ++j) {
+    std::uint32_t a[4][4];
+    unpack(w[j], a);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[j][h][r] = 0;
+    }
+    mma_s8_16832(acc[j][0], a[0], b0[j].x, b0[j].y);
+    mma_s8_16832(acc[j][1], a[1], b0[j].z, b0[j].w);
+    mma_s8_16832(acc[j][0], a[2], b1[j].x, b1[j].y);
+    mma_s8_16832(acc[j][1], a[3], b1[j].z, b1[j].w);
+  }
+#pragma unroll
+  for (std::uint32_t j = 0; j < kPerWarp; ++j) {
+    if (tq == 0 && first + kLoopComputeWarps * j < g1) {
+      const std::int32_t sum = act_sums[group[j]];
+      out[group[j] * 16u + gl] = kAlpha * (acc[j][0][0] + acc[j][1][0]) + kBeta * sum;
+      out[group[j] * 16u + gl + 8u] = kAlpha * (acc[j][0][2] + acc[j][1][2]) + kBeta * sum;
+    }
   }
 }
 
@@ -280,12 +355,25 @@ __device__ __forceinline__ void gemv_prologue(const LoopLaunch& L, Ctx& c, const
     norm_pack_body<ActBits, NormIters>(a, 0, t, ComputeSync{}, sc.norm.warp_sums, sc.norm.warp_max,
                                        sc.norm.code_sums);
   } else if (g.act_source == kActPackF16) {
+    // Batches of eight groups per warp: all eight L2 loads are in flight
+    // before the first group's reductions.
     const unsigned warp = t >> 5, lane = t & 31u;
-    for (std::uint32_t group = warp; group < G; group += kLoopComputeWarps) {
-      const uint2 raw = ld_cg8(g.f16_input + static_cast<std::size_t>(group) * kGroup + 4u * lane);
-      const __half* hv = reinterpret_cast<const __half*>(&raw);
-      const float x[4] = {h2f(hv[0]), h2f(hv[1]), h2f(hv[2]), h2f(hv[3])};
-      pack_warp_group<ActBits>(x, lane, c.act_codes + group * kGroup, c.act_scales + group, c.act_sums + group);
+    constexpr std::uint32_t kBatch = 8;
+    for (std::uint32_t first = warp; first < G; first += kBatch * kLoopComputeWarps) {
+      uint2 raw[kBatch];
+#pragma unroll
+      for (std::uint32_t j = 0; j < kBatch; ++j) {
+        const std::uint32_t group = min(first + j * kLoopComputeWarps, G - 1u);
+        raw[j] = ld_cg8(g.f16_input + static_cast<std::size_t>(group) * kGroup + 4u * lane);
+      }
+#pragma unroll
+      for (std::uint32_t j = 0; j < kBatch; ++j) {
+        const std::uint32_t group = first + j * kLoopComputeWarps;
+        if (group >= G) break;
+        const __half* hv = reinterpret_cast<const __half*>(&raw[j]);
+        const float x[4] = {h2f(hv[0]), h2f(hv[1]), h2f(hv[2]), h2f(hv[3])};
+        pack_warp_group<ActBits>(x, lane, c.act_codes + group * kGroup, c.act_scales + group, c.act_sums + group);
+      }
     }
   } else {
     for (std::uint32_t i = t; i < G * 8u; i += kLoopComputeThreads) {
@@ -303,8 +391,7 @@ template <int Bits>
 __device__ __forceinline__ void gemv_units(Ctx& c, const LoopOp& op, float* best, std::uint32_t* best_index) {
   const LoopGemv& g = op.gemv;
   const unsigned t = threadIdx.x, warp = t >> 5, lane = t & 31u;
-  constexpr std::uint32_t kBlock = Bits * 256u;
-  constexpr std::uint32_t kPerSlot = kLoopSlotBytes / kBlock;
+  constexpr std::uint32_t kPerSlot = kLoopSlotBytes / (Bits * 256u);
   const std::uint32_t G = g.groups;
   const std::uint32_t parts = g.paired ? 2u : 1u;
   for (std::uint32_t u = first_unit(c, op.rotation); u < g.units; u += c.ctas, ++c.unit_counter) {
@@ -315,18 +402,14 @@ __device__ __forceinline__ void gemv_units(Ctx& c, const LoopOp& op, float* best
     for (std::uint32_t p = 0; p < 2; ++p) {
       if (p >= parts) break;
       mats[p] = locate(g, u, p, tiles[p]);
-      scale_pos[p] = c.n++;
+      scale_pos[p] = c.sn++;
       std::int32_t* dpart = dbuf + p * G * 16u;
       for (std::uint32_t g0 = 0; g0 < G; g0 += kPerSlot) {
         const std::uint32_t pos = c.n++, slot = pos % c.slots;
-        const bool ok = ring_wait(c, slot, pos / c.slots, lane);
-        const std::uint32_t g1 = min(G, g0 + kPerSlot);
+        const bool ok = ring_wait(c, &c.full[slot], pos / c.slots, lane);
         if (ok) {
-          const std::uint8_t* base = c.ring + static_cast<std::size_t>(slot) * kLoopSlotBytes;
-          for (std::uint32_t gg = g0 + ((warp + 8u - g0 % 8u) % 8u); gg < g1; gg += 8u) {
-            group_dots<Bits>(base + (gg - g0) * kBlock, c.act_codes + gg * kGroup, c.act_sums[gg], lane,
-                             dpart + gg * 16u);
-          }
+          slot_dots<Bits>(c.ring + static_cast<std::size_t>(slot) * kLoopSlotBytes, g0, min(G, g0 + kPerSlot),
+                          c.act_codes, c.act_sums, warp, lane, dpart);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&c.empty[slot]);
@@ -338,15 +421,17 @@ __device__ __forceinline__ void gemv_units(Ctx& c, const LoopOp& op, float* best
     // lanes 0-15 run part 0's rows, lanes 16-31 part 1's.
     const std::uint32_t p = lane >> 4, row = lane & 15u;
     bool ok = true;
-    ok = ring_wait(c, scale_pos[0] % c.slots, scale_pos[0] / c.slots, lane);
-    if (parts == 2) ok = ring_wait(c, scale_pos[1] % c.slots, scale_pos[1] / c.slots, lane) && ok;
+    ok = ring_wait(c, &c.scale_full[scale_pos[0] % kLoopScaleSlots], scale_pos[0] / kLoopScaleSlots, lane);
+    if (parts == 2) {
+      ok = ring_wait(c, &c.scale_full[scale_pos[1] % kLoopScaleSlots], scale_pos[1] / kLoopScaleSlots, lane) && ok;
+    }
     const std::uint32_t my_scale = p == 0 ? scale_pos[0] : scale_pos[1];
     const std::uint32_t my_tile = p == 0 ? tiles[0] : tiles[1];
     const std::uint32_t my_mat = p == 0 ? mats[0] : mats[1];
     float acc = 0.0f;
     if (ok && p < parts) {
-      const __half* ws =
-          reinterpret_cast<const __half*>(c.ring + static_cast<std::size_t>(my_scale % c.slots) * kLoopSlotBytes);
+      const __half* ws = reinterpret_cast<const __half*>(
+          c.scale_ring + static_cast<std::size_t>(my_scale % kLoopScaleSlots) * c.scale_slot_bytes);
       const std::int32_t* d = dbuf + p * G * 16u;
       std::uint32_t gg = 0;
       for (; gg + 8u <= G; gg += 8u) {
@@ -402,8 +487,8 @@ __device__ __forceinline__ void gemv_units(Ctx& c, const LoopOp& op, float* best
     }
     __syncwarp();
     if (lane == 0) {
-      mbar_arrive_count(&c.empty[scale_pos[0] % c.slots], kLoopComputeWarps);
-      if (parts == 2) mbar_arrive_count(&c.empty[scale_pos[1] % c.slots], kLoopComputeWarps);
+      mbar_arrive(&c.scale_empty[scale_pos[0] % kLoopScaleSlots]);
+      if (parts == 2) mbar_arrive(&c.scale_empty[scale_pos[1] % kLoopScaleSlots]);
     }
   }
 }
@@ -503,6 +588,11 @@ __global__ void __launch_bounds__(kLoopThreads, 1) token_loop_kernel(const __gri
   c.act_scales = reinterpret_cast<__half*>(smem + L.act_scales_offset);
   c.act_sums = reinterpret_cast<std::int32_t*>(smem + L.act_sums_offset);
   c.dots = reinterpret_cast<std::int32_t*>(smem + L.dots_offset);
+  c.scale_ring = smem + L.scale_offset;
+  c.scale_full = reinterpret_cast<std::uint64_t*>(smem + L.scale_bars_offset);
+  c.scale_empty = c.scale_full + kLoopScaleSlots;
+  c.scale_slot_bytes = L.scale_slot_bytes;
+  c.sn = 0;
   c.dots_half = L.dots_half;
   c.slots = L.slots;
   c.cta = blockIdx.x;
@@ -510,18 +600,26 @@ __global__ void __launch_bounds__(kLoopThreads, 1) token_loop_kernel(const __gri
   c.n = 0;
   c.unit_counter = 0;
   c.abort = &s_abort;
+  c.trace = L.trace;
 
   if (threadIdx.x == 0) {
+    trace_mark(c, 0, 0);
+    trace_mark(c, 0, 1);
     for (std::uint32_t s = 0; s < L.slots; ++s) {
       mbar_init(&c.full[s], 1);
       mbar_init(&c.empty[s], kLoopComputeWarps);
+    }
+    for (std::uint32_t s = 0; s < kLoopScaleSlots; ++s) {
+      mbar_init(&c.scale_full[s], 1);
+      mbar_init(&c.scale_empty[s], 1);
     }
     fence_mbar_init();
     s_abort = 0;
   }
   __syncthreads();
   if (threadIdx.x >= kLoopComputeThreads) {
-    if (threadIdx.x == kLoopComputeThreads) produce(L, c);
+    const unsigned producer = (threadIdx.x - kLoopComputeThreads) >> 5;
+    if ((threadIdx.x & 31u) == 0) produce(L, c, producer);
     return;
   }
 
@@ -533,7 +631,7 @@ __global__ void __launch_bounds__(kLoopThreads, 1) token_loop_kernel(const __gri
     const std::uint32_t kind = op.kind;
     if (kind == kLoopGemv) {
       const LoopGemv& g = op.gemv;
-      if (i > 0) grid_barrier(c, target);
+      if (i > 0) grid_barrier(c, target, i);
       const bool logits = g.m[0].epilogue == kEpiLogits;
       if (logits && t == 0) {
         s_best = -__int_as_float(0x7f800000);
@@ -560,7 +658,7 @@ __global__ void __launch_bounds__(kLoopThreads, 1) token_loop_kernel(const __gri
       float S[kGdnRows];
       // The state does not depend on this step: load it before the barrier.
       if (u < a.value_heads) gdn_load_state(a, u, t, S);
-      const bool alive = i == 0 || grid_barrier(c, target);
+      const bool alive = i == 0 || grid_barrier(c, target, i);
       for (; u < a.value_heads; u += c.ctas) {
         if (alive) {
           gdn_recurrent_tokens(a, u, t, S, ComputeSync{}, scratch.gdn);
@@ -569,10 +667,10 @@ __global__ void __launch_bounds__(kLoopThreads, 1) token_loop_kernel(const __gri
         if (u + c.ctas < a.value_heads) gdn_load_state(a, u + c.ctas, t, S);
       }
     } else if (kind == kLoopAttention) {
-      const bool alive = i == 0 || grid_barrier(c, target);
+      const bool alive = i == 0 || grid_barrier(c, target, i);
       if (alive) attention_units(L, c, op, scratch, &s_flag);
     } else if (kind == kLoopArgmax) {
-      grid_barrier(c, target);
+      grid_barrier(c, target, i);
       if (c.cta == 0 && warp == 0) {
         float best = -__int_as_float(0x7f800000);
         std::uint32_t index = 0xffffffffu;
@@ -595,9 +693,14 @@ __global__ void __launch_bounds__(kLoopThreads, 1) token_loop_kernel(const __gri
     }
   }
   if (c.cta == 0 && t == 0) L.control->epoch = base + (L.op_count - 1u) * c.ctas;
+  if (t == 0) {
+    trace_mark(c, L.op_count, 0);
+    trace_mark(c, L.op_count, 1);
+  }
 }
 
 using LoopKernel = void (*)(LoopLaunch);
+
 
 LoopKernel select_kernel(int act_bits, std::uint32_t hidden) {
   const std::uint32_t iterations = hidden / 256u;
@@ -619,11 +722,6 @@ std::uint32_t align_up(std::uint32_t value, std::uint32_t alignment) {
 }  // namespace
 
 bool token_loop_supported_hidden(std::uint32_t hidden) { return select_kernel(4, hidden) != nullptr; }
-
-std::uint32_t token_loop_unit_slots(std::uint32_t bits, std::uint32_t groups, bool paired) {
-  const std::uint32_t per_slot = kLoopSlotBytes / (bits * 256u);
-  return (paired ? 2u : 1u) * (1u + (groups + per_slot - 1u) / per_slot);
-}
 
 int token_loop_grid(int device, std::uint32_t* ctas) {
   int sms = 0;
@@ -663,7 +761,12 @@ int plan_token_loop(LoopLaunch& L, std::uint32_t max_groups, std::uint32_t dots_
   offset = align_up(offset + max_groups * 4u, 16);
   L.dots_offset = offset;
   L.dots_half = dots_half;
-  offset = align_up(offset + 2u * dots_half * 4u, 1024);
+  offset = align_up(offset + 2u * dots_half * 4u, 128);
+  L.scale_slot_bytes = align_up(max_groups * 32u, 128);
+  L.scale_offset = offset;
+  offset += kLoopScaleSlots * L.scale_slot_bytes;
+  L.scale_bars_offset = offset;
+  offset = align_up(offset + kLoopScaleSlots * 16u, 1024);
   if (offset >= available) return fail(GFXB_UNSUPPORTED, "token kernel: shared memory exhausted");
   L.slots = std::min<std::uint32_t>((available - offset) / (kLoopSlotBytes + 16u), 64u);
   if (L.slots < 4) return fail(GFXB_UNSUPPORTED, "token kernel: weight ring too small");

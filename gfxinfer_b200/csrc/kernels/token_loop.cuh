@@ -2,12 +2,18 @@
 // layers, the LM head and the argmax) as a list of operations executed by one
 // CTA per SM.
 //
-// Each CTA has one producer warp and eight compute warps. The producer walks
+// Each CTA has four producer warps and eight compute warps. The producers walk
 // the CTA's share of every weight matrix of the step, in step order, and
-// streams it into a shared-memory ring with bulk copies (cp.async.bulk,
-// mbarrier completion). Weights never depend on activations, so the stream
-// runs ahead across operation and layer boundaries while the compute warps
-// wait at grid barriers. Compute warps run each operation's units (16-row
+// streams it into shared memory with bulk copies (cp.async.bulk, mbarrier
+// completion): weight codes into a ring of 16 KB slots, each tile's fp16
+// scales into a small ring of its own (a tile's scales stay until its fp32
+// chain is done, while its code slots are released as soon as they are
+// read). The four producers (lane 0 of each producer warp) issue alternate
+// copies, so one producer's wait for a free slot never stalls the stream; a
+// waiting producer may be suspended in hardware, which is why each has a
+// warp of its own. Weights never depend on activations,
+// so the stream runs ahead across operation and layer boundaries while the
+// compute warps wait at grid barriers. Compute warps run each operation's units (16-row
 // weight tiles, GDN value heads, attention chunks) and meet at a grid barrier
 // before every operation that reads another CTA's output.
 //
@@ -27,9 +33,11 @@ namespace gfxb {
 
 constexpr unsigned kLoopComputeWarps = 8;
 constexpr unsigned kLoopComputeThreads = kLoopComputeWarps * 32;
-constexpr unsigned kLoopThreads = kLoopComputeThreads + 32;  // + the producer warp
-constexpr unsigned kLoopSlotBytes = 8192;                    // one ring slot
-constexpr unsigned kLoopMaxGroups = kLoopSlotBytes / 32;     // a tile's fp16 scales fit one slot
+constexpr unsigned kLoopSlotBytes = 16384;                   // one code-ring slot
+constexpr unsigned kLoopProducerLanes = 4;                   // producer warps (lane 0 of each issues copies)
+constexpr unsigned kLoopThreads = kLoopComputeThreads + 32 * kLoopProducerLanes;
+constexpr unsigned kLoopScaleSlots = 4;                      // scale-ring slots (one tile's scales each)
+constexpr unsigned kLoopMaxGroups = 512;                     // K <= 65536
 constexpr unsigned kLoopMaxCtas = 1024;
 constexpr unsigned kLoopMaxKvHeads = 64;
 constexpr unsigned kLoopMaxNormIterations = 40;  // hidden <= 10240
@@ -117,20 +125,25 @@ struct LoopLaunch {
   std::uint32_t* selected;    // argmax result
   std::uint32_t* tokens;      // next input token
   std::uint64_t* position;    // advanced by one per step
-  std::uint32_t slots;        // ring slots
+  std::uint32_t slots;        // code-ring slots
   std::uint32_t ring_offset, bars_offset, act_offset, act_scales_offset, act_sums_offset, dots_offset;
+  std::uint32_t scale_offset, scale_bars_offset;
+  std::uint32_t scale_slot_bytes;  // largest K / 128 * 32, rounded to 128
   std::uint32_t dots_half;    // int32 words per dots buffer (two buffers)
   std::uint32_t smem_bytes;   // dynamic shared memory of the launch
   std::uint32_t ctas;         // grid: one CTA per SM
   std::uint32_t act_bits;     // 4 or 8
+  // Optional timeline ([op_count + 1][2][ctas] globaltimer ns, null: off).
+  // Entry (i, 0, cta): the CTA's compute warps finished operation i - 1 and
+  // reached the grid barrier in front of operation i; (i, 1, cta): the
+  // barrier released. Entry i = 0 is the kernel start, i = op_count its end.
+  std::uint64_t* trace;
 };
 
 // Shared-memory plan for the given largest K (groups) and dots buffer; also
 // configures the kernel and checks that one CTA fits each SM. Call outside
 // stream capture; launch_token_loop then only launches.
 int plan_token_loop(LoopLaunch& launch, std::uint32_t max_groups, std::uint32_t dots_half, int device);
-// Slots one unit of a GEMV holds at once (must not exceed the ring).
-std::uint32_t token_loop_unit_slots(std::uint32_t bits, std::uint32_t groups, bool paired);
 // Grid size (one CTA per SM).
 int token_loop_grid(int device, std::uint32_t* ctas);
 int launch_token_loop(const LoopLaunch& launch, cudaStream_t stream);

@@ -104,8 +104,9 @@ class QwenDecodeSession:
     @classmethod
     def create(cls, engine: Engine, maximum_context_tokens: int | None = None, graph_verifier_batch: int = 0,
                use_graphs: bool = True, step_kernel: int = abi.STEP_AUTO) -> "QwenDecodeSession":
-        """step_kernel: abi.STEP_AUTO (persistent token kernel where supported), abi.STEP_LAUNCHES
-        (per-operation kernels) or abi.STEP_PERSISTENT (token kernel or GFXB_UNSUPPORTED)."""
+        """step_kernel: abi.STEP_AUTO (the faster path on B200: per-operation kernels today),
+        abi.STEP_LAUNCHES (per-operation kernels) or abi.STEP_PERSISTENT (token kernel or
+        GFXB_UNSUPPORTED)."""
         ctx = maximum_context_tokens or engine.config.max_context
         config = abi.SessionConfig(ctx, graph_verifier_batch, int(use_graphs), step_kernel)
         handle = ctypes.c_void_p()
@@ -170,6 +171,27 @@ class QwenDecodeSession:
         check(lib().gfxb_session_read_state(self._handle, hidden.ctypes.data,
                                             logits.ctypes.data if logits_count else None, logits_count))
         return hidden, logits[:logits_count]
+
+    def trace_step(self, token: int):
+        """One greedy step on the persistent token kernel with its timeline recorded.
+
+        Returns (next_token, timeline, op_kinds): timeline is int64 nanoseconds
+        [op_count + 1][2][ctas] (barrier arrival, barrier release per operation
+        and CTA; see gfxb_session_trace_step), op_kinds the operation codes."""
+        import numpy as np
+
+        ops, ctas = ctypes.c_uint(), ctypes.c_uint()
+        out = ctypes.c_uint32()
+        probe = lib().gfxb_session_trace_step(self._handle, token, ctypes.byref(out), None, 0, ctypes.byref(ops),
+                                              ctypes.byref(ctas), None)
+        if probe not in (0, 1):  # 1: the probe's missing buffer; anything else is a real failure
+            check(probe)
+        timeline = np.zeros((ops.value + 1, 2, ctas.value), np.uint64)
+        kinds = np.zeros(ops.value, np.uint32)
+        check(lib().gfxb_session_trace_step(self._handle, token, ctypes.byref(out), timeline.ctypes.data,
+                                            timeline.size, ctypes.byref(ops), ctypes.byref(ctas),
+                                            kinds.ctypes.data))
+        return out.value, timeline.astype(np.int64), kinds
 
     def close(self) -> None:
         if self._handle:

@@ -250,13 +250,14 @@ typedef struct {
   uint32_t step_kernel;          /* GFXB_STEP_*: how a batch-1 greedy step runs */
 } gfxb_session_config;
 
-/* Batch-1 greedy step execution. AUTO uses the persistent token kernel (one
- * launch per token: every layer, the LM head and the argmax, with the weight
- * stream running ahead across layers) where the session supports it (one
- * GPU, hidden size 256 x {4, 8, 16, 20}) and the per-operation launches
- * otherwise; LAUNCHES always uses the per-operation kernels; PERSISTENT fails
- * session creation with GFXB_UNSUPPORTED where the token kernel cannot run.
- * Both paths produce identical bits. */
+/* Batch-1 greedy step execution. LAUNCHES runs the per-operation kernels
+ * (captured in a CUDA graph when use_graphs is set). PERSISTENT runs the
+ * persistent token kernel (one launch per token: every layer, the LM head and
+ * the argmax, with the weight stream running ahead across layers) and fails
+ * session creation with GFXB_UNSUPPORTED where it cannot run (tensor
+ * parallelism, hidden size not 256 x {4, 8, 16, 20}). AUTO picks the faster
+ * path measured on B200, currently the per-operation launches. Both paths
+ * produce identical bits. */
 enum { GFXB_STEP_AUTO = 0, GFXB_STEP_LAUNCHES = 1, GFXB_STEP_PERSISTENT = 2 };
 
 int gfxb_session_create(gfxb_engine* engine, const gfxb_session_config* config, gfxb_session** session);
@@ -286,6 +287,17 @@ void* gfxb_session_stream(gfxb_session* session);
  * bytes of one launch (codes, fp16 scales, A4 activation, fp32 outputs).
  * Used to time the dominant kernel in isolation. */
 int gfxb_session_enqueue_gemv(gfxb_session* session, int kind, unsigned launches, uint64_t* bytes);
+/* One greedy step on the persistent token kernel with its timeline recorded
+ * (GFXB_UNSUPPORTED when the session runs per-operation launches). timeline
+ * receives [op_count + 1][2][ctas] globaltimer nanoseconds: entry (i, 0, c)
+ * is when CTA c finished operation i - 1 and reached the grid barrier before
+ * operation i, (i, 1, c) when that barrier released it; i = 0 is the kernel
+ * start and i = op_count its end. op_kinds (optional, op_count entries): 1
+ * GEMV (| activation source << 4 | weight bits << 8), 2 GDN, 3 attention,
+ * 4 argmax. For profiling; the step's result is that of greedy_step. */
+int gfxb_session_trace_step(gfxb_session* session, uint32_t input_token, uint32_t* output_token,
+                            uint64_t* timeline, size_t timeline_entries, unsigned* op_count, unsigned* ctas,
+                            uint32_t* op_kinds);
 /* Copies the last token's final hidden state (fp16 [hidden]) and logits of the
  * local vocabulary shard (fp32) to host memory, for parity checks. */
 int gfxb_session_read_state(gfxb_session* session, uint16_t* hidden, float* logits, size_t logits_count);

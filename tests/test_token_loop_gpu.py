@@ -140,7 +140,29 @@ def test_persistent_required_is_refused_for_unsupported_hidden():
     engine = _engine(**kw)
     with pytest.raises(GfxbError):
         _session(engine, "persistent")
-    auto = gs.QwenDecodeSession.create(engine)  # AUTO falls back to per-operation launches
+    auto = gs.QwenDecodeSession.create(engine)  # AUTO runs the per-operation launches
     auto.greedy_step(1)
     auto.close()
     engine.close()
+
+
+def test_trace_step_timeline(oracle, small_engine):
+    """The traced step returns the greedy step's token and a consistent timeline:
+    per CTA, barrier arrival <= release, and operation i + 1 starts after operation i."""
+    cfg = model_config(**SMALL_MODEL)
+    prompt = prompt_tokens(oracle, cfg.seed + 10, cfg.vocab, 5)
+    a = _session(small_engine, "persistent")
+    b = _session(small_engine, "launches")
+    for t in prompt[:-1]:
+        a.greedy_step(t)
+        b.greedy_step(t)
+    token, timeline, kinds = a.trace_step(prompt[-1])
+    assert token == b.greedy_step(prompt[-1])
+    assert len(kinds) + 1 == timeline.shape[0]
+    assert set(np.unique(kinds) & 0xF) <= {1, 2, 3, 4}
+    assert kinds[-1] == 4  # argmax closes the step
+    assert (timeline > 0).all()
+    assert (timeline[:, 1, :] >= timeline[:, 0, :]).all()
+    assert (np.diff(timeline[:, 1, :], axis=0) >= 0).all()
+    a.close()
+    b.close()
