@@ -53,6 +53,8 @@ SIGNATURES: dict[str, tuple] = {
     "gfxb_quantize_activation_i8": (c_int, [P, P, P, c_size_t, c_uint, P]),
     "gfxb_gfx12_i4_gemm": (c_int, [c_int, P, P, P, P, P, c_size_t, c_size_t, c_uint, c_int, P]),
     "gfxb_gfx12_i8_gemm": (c_int, [c_int, P, P, P, P, P, c_size_t, c_size_t, c_uint, P]),
+    "gfxb_lowbit_gemv_f16": (c_int, [c_int, POINTER(GemvMatrix), c_uint, P, c_size_t, c_uint, P]),
+    "gfxb_gfx12_f16_gemm": (c_int, [c_int, P, P, P, P, c_size_t, c_size_t, c_uint, P]),
     "gfxb_residual_rms_norm_pack": (c_int, [P, P, P, P, P, c_size_t, c_uint, ctypes.c_float, c_int, c_int, P, P, P, P, P]),
     "gfxb_silu_multiply_pack": (c_int, [P, P, c_size_t, c_uint, P, c_int, P, P, P, P, P]),
     "gfxb_gdn_conv_update": (c_int, [P, P, P, P, P, P, c_size_t, c_uint, P]),

@@ -91,3 +91,19 @@ def gfx12_i8_gemm(fmt, tiled, tiled_scales, a8, a_scales, rows, cols, batch):
     check(lib().gfxb_gfx12_i8_gemm(fmt, _p(tiled), _p(tiled_scales), _p(a8), _p(a_scales), _p(out),
                                    rows, cols, batch, _stream()))
     return out
+
+
+def lowbit_gemv_f16(fmt: int, matrices, x_f16: torch.Tensor) -> None:
+    """fp16-activation GEMV; matrices: list of (codes, tiled_scales, output, rows, output_f16)."""
+    batch, cols = x_f16.shape
+    arr = (abi.GemvMatrix * len(matrices))()
+    for i, (codes, scales, output, rows, f16) in enumerate(matrices):
+        arr[i] = abi.GemvMatrix(_p(codes), _p(scales), _p(output), rows, int(f16))
+    check(lib().gfxb_lowbit_gemv_f16(fmt, arr, len(matrices), _p(x_f16), cols, batch, _stream()))
+
+
+def gfx12_f16_gemm(fmt, tiled, tiled_scales, x_f16, rows, cols, batch):
+    out = torch.empty((batch, rows), dtype=torch.float32, device=tiled.device)
+    check(lib().gfxb_gfx12_f16_gemm(fmt, _p(tiled), _p(tiled_scales), _p(x_f16), _p(out), rows, cols, batch,
+                                    _stream()))
+    return out

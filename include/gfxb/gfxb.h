@@ -104,6 +104,15 @@ int gfxb_lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, unsigned matr
                      const int8_t* act_codes, const uint16_t* act_scales,
                      const int32_t* act_sums, size_t columns, unsigned batch, void* stream);
 
+/* FP16-activation GEMV over the b200 layout: y[b][n] = sum_k fp16(q * ws) *
+ * x[b][k], fp32 accumulation on the f16 tensor cores (the reference's
+ * gfx12_f16_gemm arithmetic, lowbit_gemv.hip:757-834; its summation order is
+ * the tensor cores', so results match an exact sum within ~1e-5 relative).
+ * activations [B][K] fp16 (8-byte aligned), 1..4 matrices sharing K and
+ * format, batch in [1, 32]. W2, W3 and W4. */
+int gfxb_lowbit_gemv_f16(int format, const gfxb_gemv_matrix* matrices, unsigned matrix_count,
+                         const uint16_t* activations, size_t columns, unsigned batch, void* stream);
+
 /* ---- reference-layout drop-ins (lowbit_gemv.h:79-170) ------------------------ */
 int gfxb_quantize_activation_i4(const uint16_t* input, uint8_t* packed_output, uint16_t* scales,
                                 size_t columns, unsigned batch, void* stream);
@@ -120,6 +129,14 @@ int gfxb_gfx12_i8_gemm(int format, const uint8_t* tiled_weights,
                        const uint16_t* tiled_weight_scales, const int8_t* quantized_activations,
                        const uint16_t* activation_scales, float* output, size_t rows,
                        size_t columns, unsigned batch, void* stream);
+
+/* Replaces launch_gfx12_f16_gemm (lowbit_gemv.h:161-170): gfx12 tiled weights
+ * (quantization.cpp:253-318; W3 in the sequential 3-bit fragment order, which
+ * the reference does not support here), fp16 activations [B][K], fp32 output
+ * [B][N]. Same argument checks and error codes as the reference launcher. */
+int gfxb_gfx12_f16_gemm(int format, const uint8_t* tiled_weights, const uint16_t* tiled_weight_scales,
+                        const uint16_t* activations, float* output, size_t rows, size_t columns,
+                        unsigned batch, void* stream);
 
 /* ---- decode-path operators (qwen_ops.h) -------------------------------------
  * Fused forms of the reference launchers; each optional output may be NULL. */

@@ -175,3 +175,69 @@ def test_reference_layout_dropins_bit_exact(oracle, ops, fmt):
     a8, s8 = oracle.quantize_a8(x16)
     np.testing.assert_array_equal(got4.cpu().numpy(), oracle.gemv(logical, scales16, a4, s4))
     np.testing.assert_array_equal(got8.cpu().numpy(), oracle.gemv(logical, scales16, a8, s8))
+
+
+# ---- fp16 activations (lowbit_gemv.hip:757-834) ------------------------------
+# The reference accumulates fp16(q * scale) * x in fp32 on its matrix cores; the
+# CUDA path does the same on the f16 tensor cores, so the summation order is
+# the hardware's. Tolerance: |got - exact| <= 1e-3 * max(1, |exact|), the
+# north-star bound for fp32-accumulated GEMV outputs (an fp32 accumulation of
+# K = 17408 terms stays near 1e-6 relative).
+F16_TOLERANCE = 1e-3
+
+
+def _assert_f16_close(got, exact):
+    err = np.abs(got.astype(np.float64) - exact) / np.maximum(1.0, np.abs(exact))
+    assert err.max() <= F16_TOLERANCE, err.max()
+
+
+@pytest.mark.parametrize("batch", [1, 5])
+def test_config0_w3_f16_activation_gemv(oracle, ops, batch):
+    rows, cols = 17408, 5120
+    codes, scales16, logical = _quantized(oracle, rows, cols, W3, seed=0)
+    b200, tiled = _device_b200(ops, codes, scales16, rows, cols, W3)
+    x16 = _activations(batch, cols, seed=300 + batch)
+    out = torch.empty((batch, rows), dtype=torch.float32, device="cuda")
+    ops.lowbit_gemv_f16(W3, [(b200, tiled, out, rows, False)], torch.from_numpy(x16).cuda())
+    torch.cuda.synchronize()
+    _assert_f16_close(out.cpu().numpy(), oracle.gemv_f16(logical, scales16, x16))
+
+
+@pytest.mark.parametrize("fmt", [W2, W3, W4])
+@pytest.mark.parametrize("batch", [1, 3, 8, 9, 32])
+def test_f16_activation_formats_batches_and_layouts(oracle, ops, fmt, batch):
+    rows, cols = 80, 1280
+    codes, scales16, logical = _quantized(oracle, rows, cols, fmt, seed=fmt * 7 + batch)
+    b200, tiled = _device_b200(ops, codes, scales16, rows, cols, fmt)
+    x16 = _activations(batch, cols, seed=batch + 40)
+    x = torch.from_numpy(x16).cuda()
+    exact = oracle.gemv_f16(logical, scales16, x16)
+    out32 = torch.empty((batch, 48), dtype=torch.float32, device="cuda")  # rows 0-47, fp32
+    out16 = torch.empty((batch, 32), dtype=torch.float16, device="cuda")  # rows 48-79, fp16
+    ops.lowbit_gemv_f16(fmt, [(b200, tiled, out32, 48, False), (b200[48 * cols * {1: 2, 2: 3, 3: 4}[fmt] // 8:],
+                              tiled[48 * cols // 128:], out16, 32, True)], x)
+    status, gfx12, gfx12_scales = oracle.tile(codes, scales16.astype(np.float32).reshape(-1), rows, cols, fmt)
+    assert status == 0
+    dropin = ops.gfx12_f16_gemm(fmt, torch.from_numpy(gfx12).cuda(),
+                                torch.from_numpy(gfx12_scales.astype(np.float16)).cuda(), x, rows, cols, batch)
+    torch.cuda.synchronize()
+    _assert_f16_close(out32.cpu().numpy(), exact[:, :48])
+    # fp16 outputs: the same bound plus the final rounding to fp16 (half an ulp, 2^-11 relative)
+    half = out16.cpu().numpy().astype(np.float64)
+    bound = F16_TOLERANCE * np.maximum(1.0, np.abs(exact[:, 48:])) + 2.0 ** -11 * np.abs(exact[:, 48:])
+    assert (np.abs(half - exact[:, 48:]) <= bound).all()
+    _assert_f16_close(dropin.cpu().numpy(), exact)
+
+
+def test_f16_activation_rejects_bad_arguments(ops):
+    from gfxinfer_b200 import GfxbError
+
+    x = torch.zeros((1, 256), dtype=torch.float16, device="cuda")
+    w = torch.zeros(16 * 256 // 2, dtype=torch.uint8, device="cuda")
+    s = torch.zeros(16 * 2, dtype=torch.float16, device="cuda")
+    with pytest.raises(GfxbError):
+        ops.gfx12_f16_gemm(W4, w, s, x, 16, 255, 1)  # K not a multiple of 128
+    with pytest.raises(GfxbError):
+        ops.gfx12_f16_gemm(W4, w, s, x, 16, 256, 33)  # batch beyond 32
+    with pytest.raises(GfxbError):
+        ops.gfx12_f16_gemm(W4, w[1:], s, x, 16, 256, 1)  # misaligned weights
