@@ -39,7 +39,31 @@ class TpShardInfo(ctypes.Structure):
         "gdn_channels")]
 
 
-# name -> (restype, argtypes); kept in declaration order of include/gfxb/gfxb.h.
+class ArtifactIdentity(ctypes.Structure):
+    _fields_ = [("target_arch", c_char * 16), ("model_id", c_char * 32), ("weights_id", c_char * 32),
+                ("recipe_id", c_char * 64)]
+
+
+class TensorView(ctypes.Structure):
+    _fields_ = [("name", c_char_p), ("dtype", ctypes.c_uint16), ("quantization", ctypes.c_uint16),
+                ("rank", ctypes.c_uint16), ("flags", ctypes.c_uint16), ("alignment", c_uint32),
+                ("dimensions", c_uint64 * 4), ("data", c_void_p), ("data_bytes", c_uint64), ("aux", c_void_p),
+                ("aux_bytes", c_uint64), ("data_offset", c_uint64), ("aux_offset", c_uint64),
+                ("data_crc64", c_uint64)]
+
+
+class TensorWrite(ctypes.Structure):
+    _fields_ = [("name", c_char_p), ("dtype", ctypes.c_uint16), ("quantization", ctypes.c_uint16),
+                ("rank", ctypes.c_uint16), ("dimensions", c_uint64 * 4), ("data", c_void_p), ("data_bytes", c_uint64),
+                ("aux", c_void_p), ("aux_bytes", c_uint64), ("alignment", c_uint32)]
+
+
+class ArtifactLoadOptions(ctypes.Structure):
+    _fields_ = [(name, c_uint32) for name in (
+        "activation_bits", "max_context", "draft_vocab", "include_mtp", "verify_checksums")]
+
+
+# name -> (restype, argtypes); kept in declaration order of include/gfxb/gfxb.h, then artifact.h.
 SIGNATURES: dict[str, tuple] = {
     "gfxb_last_error_message": (c_char_p, []),
     "gfxb_abi_version": (c_int, []),
@@ -90,6 +114,19 @@ SIGNATURES: dict[str, tuple] = {
     "gfxb_session_read_state": (c_int, [P, P, P, c_size_t]),
     "gfxb_session_trace_step": (c_int, [P, c_uint32, POINTER(c_uint32), P, c_size_t, POINTER(c_uint), POINTER(c_uint),
                                         P]),
+    "gfxb_crc64_ecma": (c_int, [c_uint64, P, c_size_t, POINTER(c_uint64)]),
+    "gfxb_artifact_open": (c_int, [c_char_p, c_int, POINTER(c_void_p)]),
+    "gfxb_artifact_close": (c_int, [P]),
+    "gfxb_artifact_identity_of": (c_int, [P, POINTER(ArtifactIdentity)]),
+    "gfxb_artifact_file_bytes": (c_int, [P, POINTER(c_uint64)]),
+    "gfxb_artifact_tensor_count": (c_int, [P, POINTER(c_size_t)]),
+    "gfxb_artifact_tensor_at": (c_int, [P, c_size_t, POINTER(TensorView)]),
+    "gfxb_artifact_find": (c_int, [P, c_char_p, POINTER(TensorView), POINTER(c_int)]),
+    "gfxb_artifact_write": (c_int, [c_char_p, POINTER(ArtifactIdentity), POINTER(TensorWrite), c_size_t]),
+    "gfxb_engine_create_from_artifact": (c_int, [c_char_p, POINTER(ArtifactLoadOptions), c_int, c_int, c_int, P,
+                                                 POINTER(c_void_p)]),
+    "gfxb_engine_config": (c_int, [P, POINTER(ModelConfig)]),
+    "gfxb_engine_export_artifact": (c_int, [P, c_char_p, c_char_p]),
 }
 
 

@@ -17,12 +17,15 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <string>
 #include <vector>
 
+#include "gfxb/artifact.h"
 #include "gfxb/gfxb.h"
+#include "host/artifact_internal.h"
 #include "kernels/common.cuh"
 #include "kernels/ops.cuh"
 #include "kernels/token_loop.cuh"
@@ -41,6 +44,9 @@ int generate_rowmajor_weights(std::uint64_t seed, std::uint32_t tensor, int form
 int generate_bf16(std::uint64_t seed, std::uint32_t tensor, std::uint64_t offset, std::uint64_t count, float lo,
                   float hi, std::uint16_t* out, cudaStream_t stream);
 int read_gemv_error(std::uint32_t* value, bool clear);
+int untile_gfx12_rowmajor(int format, const std::uint8_t* tiled_codes, const std::uint16_t* tiled_scales,
+                          std::uint8_t* codes, std::uint16_t* scales, std::size_t rows, std::size_t columns,
+                          cudaStream_t stream);
 
 namespace {
 
@@ -225,77 +231,214 @@ Shard make_shard(const gfxb_model_config& c, std::uint32_t tp, std::uint32_t ran
   return s;
 }
 
-// Plans (pass 1) or places and generates (pass 2) every weight of the shard.
-int build_weights(gfxb_engine& e, Planner& plan, bool generate) {
+// Where the weights come from: seeded synthetic generation on the device, or
+// a `.gfxi` artifact (mapped on the host; copied shard by shard, repacked to
+// the b200 layout when the recipe is a reference gfx12 tiled one).
+struct WeightSource {
+  const gfxi::View* view = nullptr;   // null: synthetic weights
+  bool gfx12 = false;                 // reference tiled recipe (else "b200-v1")
+  bool sequential_w3 = false;         // the tiled recipe's W3 fragments are sequential 3-bit
+  std::uint8_t* scratch = nullptr;    // device staging for repacks (placement pass)
+  std::size_t scratch_bytes = 0;      // largest staging need (planning pass)
+};
+
+std::string layer_name(std::uint32_t id, const char* suffix) {
+  if (id == kLayerMtp) return std::string("mtp.layers.0.") + suffix;
+  return "model.language_model.layers." + std::to_string(id) + "." + suffix;
+}
+
+int bits_of_quantization(std::uint16_t quantization) {
+  return quantization == GFXB_QUANT_W2G128 ? 2 : (quantization == GFXB_QUANT_W3G128 ? 3 : (quantization == GFXB_QUANT_W4G128 ? 4 : 0));
+}
+
+int artifact_error(const std::string& message) { return fail(GFXB_CORRUPT_ARTIFACT, message.c_str()); }
+
+// Checks a 2-D low-bit tensor of the artifact against the expected global shape.
+int check_matrix_tensor(const gfxi::View& view, const WeightSource& src, const std::string& name,
+                        std::uint32_t global_rows, std::uint32_t global_cols, int* bits) {
+  const gfxi::Tensor* t = view.find(name);
+  if (t == nullptr) return artifact_error("artifact lacks " + name);
+  const int b = bits_of_quantization(t->quantization);
+  if (t->rank != 2 || t->dtype != GFXB_DTYPE_U8 || b == 0 || t->dimensions[0] != global_rows ||
+      t->dimensions[1] != global_cols) {
+    return artifact_error("artifact tensor has an unexpected shape or format: " + name);
+  }
+  const std::uint64_t code_bytes = static_cast<std::uint64_t>(global_rows) * global_cols * b / 8;
+  const std::uint64_t scale_bytes = static_cast<std::uint64_t>(global_rows) * (global_cols / 128) * 2;
+  if (t->data_bytes != code_bytes || t->aux_bytes != scale_bytes) {
+    return artifact_error("artifact tensor payload sizes do not match its shape: " + name);
+  }
+  if (src.gfx12 && b == 3 && !src.sequential_w3) {
+    return fail(GFXB_UNSUPPORTED, "bit-plane W3 tiles (recipes without w3seq) are not supported");
+  }
+  *bits = b;
+  return GFXB_OK;
+}
+
+// Copies this shard's rows (row segments) and columns (one 128-group range)
+// of a [global_rows][global_cols] tensor stored as [N/16][K/128][block] (both
+// the b200 and the gfx12 tiled layouts, and the tiled scales, have this
+// blocking) into a packed local block array.
+int copy_blocks(const std::byte* source, std::uint32_t global_cols, std::uint32_t block_bytes, std::uint8_t* dest,
+                std::uint32_t cols, std::uint32_t col_offset, const std::vector<std::uint32_t>& local_begin,
+                const std::vector<std::uint32_t>& global_begin, std::uint32_t rows, cudaStream_t stream) {
+  const std::size_t G = global_cols / 128, g0 = col_offset / 128, ng = cols / 128;
+  for (std::size_t i = 0; i < local_begin.size(); ++i) {
+    const std::uint32_t end = i + 1 < local_begin.size() ? local_begin[i + 1] : rows;
+    const std::size_t tiles = (end - local_begin[i]) / 16, t_src = global_begin[i] / 16, t_dst = local_begin[i] / 16;
+    if (tiles == 0) continue;
+    GFXB_TRY(cuda_check(cudaMemcpy2DAsync(dest + t_dst * ng * block_bytes, ng * block_bytes,
+                                          source + (t_src * G + g0) * block_bytes, G * block_bytes, ng * block_bytes,
+                                          tiles, cudaMemcpyHostToDevice, stream),
+                        "weight upload failed"));
+  }
+  return GFXB_OK;
+}
+
+// Plans (pass 1) or places and fills (pass 2) every weight of the shard.
+int build_weights(gfxb_engine& e, Planner& plan, bool generate, WeightSource& src) {
   const gfxb_model_config& c = e.cfg;
   const Shard& s = e.shard;
   const cudaStream_t stream = e.stream;
   const std::uint64_t seed = c.seed;
-  auto matrix = [&](QMatrix& m, std::uint32_t tensor, std::uint32_t bits, std::uint32_t rows, std::uint32_t cols,
-                    std::uint32_t global_cols, std::uint32_t col_offset, std::vector<std::uint32_t> local_begin,
-                    std::vector<std::uint32_t> global_begin) -> int {
+  auto matrix = [&](QMatrix& m, std::uint32_t tensor, const std::string& name, std::uint32_t bits, std::uint32_t rows,
+                    std::uint32_t cols, std::uint32_t global_rows, std::uint32_t global_cols, std::uint32_t col_offset,
+                    std::vector<std::uint32_t> local_begin, std::vector<std::uint32_t> global_begin) -> int {
+    if (src.view != nullptr) {
+      int b = 0;
+      GFXB_TRY(check_matrix_tensor(*src.view, src, name, global_rows, global_cols, &b));
+      bits = static_cast<std::uint32_t>(b);
+    }
     m.format = format_of(bits);
     m.rows = rows;
     m.cols = cols;
-    m.codes = plan.take<std::uint8_t>(static_cast<std::size_t>(rows) * cols * bits / 8);
+    const std::size_t code_bytes = static_cast<std::size_t>(rows) * cols * bits / 8;
+    m.codes = plan.take<std::uint8_t>(code_bytes);
     m.scales = plan.take<std::uint16_t>(static_cast<std::size_t>(rows) * (cols / 128));
+    if (src.view != nullptr && src.gfx12) src.scratch_bytes = std::max(src.scratch_bytes, code_bytes);
     if (!generate) return GFXB_OK;
-    return generate_b200_weights(seed, tensor, m.format, m.codes, m.scales, rows, cols, global_cols, col_offset,
-                                 local_begin.data(), global_begin.data(),
-                                 static_cast<std::uint32_t>(local_begin.size()), stream);
+    if (src.view == nullptr) {
+      return generate_b200_weights(seed, tensor, m.format, m.codes, m.scales, rows, cols, global_cols, col_offset,
+                                   local_begin.data(), global_begin.data(),
+                                   static_cast<std::uint32_t>(local_begin.size()), stream);
+    }
+    const gfxi::Tensor& t = *src.view->find(name);
+    std::uint8_t* codes = src.gfx12 ? src.scratch : m.codes;
+    GFXB_TRY(copy_blocks(src.view->data(t), global_cols, bits * 256u, codes, cols, col_offset, local_begin,
+                         global_begin, rows, stream));
+    GFXB_TRY(copy_blocks(src.view->aux(t), global_cols, 32u, reinterpret_cast<std::uint8_t*>(m.scales), cols,
+                         col_offset, local_begin, global_begin, rows, stream));
+    if (src.gfx12) return gfxb_repack_gfx12_to_b200(m.format, src.scratch, m.codes, rows, cols, stream);
+    return GFXB_OK;
   };
-  auto simple = [&](QMatrix& m, std::uint32_t tensor, std::uint32_t bits, std::uint32_t rows, std::uint32_t cols,
-                    std::uint32_t row0, std::uint32_t global_cols, std::uint32_t col0) -> int {
-    return matrix(m, tensor, bits, rows, cols, global_cols, col0, {0}, {row0});
+  auto simple = [&](QMatrix& m, std::uint32_t tensor, const std::string& name, std::uint32_t bits, std::uint32_t rows,
+                    std::uint32_t cols, std::uint32_t row0, std::uint32_t global_rows, std::uint32_t global_cols,
+                    std::uint32_t col0) -> int {
+    return matrix(m, tensor, name, bits, rows, cols, global_rows, global_cols, col0, {0}, {row0});
   };
-  auto vector_bf16 = [&](std::uint16_t*& out, std::uint32_t tensor, std::uint64_t count, std::uint64_t offset,
-                         float lo, float hi) -> int {
+  // bf16 vectors: `count` values from element `offset` (of `total`) of the tensor
+  auto vector_bf16 = [&](std::uint16_t*& out, std::uint32_t tensor, const std::string& name, std::uint64_t count,
+                         std::uint64_t offset, std::uint64_t total, float lo, float hi) -> int {
     out = plan.take<std::uint16_t>(count);
+    if (src.view != nullptr) {
+      const gfxi::Tensor* t = src.view->find(name);
+      if (t == nullptr) return artifact_error("artifact lacks " + name);
+      std::uint64_t elements = t->rank == 0 ? 0 : 1;
+      for (std::uint16_t d = 0; d < t->rank; ++d) elements *= t->dimensions[d];
+      if (t->dtype != GFXB_DTYPE_BF16 || t->quantization != GFXB_QUANT_NONE || elements != total ||
+          t->data_bytes != total * 2) {
+        return artifact_error("artifact tensor has an unexpected shape or type: " + name);
+      }
+      if (!generate) return GFXB_OK;
+      return cuda_check(cudaMemcpyAsync(out, src.view->data(*t) + offset * 2, count * 2, cudaMemcpyHostToDevice, stream),
+                        "weight upload failed");
+    }
     if (!generate) return GFXB_OK;
     return generate_bf16(seed, tensor, offset, count, lo, hi, out, stream);
   };
   const std::uint32_t H = c.hidden;
   auto mlp = [&](Layer& L, std::uint32_t id) -> int {
-    GFXB_TRY(vector_bf16(L.input_norm, tensor_id(id, kInputNorm), H, 0, -0.1f, 0.1f));
-    GFXB_TRY(vector_bf16(L.post_norm, tensor_id(id, kPostNorm), H, 0, -0.1f, 0.1f));
-    GFXB_TRY(simple(L.gate, tensor_id(id, kGate), c.mlp_bits, s.inter, H, s.i0, H, 0));
-    GFXB_TRY(simple(L.up, tensor_id(id, kUp), c.mlp_bits, s.inter, H, s.i0, H, 0));
-    GFXB_TRY(simple(L.down, tensor_id(id, kDown), c.mlp_bits, H, s.inter, 0, c.intermediate, s.i0));
+    GFXB_TRY(vector_bf16(L.input_norm, tensor_id(id, kInputNorm), layer_name(id, "input_layernorm.weight"), H, 0, H,
+                         -0.1f, 0.1f));
+    GFXB_TRY(vector_bf16(L.post_norm, tensor_id(id, kPostNorm), layer_name(id, "post_attention_layernorm.weight"), H, 0,
+                         H, -0.1f, 0.1f));
+    GFXB_TRY(simple(L.gate, tensor_id(id, kGate), layer_name(id, "mlp.gate_proj.weight"), c.mlp_bits, s.inter, H, s.i0,
+                    c.intermediate, H, 0));
+    GFXB_TRY(simple(L.up, tensor_id(id, kUp), layer_name(id, "mlp.up_proj.weight"), c.mlp_bits, s.inter, H, s.i0,
+                    c.intermediate, H, 0));
+    GFXB_TRY(simple(L.down, tensor_id(id, kDown), layer_name(id, "mlp.down_proj.weight"), c.mlp_bits, H, s.inter, 0, H,
+                    c.intermediate, s.i0));
+    if (L.gate.format != L.up.format) return artifact_error("gate and up projections differ in format");
     return GFXB_OK;
   };
   auto attention = [&](Layer& L, std::uint32_t id) -> int {
-    GFXB_TRY(simple(L.q, tensor_id(id, kQ), c.proj_bits, s.nq * 512, H, s.qh0 * 512, H, 0));
-    GFXB_TRY(simple(L.k, tensor_id(id, kK), c.proj_bits, s.nkv * 256, H, s.kv0 * 256, H, 0));
-    GFXB_TRY(simple(L.v, tensor_id(id, kV), c.proj_bits, s.nkv * 256, H, s.kv0 * 256, H, 0));
-    GFXB_TRY(simple(L.out, tensor_id(id, kO), c.proj_bits, H, s.nq * 256, 0, c.q_heads * 256, s.qh0 * 256));
-    GFXB_TRY(vector_bf16(L.q_norm, tensor_id(id, kQNorm), 256, 0, -0.1f, 0.1f));
-    GFXB_TRY(vector_bf16(L.k_norm, tensor_id(id, kKNorm), 256, 0, -0.1f, 0.1f));
+    GFXB_TRY(simple(L.q, tensor_id(id, kQ), layer_name(id, "self_attn.q_proj.weight"), c.proj_bits, s.nq * 512, H,
+                    s.qh0 * 512, c.q_heads * 512, H, 0));
+    GFXB_TRY(simple(L.k, tensor_id(id, kK), layer_name(id, "self_attn.k_proj.weight"), c.proj_bits, s.nkv * 256, H,
+                    s.kv0 * 256, c.kv_heads * 256, H, 0));
+    GFXB_TRY(simple(L.v, tensor_id(id, kV), layer_name(id, "self_attn.v_proj.weight"), c.proj_bits, s.nkv * 256, H,
+                    s.kv0 * 256, c.kv_heads * 256, H, 0));
+    GFXB_TRY(simple(L.out, tensor_id(id, kO), layer_name(id, "self_attn.o_proj.weight"), c.proj_bits, H, s.nq * 256, 0,
+                    H, c.q_heads * 256, s.qh0 * 256));
+    GFXB_TRY(vector_bf16(L.q_norm, tensor_id(id, kQNorm), layer_name(id, "self_attn.q_norm.weight"), 256, 0, 256,
+                         -0.1f, 0.1f));
+    GFXB_TRY(vector_bf16(L.k_norm, tensor_id(id, kKNorm), layer_name(id, "self_attn.k_norm.weight"), 256, 0, 256,
+                         -0.1f, 0.1f));
+    if (L.q.format != L.k.format || L.q.format != L.v.format) {
+      return artifact_error("q/k/v projections differ in format");
+    }
     return GFXB_OK;
   };
   auto gdn = [&](Layer& L, std::uint32_t id) -> int {
     const std::uint32_t nk_all = c.gdn_key_heads * 128, nv_all = c.gdn_value_heads * 128;
-    GFXB_TRY(matrix(L.qkv, tensor_id(id, kQkv), c.proj_bits, s.channels, H, H, 0,
-                    {0, s.nk * 128, 2 * s.nk * 128}, {s.kh0 * 128, nk_all + s.kh0 * 128, 2 * nk_all + s.vh0 * 128}));
-    GFXB_TRY(simple(L.z, tensor_id(id, kZ), c.proj_bits, s.nv * 128, H, s.vh0 * 128, H, 0));
-    GFXB_TRY(simple(L.a, tensor_id(id, kA), c.proj_bits, c.gdn_value_heads, H, 0, H, 0));
-    GFXB_TRY(simple(L.b, tensor_id(id, kB), c.proj_bits, c.gdn_value_heads, H, 0, H, 0));
-    GFXB_TRY(simple(L.out, tensor_id(id, kGdnOut), c.proj_bits, H, s.nv * 128, 0, nv_all, s.vh0 * 128));
-    // conv weights [channels][4] follow the qkv channel map
+    const std::uint32_t channels_all = 2 * nk_all + nv_all;
+    GFXB_TRY(matrix(L.qkv, tensor_id(id, kQkv), layer_name(id, "linear_attn.in_proj_qkv.weight"), c.proj_bits,
+                    s.channels, H, channels_all, H, 0, {0, s.nk * 128, 2 * s.nk * 128},
+                    {s.kh0 * 128, nk_all + s.kh0 * 128, 2 * nk_all + s.vh0 * 128}));
+    GFXB_TRY(simple(L.z, tensor_id(id, kZ), layer_name(id, "linear_attn.in_proj_z.weight"), c.proj_bits, s.nv * 128, H,
+                    s.vh0 * 128, nv_all, H, 0));
+    GFXB_TRY(simple(L.a, tensor_id(id, kA), layer_name(id, "linear_attn.in_proj_a.weight"), c.proj_bits,
+                    c.gdn_value_heads, H, 0, c.gdn_value_heads, H, 0));
+    GFXB_TRY(simple(L.b, tensor_id(id, kB), layer_name(id, "linear_attn.in_proj_b.weight"), c.proj_bits,
+                    c.gdn_value_heads, H, 0, c.gdn_value_heads, H, 0));
+    GFXB_TRY(simple(L.out, tensor_id(id, kGdnOut), layer_name(id, "linear_attn.out_proj.weight"), c.proj_bits, H,
+                    s.nv * 128, 0, H, nv_all, s.vh0 * 128));
+    if (L.qkv.format != L.z.format || L.qkv.format != L.a.format || L.qkv.format != L.b.format) {
+      return artifact_error("GDN input projections differ in format");
+    }
+    // conv weights [channels][4] (reference [channels][1][4]) follow the qkv channel map
     L.conv = plan.take<std::uint16_t>(static_cast<std::size_t>(s.channels) * 4);
+    const std::uint64_t starts[3] = {static_cast<std::uint64_t>(s.kh0) * 128, nk_all + static_cast<std::uint64_t>(s.kh0) * 128,
+                                     2ull * nk_all + static_cast<std::uint64_t>(s.vh0) * 128};
+    const std::uint64_t counts[3] = {s.nk * 128ull, s.nk * 128ull, s.nv * 128ull};
+    const std::string conv_name = layer_name(id, "linear_attn.conv1d.weight");
+    const gfxi::Tensor* conv = nullptr;
+    if (src.view != nullptr) {
+      conv = src.view->find(conv_name);
+      if (conv == nullptr || conv->dtype != GFXB_DTYPE_BF16 || conv->data_bytes != channels_all * 8ull) {
+        return artifact_error("artifact lacks a valid " + conv_name);
+      }
+    }
     if (generate) {
       const std::uint32_t tensor = tensor_id(id, kConv);
-      const std::uint64_t starts[3] = {static_cast<std::uint64_t>(s.kh0) * 128, nk_all + static_cast<std::uint64_t>(s.kh0) * 128,
-                                       2ull * nk_all + static_cast<std::uint64_t>(s.vh0) * 128};
-      const std::uint64_t counts[3] = {s.nk * 128ull, s.nk * 128ull, s.nv * 128ull};
       std::uint64_t local = 0;
       for (int i = 0; i < 3; ++i) {
-        GFXB_TRY(generate_bf16(seed, tensor, starts[i] * 4, counts[i] * 4, -0.5f, 0.5f, L.conv + local * 4, stream));
+        if (conv != nullptr) {
+          GFXB_TRY(cuda_check(cudaMemcpyAsync(L.conv + local * 4, src.view->data(*conv) + starts[i] * 8, counts[i] * 8,
+                                              cudaMemcpyHostToDevice, stream),
+                              "weight upload failed"));
+        } else {
+          GFXB_TRY(generate_bf16(seed, tensor, starts[i] * 4, counts[i] * 4, -0.5f, 0.5f, L.conv + local * 4, stream));
+        }
         local += counts[i];
       }
     }
-    GFXB_TRY(vector_bf16(L.a_log, tensor_id(id, kALog), s.nv, s.vh0, -1.0f, 1.0f));
-    GFXB_TRY(vector_bf16(L.dt_bias, tensor_id(id, kDtBias), s.nv, s.vh0, -1.0f, 1.0f));
-    GFXB_TRY(vector_bf16(L.gdn_norm, tensor_id(id, kGdnNorm), 128, 0, 0.8f, 1.2f));
+    GFXB_TRY(vector_bf16(L.a_log, tensor_id(id, kALog), layer_name(id, "linear_attn.A_log"), s.nv, s.vh0,
+                         c.gdn_value_heads, -1.0f, 1.0f));
+    GFXB_TRY(vector_bf16(L.dt_bias, tensor_id(id, kDtBias), layer_name(id, "linear_attn.dt_bias"), s.nv, s.vh0,
+                         c.gdn_value_heads, -1.0f, 1.0f));
+    GFXB_TRY(vector_bf16(L.gdn_norm, tensor_id(id, kGdnNorm), layer_name(id, "linear_attn.norm.weight"), 128, 0, 128,
+                         0.8f, 1.2f));
     return GFXB_OK;
   };
   e.layers.resize(c.layers);
@@ -309,24 +452,57 @@ int build_weights(gfxb_engine& e, Planner& plan, bool generate) {
   }
   // embedding (row-major, replicated), LM head (vocabulary rows), final norm
   {
-    const int format = format_of(c.emb_bits);
-    e.emb_codes = plan.take<std::uint8_t>(static_cast<std::size_t>(c.vocab) * H * c.emb_bits / 8);
+    std::uint32_t emb_bits = c.emb_bits;
+    const char* emb_name = "model.language_model.embed_tokens.weight";
+    if (src.view != nullptr) {
+      int b = 0;
+      GFXB_TRY(check_matrix_tensor(*src.view, src, emb_name, c.vocab, H, &b));
+      if (b == 3) return fail(GFXB_UNSUPPORTED, "the embedding must be W2 or W4");
+      emb_bits = static_cast<std::uint32_t>(b);
+    }
+    const int format = format_of(emb_bits);
+    const std::size_t code_bytes = static_cast<std::size_t>(c.vocab) * H * emb_bits / 8;
+    const std::size_t scale_bytes = static_cast<std::size_t>(c.vocab) * (H / 128) * 2;
+    e.emb_codes = plan.take<std::uint8_t>(code_bytes);
     e.emb_scales = plan.take<std::uint16_t>(static_cast<std::size_t>(c.vocab) * (H / 128));
-    if (generate) {
+    if (src.view != nullptr && src.gfx12) src.scratch_bytes = std::max(src.scratch_bytes, code_bytes + scale_bytes + 256);
+    if (generate && src.view == nullptr) {
       GFXB_TRY(generate_rowmajor_weights(seed, tensor_id(kLayerGlobal, kEmbedding), format, e.emb_codes, e.emb_scales,
                                          c.vocab, H, stream));
+    } else if (generate) {
+      const gfxi::Tensor& t = *src.view->find(emb_name);
+      if (src.gfx12) {
+        std::uint8_t* staged_scales = src.scratch + ((code_bytes + 255) & ~std::size_t{255});
+        GFXB_TRY(cuda_check(cudaMemcpyAsync(src.scratch, src.view->data(t), code_bytes, cudaMemcpyHostToDevice, stream),
+                            "weight upload failed"));
+        GFXB_TRY(cuda_check(cudaMemcpyAsync(staged_scales, src.view->aux(t), scale_bytes, cudaMemcpyHostToDevice, stream),
+                            "weight upload failed"));
+        GFXB_TRY(untile_gfx12_rowmajor(format, src.scratch, reinterpret_cast<const std::uint16_t*>(staged_scales),
+                                       e.emb_codes, e.emb_scales, c.vocab, H, stream));
+      } else {
+        GFXB_TRY(cuda_check(cudaMemcpyAsync(e.emb_codes, src.view->data(t), code_bytes, cudaMemcpyHostToDevice, stream),
+                            "weight upload failed"));
+        GFXB_TRY(cuda_check(cudaMemcpyAsync(e.emb_scales, src.view->aux(t), scale_bytes, cudaMemcpyHostToDevice, stream),
+                            "weight upload failed"));
+      }
     }
+    e.cfg.emb_bits = emb_bits;
   }
-  GFXB_TRY(simple(e.lm_head, tensor_id(kLayerGlobal, kLmHead), c.head_bits, s.vocab, H, s.v0, H, 0));
-  GFXB_TRY(vector_bf16(e.final_norm, tensor_id(kLayerGlobal, kFinalNorm), H, 0, -0.1f, 0.1f));
+  GFXB_TRY(simple(e.lm_head, tensor_id(kLayerGlobal, kLmHead), "lm_head.weight", c.head_bits, s.vocab, H, s.v0, c.vocab,
+                  H, 0));
+  GFXB_TRY(vector_bf16(e.final_norm, tensor_id(kLayerGlobal, kFinalNorm), "model.language_model.norm.weight", H, 0, H,
+                       -0.1f, 0.1f));
   if (e.has_mtp) {
     e.mtp.attention = true;
     GFXB_TRY(mlp(e.mtp, kLayerMtp));
     GFXB_TRY(attention(e.mtp, kLayerMtp));
-    GFXB_TRY(simple(e.fc, tensor_id(kLayerMtp, kFc), c.proj_bits, H, s.fc_cols, 0, 2 * H, s.fc0));
-    GFXB_TRY(vector_bf16(e.pre_emb_norm, tensor_id(kLayerMtp, kPreEmbNorm), H, 0, -0.1f, 0.1f));
-    GFXB_TRY(vector_bf16(e.pre_hidden_norm, tensor_id(kLayerMtp, kPreHiddenNorm), H, 0, -0.1f, 0.1f));
-    GFXB_TRY(vector_bf16(e.mtp_final_norm, tensor_id(kLayerMtp, kMtpFinalNorm), H, 0, -0.1f, 0.1f));
+    GFXB_TRY(simple(e.fc, tensor_id(kLayerMtp, kFc), "mtp.fc.weight", c.proj_bits, H, s.fc_cols, 0, H, 2 * H, s.fc0));
+    GFXB_TRY(vector_bf16(e.pre_emb_norm, tensor_id(kLayerMtp, kPreEmbNorm), "mtp.pre_fc_norm_embedding.weight", H, 0, H,
+                         -0.1f, 0.1f));
+    GFXB_TRY(vector_bf16(e.pre_hidden_norm, tensor_id(kLayerMtp, kPreHiddenNorm), "mtp.pre_fc_norm_hidden.weight", H, 0,
+                         H, -0.1f, 0.1f));
+    GFXB_TRY(vector_bf16(e.mtp_final_norm, tensor_id(kLayerMtp, kMtpFinalNorm), "mtp.norm.weight", H, 0, H, -0.1f,
+                         0.1f));
   }
   return GFXB_OK;
 }
@@ -1075,33 +1251,51 @@ extern "C" int gfxb_tp_shard(const gfxb_model_config* config, int tp_rank, int t
   return GFXB_OK;
 }
 
-extern "C" int gfxb_engine_create_synthetic(const gfxb_model_config* config, int device, int tp_rank, int tp_size,
-                                            const void* nccl_id128, int include_mtp, gfxb_engine** out) {
-  if (config == nullptr || out == nullptr) return fail(GFXB_INVALID_ARGUMENT, "engine arguments are null");
+namespace gfxb {
+namespace {
+
+int create_engine(const gfxb_model_config& config, int device, int tp_rank, int tp_size, const void* nccl_id128,
+                  bool include_mtp, WeightSource& src, gfxb_engine** out) {
   *out = nullptr;
   if (tp_size < 1 || tp_size > 8 || tp_rank < 0 || tp_rank >= tp_size) {
     return fail(GFXB_INVALID_ARGUMENT, "tensor-parallel rank/size are invalid");
   }
   if (tp_size > 1 && nccl_id128 == nullptr) return fail(GFXB_INVALID_ARGUMENT, "TP > 1 requires an NCCL id");
-  GFXB_TRY(validate_config(*config, static_cast<std::uint32_t>(tp_size)));
+  GFXB_TRY(validate_config(config, static_cast<std::uint32_t>(tp_size)));
   GFXB_TRY(gfxb_require_sm100_device(device, nullptr));
   GFXB_TRY(cuda_check(cudaSetDevice(device), "cudaSetDevice failed"));
   auto e = std::make_unique<gfxb_engine>();
-  e->cfg = *config;
+  e->cfg = config;
   e->device = device;
-  e->has_mtp = include_mtp != 0;
-  e->shard = make_shard(*config, static_cast<std::uint32_t>(tp_size), static_cast<std::uint32_t>(tp_rank));
+  e->has_mtp = include_mtp;
+  e->shard = make_shard(config, static_cast<std::uint32_t>(tp_size), static_cast<std::uint32_t>(tp_rank));
   GFXB_TRY(cuda_check(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream creation failed"));
   Planner plan;
-  GFXB_TRY(build_weights(*e, plan, false));
+  int status = build_weights(*e, plan, false, src);
+  if (status != GFXB_OK) {
+    cudaStreamDestroy(e->stream);
+    return status;
+  }
   e->arena_bytes = plan.offset;
   void* arena = nullptr;
-  GFXB_TRY(cuda_check(cudaMalloc(&arena, e->arena_bytes), "weight arena allocation failed"));
+  status = cuda_check(cudaMalloc(&arena, e->arena_bytes), "weight arena allocation failed");
+  if (status == GFXB_OK && src.scratch_bytes != 0) {
+    void* scratch = nullptr;
+    status = cuda_check(cudaMalloc(&scratch, src.scratch_bytes), "repack staging allocation failed");
+    src.scratch = static_cast<std::uint8_t*>(scratch);
+  }
   e->arena = static_cast<std::byte*>(arena);
-  Planner place;
-  place.base = e->arena;
-  int status = build_weights(*e, place, true);
-  if (status == GFXB_OK) status = cuda_check(cudaStreamSynchronize(e->stream), "weight generation failed");
+  if (status == GFXB_OK) {
+    Planner place;
+    place.base = e->arena;
+    status = build_weights(*e, place, true, src);
+  }
+  if (status == GFXB_OK) status = cuda_check(cudaStreamSynchronize(e->stream), "weight upload failed");
+  if (src.scratch != nullptr) {
+    cudaStreamSynchronize(e->stream);
+    cudaFree(src.scratch);
+    src.scratch = nullptr;
+  }
   if (status == GFXB_OK && tp_size > 1) {
     status = load_nccl(nccl());
     if (status == GFXB_OK) {
@@ -1116,6 +1310,283 @@ extern "C" int gfxb_engine_create_synthetic(const gfxb_model_config* config, int
     return status;
   }
   *out = e.release();
+  return GFXB_OK;
+}
+
+// Model shape of an artifact from its tensor shapes (the reference inventory,
+// qwen38_spec.cpp:32-102): hidden and vocabulary from the embedding, layer
+// count and attention placement from the per-layer names, head counts from
+// the projection heights.
+int derive_config(const gfxi::View& view, const gfxb_artifact_load_options& options, gfxb_model_config& c) {
+  c = gfxb_model_config{};
+  const gfxi::Tensor* emb = view.find("model.language_model.embed_tokens.weight");
+  const gfxi::Tensor* head = view.find("lm_head.weight");
+  if (emb == nullptr || head == nullptr || view.find("model.language_model.norm.weight") == nullptr) {
+    return artifact_error("artifact lacks embedding, final norm, or LM head");
+  }
+  if (emb->rank != 2 || head->rank != 2 || head->dimensions[0] != emb->dimensions[0] ||
+      head->dimensions[1] != emb->dimensions[1] || emb->dimensions[0] > 0xffffffffull ||
+      emb->dimensions[1] > 0xffffffffull) {
+    return artifact_error("embedding and LM head shapes disagree");
+  }
+  c.vocab = static_cast<std::uint32_t>(emb->dimensions[0]);
+  c.hidden = static_cast<std::uint32_t>(emb->dimensions[1]);
+  c.emb_bits = static_cast<std::uint32_t>(bits_of_quantization(emb->quantization));
+  c.head_bits = static_cast<std::uint32_t>(bits_of_quantization(head->quantization));
+  while (view.find(layer_name(c.layers, "input_layernorm.weight")) != nullptr) ++c.layers;
+  if (c.layers == 0) return artifact_error("artifact has no decoder layers");
+  std::int64_t first_attention = -1, first_gdn = -1;
+  for (std::uint32_t i = 0; i < c.layers; ++i) {
+    const bool attention = view.find(layer_name(i, "self_attn.q_proj.weight")) != nullptr;
+    if (attention && first_attention < 0) first_attention = i;
+    if (!attention && first_gdn < 0) first_gdn = i;
+  }
+  c.attention_interval = first_attention < 0 ? c.layers + 1 : static_cast<std::uint32_t>(first_attention) + 1;
+  for (std::uint32_t i = 0; i < c.layers; ++i) {
+    const bool attention = view.find(layer_name(i, "self_attn.q_proj.weight")) != nullptr;
+    if (attention != ((i + 1) % c.attention_interval == 0)) {
+      return fail(GFXB_UNSUPPORTED, "attention layers must repeat with a fixed interval");
+    }
+  }
+  const gfxi::Tensor* gate = view.find(layer_name(0, "mlp.gate_proj.weight"));
+  if (gate == nullptr || gate->rank != 2) return artifact_error("artifact lacks layer 0's MLP");
+  c.intermediate = static_cast<std::uint32_t>(gate->dimensions[0]);
+  c.mlp_bits = static_cast<std::uint32_t>(bits_of_quantization(gate->quantization));
+  c.gdn_key_heads = 16;  // placeholders for models without GDN or attention layers
+  c.gdn_value_heads = 48;
+  c.q_heads = 24;
+  c.kv_heads = 4;
+  c.proj_bits = 4;
+  if (first_gdn >= 0) {
+    const std::uint32_t id = static_cast<std::uint32_t>(first_gdn);
+    const gfxi::Tensor* qkv = view.find(layer_name(id, "linear_attn.in_proj_qkv.weight"));
+    const gfxi::Tensor* a_log = view.find(layer_name(id, "linear_attn.A_log"));
+    if (qkv == nullptr || a_log == nullptr || a_log->rank != 1) return artifact_error("artifact lacks a GDN layer's tensors");
+    c.gdn_value_heads = static_cast<std::uint32_t>(a_log->dimensions[0]);
+    const std::uint64_t key_rows = qkv->dimensions[0] - static_cast<std::uint64_t>(c.gdn_value_heads) * 128;
+    if (qkv->dimensions[0] <= static_cast<std::uint64_t>(c.gdn_value_heads) * 128 || key_rows % 256 != 0) {
+      return artifact_error("GDN qkv projection height is inconsistent with its heads");
+    }
+    c.gdn_key_heads = static_cast<std::uint32_t>(key_rows / 256);
+    c.proj_bits = static_cast<std::uint32_t>(bits_of_quantization(qkv->quantization));
+  }
+  const std::uint32_t attention_id = first_attention >= 0 ? static_cast<std::uint32_t>(first_attention) : kLayerMtp;
+  const gfxi::Tensor* q = view.find(layer_name(attention_id, "self_attn.q_proj.weight"));
+  const gfxi::Tensor* k = view.find(layer_name(attention_id, "self_attn.k_proj.weight"));
+  if (q != nullptr && k != nullptr) {
+    c.q_heads = static_cast<std::uint32_t>(q->dimensions[0] / 512);
+    c.kv_heads = static_cast<std::uint32_t>(k->dimensions[0] / 256);
+    if (first_gdn < 0) c.proj_bits = static_cast<std::uint32_t>(bits_of_quantization(q->quantization));
+  } else if (first_attention >= 0) {
+    return artifact_error("artifact lacks an attention layer's projections");
+  }
+  c.activation_bits = options.activation_bits;
+  c.max_context = options.max_context;
+  c.draft_vocab = options.draft_vocab != 0 ? options.draft_vocab : std::min<std::uint32_t>(98304u, c.vocab);
+  if (c.draft_vocab > c.vocab || c.draft_vocab % 16 != 0) return fail(GFXB_INVALID_ARGUMENT, "invalid MTP draft vocabulary");
+  c.seed = 0;
+  return GFXB_OK;
+}
+
+bool has_substring(const char* text, const char* part) { return std::strstr(text, part) != nullptr; }
+
+}  // namespace
+}  // namespace gfxb
+
+extern "C" int gfxb_engine_create_synthetic(const gfxb_model_config* config, int device, int tp_rank, int tp_size,
+                                            const void* nccl_id128, int include_mtp, gfxb_engine** out) {
+  if (config == nullptr || out == nullptr) return fail(GFXB_INVALID_ARGUMENT, "engine arguments are null");
+  WeightSource synthetic;
+  return create_engine(*config, device, tp_rank, tp_size, nccl_id128, include_mtp != 0, synthetic, out);
+}
+
+extern "C" int gfxb_engine_create_from_artifact(const char* path, const gfxb_artifact_load_options* options,
+                                                int device, int tp_rank, int tp_size, const void* nccl_id128,
+                                                gfxb_engine** out) {
+  if (path == nullptr || options == nullptr || out == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  gfxi::View view;
+  GFXB_TRY(view.open(path, options->verify_checksums != 0));
+  const gfxb_artifact_identity& id = view.identity();
+  if (std::strcmp(id.target_arch, "sm_100a") != 0 && std::strcmp(id.target_arch, "gfx1200") != 0) {
+    const std::string message = std::string("artifact target is ") + id.target_arch + "; expected sm_100a or gfx1200";
+    return fail(GFXB_UNSUPPORTED, message.c_str());
+  }
+  if (std::strcmp(id.model_id, "qwen3.8-27b") != 0 && std::strcmp(id.model_id, "qwen-hybrid") != 0) {
+    const std::string message = std::string("artifact model is ") + id.model_id + "; expected qwen3.8-27b or qwen-hybrid";
+    return fail(GFXB_UNSUPPORTED, message.c_str());
+  }
+  WeightSource src;
+  src.view = &view;
+  if (std::strcmp(id.recipe_id, "b200-v1") == 0) {
+    src.gfx12 = false;
+  } else if (has_substring(id.recipe_id, "tiled-v")) {
+    src.gfx12 = true;
+    src.sequential_w3 = has_substring(id.recipe_id, "w3seq");
+  } else {
+    const std::string message = std::string("artifact recipe ") + id.recipe_id + " is not a tiled or b200 recipe";
+    return fail(GFXB_UNSUPPORTED, message.c_str());
+  }
+  gfxb_model_config config{};
+  GFXB_TRY(derive_config(view, *options, config));
+  if (options->include_mtp != 0 && view.find("mtp.fc.weight") == nullptr) {
+    return fail(GFXB_CORRUPT_ARTIFACT, "artifact lacks the MTP layer");
+  }
+  return create_engine(config, device, tp_rank, tp_size, nccl_id128, options->include_mtp != 0, src, out);
+}
+
+namespace gfxb {
+namespace {
+
+struct ExportItem {
+  gfxi::Plan plan;
+  const void* data = nullptr;  // device
+  const void* aux = nullptr;   // device
+};
+
+void export_matrix(std::vector<ExportItem>& items, const std::string& name, const QMatrix& m) {
+  ExportItem item;
+  item.plan.name = name;
+  item.plan.dtype = GFXB_DTYPE_U8;
+  item.plan.quantization = static_cast<std::uint16_t>(m.format);  // GFXB_W* equal the Quantization values
+  item.plan.dimensions = {m.rows, m.cols};
+  const int bits = m.format == GFXB_W2 ? 2 : (m.format == GFXB_W3 ? 3 : 4);
+  item.plan.data_bytes = static_cast<std::uint64_t>(m.rows) * m.cols * bits / 8;
+  item.plan.aux_bytes = static_cast<std::uint64_t>(m.rows) * (m.cols / 128) * 2;
+  item.data = m.codes;
+  item.aux = m.scales;
+  items.push_back(std::move(item));
+}
+
+void export_bf16(std::vector<ExportItem>& items, const std::string& name, const std::uint16_t* values,
+                 std::vector<std::uint64_t> dimensions) {
+  ExportItem item;
+  item.plan.name = name;
+  item.plan.dtype = GFXB_DTYPE_BF16;
+  item.plan.quantization = GFXB_QUANT_NONE;
+  std::uint64_t count = 1;
+  for (std::uint64_t d : dimensions) count *= d;
+  item.plan.dimensions = std::move(dimensions);
+  item.plan.data_bytes = count * 2;
+  item.data = values;
+  items.push_back(std::move(item));
+}
+
+std::vector<ExportItem> export_items(const gfxb_engine& e) {
+  const gfxb_model_config& c = e.cfg;
+  const std::uint64_t H = c.hidden;
+  std::vector<ExportItem> items;
+  auto mlp = [&](const Layer& L, std::uint32_t id) {
+    export_bf16(items, layer_name(id, "input_layernorm.weight"), L.input_norm, {H});
+    export_bf16(items, layer_name(id, "post_attention_layernorm.weight"), L.post_norm, {H});
+    export_matrix(items, layer_name(id, "mlp.gate_proj.weight"), L.gate);
+    export_matrix(items, layer_name(id, "mlp.up_proj.weight"), L.up);
+    export_matrix(items, layer_name(id, "mlp.down_proj.weight"), L.down);
+  };
+  auto attention = [&](const Layer& L, std::uint32_t id) {
+    export_matrix(items, layer_name(id, "self_attn.q_proj.weight"), L.q);
+    export_matrix(items, layer_name(id, "self_attn.k_proj.weight"), L.k);
+    export_matrix(items, layer_name(id, "self_attn.v_proj.weight"), L.v);
+    export_matrix(items, layer_name(id, "self_attn.o_proj.weight"), L.out);
+    export_bf16(items, layer_name(id, "self_attn.q_norm.weight"), L.q_norm, {256});
+    export_bf16(items, layer_name(id, "self_attn.k_norm.weight"), L.k_norm, {256});
+  };
+  for (std::uint32_t i = 0; i < c.layers; ++i) {
+    const Layer& L = e.layers[i];
+    mlp(L, i);
+    if (L.attention) {
+      attention(L, i);
+    } else {
+      const std::uint64_t channels = e.shard.channels;
+      export_matrix(items, layer_name(i, "linear_attn.in_proj_qkv.weight"), L.qkv);
+      export_matrix(items, layer_name(i, "linear_attn.in_proj_z.weight"), L.z);
+      export_matrix(items, layer_name(i, "linear_attn.in_proj_a.weight"), L.a);
+      export_matrix(items, layer_name(i, "linear_attn.in_proj_b.weight"), L.b);
+      export_matrix(items, layer_name(i, "linear_attn.out_proj.weight"), L.out);
+      export_bf16(items, layer_name(i, "linear_attn.conv1d.weight"), L.conv, {channels, 1, 4});
+      export_bf16(items, layer_name(i, "linear_attn.A_log"), L.a_log, {c.gdn_value_heads});
+      export_bf16(items, layer_name(i, "linear_attn.dt_bias"), L.dt_bias, {c.gdn_value_heads});
+      export_bf16(items, layer_name(i, "linear_attn.norm.weight"), L.gdn_norm, {128});
+    }
+  }
+  {
+    ExportItem emb;
+    emb.plan.name = "model.language_model.embed_tokens.weight";
+    emb.plan.dtype = GFXB_DTYPE_U8;
+    emb.plan.quantization = static_cast<std::uint16_t>(format_of(c.emb_bits));
+    emb.plan.dimensions = {c.vocab, H};
+    emb.plan.data_bytes = static_cast<std::uint64_t>(c.vocab) * H * c.emb_bits / 8;
+    emb.plan.aux_bytes = static_cast<std::uint64_t>(c.vocab) * (H / 128) * 2;
+    emb.data = e.emb_codes;
+    emb.aux = e.emb_scales;
+    items.push_back(std::move(emb));
+  }
+  export_matrix(items, "lm_head.weight", e.lm_head);
+  export_bf16(items, "model.language_model.norm.weight", e.final_norm, {H});
+  if (e.has_mtp) {
+    mlp(e.mtp, kLayerMtp);
+    attention(e.mtp, kLayerMtp);
+    export_matrix(items, "mtp.fc.weight", e.fc);
+    export_bf16(items, "mtp.pre_fc_norm_embedding.weight", e.pre_emb_norm, {H});
+    export_bf16(items, "mtp.pre_fc_norm_hidden.weight", e.pre_hidden_norm, {H});
+    export_bf16(items, "mtp.norm.weight", e.mtp_final_norm, {H});
+  }
+  std::sort(items.begin(), items.end(), [](const ExportItem& a, const ExportItem& b) { return a.plan.name < b.plan.name; });
+  return items;
+}
+
+int copy_out(gfxi::StreamWriter& writer, std::size_t index, bool aux, const void* device, std::uint64_t bytes,
+             std::byte* staging, std::size_t staging_bytes, cudaStream_t stream) {
+  const std::byte* source = static_cast<const std::byte*>(device);
+  for (std::uint64_t done = 0; done < bytes;) {
+    const std::size_t chunk = static_cast<std::size_t>(std::min<std::uint64_t>(staging_bytes, bytes - done));
+    GFXB_TRY(cuda_check(cudaMemcpyAsync(staging, source + done, chunk, cudaMemcpyDeviceToHost, stream),
+                        "weight download failed"));
+    GFXB_TRY(cuda_check(cudaStreamSynchronize(stream), "weight download failed"));
+    GFXB_TRY(writer.append(index, aux, staging, chunk));
+    done += chunk;
+  }
+  return GFXB_OK;
+}
+
+}  // namespace
+}  // namespace gfxb
+
+extern "C" int gfxb_engine_export_artifact(gfxb_engine* engine, const char* path, const char* weights_id) {
+  if (engine == nullptr || path == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  if (engine->shard.tp != 1) return fail(GFXB_UNSUPPORTED, "export needs a single-GPU engine (the whole model)");
+  gfxb_artifact_identity identity{};
+  std::snprintf(identity.target_arch, sizeof identity.target_arch, "%s", "sm_100a");
+  std::snprintf(identity.model_id, sizeof identity.model_id, "%s", "qwen-hybrid");
+  std::snprintf(identity.recipe_id, sizeof identity.recipe_id, "%s", "b200-v1");
+  const char* weights = weights_id != nullptr && weights_id[0] != '\0' ? weights_id : "synthetic";
+  if (std::strlen(weights) >= sizeof identity.weights_id) return fail(GFXB_INVALID_ARGUMENT, "weights id is too long");
+  std::snprintf(identity.weights_id, sizeof identity.weights_id, "%s", weights);
+  GFXB_TRY(cuda_check(cudaSetDevice(engine->device), "cudaSetDevice failed"));
+  const std::vector<ExportItem> items = export_items(*engine);
+  std::vector<gfxi::Plan> plans;
+  plans.reserve(items.size());
+  for (const ExportItem& item : items) plans.push_back(item.plan);
+  gfxi::StreamWriter writer;
+  GFXB_TRY(writer.create(path, identity, plans));
+  constexpr std::size_t kStaging = 64u << 20;
+  std::byte* staging = nullptr;
+  GFXB_TRY(cuda_check(cudaMallocHost(reinterpret_cast<void**>(&staging), kStaging), "staging allocation failed"));
+  int status = GFXB_OK;
+  for (std::size_t i = 0; i < items.size() && status == GFXB_OK; ++i) {
+    status = copy_out(writer, i, false, items[i].data, items[i].plan.data_bytes, staging, kStaging, engine->stream);
+    if (status == GFXB_OK && items[i].plan.aux_bytes != 0) {
+      status = copy_out(writer, i, true, items[i].aux, items[i].plan.aux_bytes, staging, kStaging, engine->stream);
+    }
+  }
+  cudaFreeHost(staging);
+  GFXB_TRY(status);
+  return writer.finalize();
+}
+
+extern "C" int gfxb_engine_config(const gfxb_engine* engine, gfxb_model_config* config) {
+  if (engine == nullptr || config == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  *config = engine->cfg;
   return GFXB_OK;
 }
 

@@ -847,6 +847,37 @@ int launch_write_b200(const Source& source, std::uint8_t* out, std::size_t rows,
   return launch_status("b200 weight layout kernel launch failed");
 }
 
+// gfx12 tiled W2/W4 codes and tiled scales -> row-major codes and scales
+// (quantization.cpp:278-314 in reverse). For W2 and W4 a fragment holds the
+// row's 32 codes of one k-tile in row-major byte order, so each fragment is
+// one contiguous piece of the row.
+__global__ void untile_gfx12_kernel(const std::uint8_t* __restrict__ tiled, std::uint8_t* __restrict__ rowmajor,
+                                    std::uint64_t bytes, std::uint32_t groups, std::uint32_t fragment) {
+  const std::uint64_t index = static_cast<std::uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= bytes) return;
+  const std::uint64_t piece = index / fragment;
+  const std::uint32_t byte = static_cast<std::uint32_t>(index % fragment);
+  const std::uint32_t local_row = static_cast<std::uint32_t>(piece & 15u);
+  const std::uint64_t k_group = piece >> 4;  // (tile * groups + group) * 4 + k_tile
+  const std::uint32_t k_tile = static_cast<std::uint32_t>(k_group & 3u);
+  const std::uint64_t tile_group = k_group >> 2;
+  const std::uint64_t tile = tile_group / groups;
+  const std::uint32_t group = static_cast<std::uint32_t>(tile_group % groups);
+  const std::uint64_t row = tile * 16u + local_row;
+  rowmajor[row * groups * 4u * fragment + (group * 4u + k_tile) * fragment + byte] = tiled[index];
+}
+
+__global__ void untile_scales_kernel(const __half* __restrict__ tiled, __half* __restrict__ rowmajor,
+                                     std::uint64_t count, std::uint32_t groups) {
+  const std::uint64_t index = static_cast<std::uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= count) return;
+  const std::uint32_t local_row = static_cast<std::uint32_t>(index & 15u);
+  const std::uint64_t tile_group = index >> 4;
+  const std::uint64_t tile = tile_group / groups;
+  const std::uint32_t group = static_cast<std::uint32_t>(tile_group % groups);
+  rowmajor[(tile * 16u + local_row) * groups + group] = tiled[index];
+}
+
 int validate_matrix_shape(int format, std::size_t rows, std::size_t columns) {
   if (format != GFXB_W2 && format != GFXB_W3 && format != GFXB_W4) {
     return fail(GFXB_UNSUPPORTED, "weight format must be W2G128, W3G128 or W4G128");
@@ -1030,6 +1061,25 @@ int generate_bf16(std::uint64_t seed, std::uint32_t tensor, std::uint64_t offset
   gen_bf16_kernel<<<static_cast<unsigned>((count + 255) / 256), 256, 0, stream>>>(seed, tensor, offset, count, lo, hi,
                                                                                    out);
   return launch_status("synthetic bf16 generation failed");
+}
+
+int untile_gfx12_rowmajor(int format, const std::uint8_t* tiled_codes, const std::uint16_t* tiled_scales,
+                          std::uint8_t* codes, std::uint16_t* scales, std::size_t rows, std::size_t columns,
+                          cudaStream_t stream) {
+  if (format != GFXB_W2 && format != GFXB_W4) return fail(GFXB_UNSUPPORTED, "row-major untiling takes W2 or W4 codes");
+  if (rows == 0 || rows % 16 != 0 || columns == 0 || columns % kGroup != 0) {
+    return fail(GFXB_INVALID_ARGUMENT, "untiling requires N divisible by 16 and K by 128");
+  }
+  const std::uint32_t groups = static_cast<std::uint32_t>(columns / kGroup);
+  const std::uint32_t fragment = format == GFXB_W2 ? 8u : 16u;
+  const std::uint64_t bytes = static_cast<std::uint64_t>(rows) * groups * 4u * fragment;
+  untile_gfx12_kernel<<<static_cast<unsigned>((bytes + 255) / 256), 256, 0, stream>>>(tiled_codes, codes, bytes, groups,
+                                                                                       fragment);
+  GFXB_TRY(launch_status("untiling launch failed"));
+  const std::uint64_t count = static_cast<std::uint64_t>(rows) * groups;
+  untile_scales_kernel<<<static_cast<unsigned>((count + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const __half*>(tiled_scales), reinterpret_cast<__half*>(scales), count, groups);
+  return launch_status("scale untiling launch failed");
 }
 
 int read_gemv_error(std::uint32_t* value, bool clear) {

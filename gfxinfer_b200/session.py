@@ -57,6 +57,24 @@ class Engine:
                                                  int(include_mtp), ctypes.byref(handle)))
         return cls(handle.value, config)
 
+    @classmethod
+    def from_artifact(cls, path: str, device: int = 0, activation_bits: int = 4, max_context: int = 512,
+                      draft_vocab: int = 0, include_mtp: bool = True, verify_checksums: bool = True,
+                      tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None) -> "Engine":
+        """Engine::create from a `.gfxi` artifact (engine.cpp:62-216); the shape comes from the tensors."""
+        options = abi.ArtifactLoadOptions(activation_bits, max_context, draft_vocab, int(include_mtp),
+                                          int(verify_checksums))
+        handle = ctypes.c_void_p()
+        check(lib().gfxb_engine_create_from_artifact(str(path).encode(), ctypes.byref(options), device, tp_rank,
+                                                     tp_size, nccl_id, ctypes.byref(handle)))
+        engine = cls(handle.value, abi.ModelConfig())
+        check(lib().gfxb_engine_config(engine.handle, ctypes.byref(engine.config)))
+        return engine
+
+    def export_artifact(self, path: str, weights_id: str = "synthetic") -> None:
+        """Write this (single-GPU) engine's weights as a "b200-v1" artifact."""
+        check(lib().gfxb_engine_export_artifact(self._handle, str(path).encode(), weights_id.encode()))
+
     @property
     def handle(self) -> ctypes.c_void_p:
         return self._handle

@@ -163,7 +163,7 @@ class Oracle:
 
 
 class Reference:
-    """The reference's own src/quantization.cpp, built by oracle/Makefile into oracle/_ref."""
+    """The reference's own src/quantization.cpp and src/artifact.cpp, built by oracle/Makefile into oracle/_ref."""
 
     def __init__(self) -> None:
         lib = ctypes.CDLL(REF_SO)
@@ -179,9 +179,59 @@ class Reference:
         lib.ref_dequantized_weight.restype = c_float
         lib.ref_dequantized_weight.argtypes = [c_void_p, c_void_p, c_size_t, c_size_t, c_int, c_size_t, c_size_t]
 
+        lib.ref_artifact_write.restype = c_int
+        lib.ref_artifact_write.argtypes = [ctypes.c_char_p] * 5 + [c_size_t] + [c_void_p] * 10
+        lib.ref_artifact_open.restype = c_int
+        lib.ref_artifact_open.argtypes = [ctypes.c_char_p, c_int, c_void_p, c_void_p]
+        lib.ref_artifact_tensor.restype = c_int
+        lib.ref_artifact_tensor.argtypes = [ctypes.c_char_p, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p]
+
     @staticmethod
     def available() -> bool:
         return os.path.exists(REF_SO)
+
+    # -- .gfxi container (src/artifact.cpp) ---------------------------------------
+    def artifact_write(self, path: str, identity: dict, tensors: list) -> int:
+        """tensors: list of (name, dtype, quantization, dims, data_bytes_obj, aux_bytes_obj_or_None, alignment)."""
+        n = len(tensors)
+        keep = []
+        names = (ctypes.c_char_p * n)(*[t[0].encode() for t in tensors])
+        dtypes = np.array([t[1] for t in tensors], np.uint16)
+        quants = np.array([t[2] for t in tensors], np.uint16)
+        ranks = np.array([len(t[3]) for t in tensors], np.uint16)
+        dims = np.zeros((n, 4), np.uint64)
+        data_ptrs, aux_ptrs = (c_void_p * n)(), (c_void_p * n)()
+        data_bytes, aux_bytes = np.zeros(n, np.uint64), np.zeros(n, np.uint64)
+        alignments = np.array([t[6] if len(t) > 6 else 256 for t in tensors], np.uint32)
+        for i, (_, _, _, shape, data, aux, *_) in enumerate(tensors):
+            dims[i, :len(shape)] = shape
+            d = np.frombuffer(memoryview(data).cast("B"), np.uint8)
+            keep.append(d)
+            data_ptrs[i], data_bytes[i] = d.ctypes.data, d.size
+            if aux is not None:
+                a = np.frombuffer(memoryview(aux).cast("B"), np.uint8)
+                keep.append(a)
+                aux_ptrs[i], aux_bytes[i] = a.ctypes.data, a.size
+        ident = [identity[k].encode() for k in ("target_arch", "model_id", "weights_id", "recipe_id")]
+        return self.lib.ref_artifact_write(str(path).encode(), *ident, n, names, _ptr(dtypes), _ptr(quants),
+                                           _ptr(ranks), _ptr(dims), data_ptrs, _ptr(data_bytes), aux_ptrs,
+                                           _ptr(aux_bytes), _ptr(alignments))
+
+    def artifact_open(self, path: str, verify: bool = True):
+        count, size = np.zeros(1, np.uint64), np.zeros(1, np.uint64)
+        status = self.lib.ref_artifact_open(str(path).encode(), int(verify), _ptr(count), _ptr(size))
+        return status, int(count[0]), int(size[0])
+
+    def artifact_tensor(self, path: str, index: int) -> dict:
+        name = ctypes.create_string_buffer(256)
+        dims, meta, spans = np.zeros(4, np.uint64), np.zeros(3, np.uint16), np.zeros(5, np.uint64)
+        status = self.lib.ref_artifact_tensor(str(path).encode(), index, name, _ptr(dims), _ptr(meta), _ptr(spans))
+        assert status == 0, status
+        rank = int(meta[2])
+        return {"name": name.value.decode(), "dtype": int(meta[0]), "quantization": int(meta[1]),
+                "dimensions": tuple(int(d) for d in dims[:rank]), "data_offset": int(spans[0]),
+                "data_bytes": int(spans[1]), "aux_offset": int(spans[2]), "aux_bytes": int(spans[3]),
+                "data_crc64": int(spans[4])}
 
     def test_matrix(self, seed: int, stddev: float, rows: int, cols: int) -> np.ndarray:
         out = np.zeros(rows * cols, np.float32)
