@@ -557,6 +557,8 @@ struct gfxb_session {
   const __half* last_hidden = nullptr;
   std::uint32_t* pinned = nullptr;  // host staging
   cudaGraphExec_t greedy_graph = nullptr;
+  cudaGraphExec_t spec_graph = nullptr;  // the speculative round for spec_drafts drafts
+  unsigned spec_drafts = 0;
   // persistent token kernel
   __half* mlp_product = nullptr;  // fp16 SiLU(gate) * up of the token kernel's MLP
   gfxb::LoopOp* loop_ops = nullptr;
@@ -1137,6 +1139,44 @@ int enqueue_greedy_step(gfxb_session& s) {
   return launch_status("advance launch failed");
 }
 
+// The device part of a speculative round (qwen_runtime.cpp:546-640, 715-867):
+// `drafts` MTP proposals chained through device token ids, the drafts copied
+// behind the seed, the causal verifier block with rollback logs, and the
+// drafts and verifier tokens copied to pinned host memory. Reads only device
+// scalars (positions, seed) set before it runs, so it can be captured once
+// and replayed every round (prepare_speculative_graphs, :642-713).
+int enqueue_speculative_body(gfxb_session& s, unsigned drafts) {
+  for (unsigned i = 0; i < drafts; ++i) {
+    const std::uint32_t* token = i == 0 ? s.seed_token : s.draft_tokens + i - 1;
+    const __half* conditioning = i == 0 ? s.target_snapshot : s.mtp_hidden;
+    GFXB_TRY(enqueue_mtp(s, token, conditioning, s.mtp_positions + i, s.draft_tokens + i));
+  }
+  copy_drafts_kernel<<<1, kMaxBlock, 0, s.stream>>>(s.draft_tokens, s.tokens, drafts);
+  GFXB_TRY(launch_status("draft copy failed"));
+  GFXB_TRY(enqueue_forward(s, drafts + 1, s.tokens, s.position, true));
+  GFXB_TRY(cuda_check(cudaMemcpyAsync(s.pinned + 128, s.draft_tokens, drafts * 4, cudaMemcpyDeviceToHost, s.stream),
+                      "draft download failed"));
+  return cuda_check(cudaMemcpyAsync(s.pinned + 160, s.selected, (drafts + 1) * 4, cudaMemcpyDeviceToHost, s.stream),
+                    "verifier download failed");
+}
+
+int capture_speculative(gfxb_session& s, unsigned drafts) {
+  cudaGraph_t graph = nullptr;
+  GFXB_TRY(cuda_check(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal), "graph capture start failed"));
+  const int status = enqueue_speculative_body(s, drafts);
+  const cudaError_t end = cudaStreamEndCapture(s.stream, &graph);
+  if (status != GFXB_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return status;
+  }
+  GFXB_TRY(cuda_check(end, "graph capture end failed"));
+  const cudaError_t inst = cudaGraphInstantiate(&s.spec_graph, graph, 0);
+  cudaGraphDestroy(graph);
+  GFXB_TRY(cuda_check(inst, "graph instantiation failed"));
+  s.spec_drafts = drafts;
+  return GFXB_OK;
+}
+
 int capture_greedy(gfxb_session& s) {
   cudaGraph_t graph = nullptr;
   GFXB_TRY(cuda_check(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal), "graph capture start failed"));
@@ -1653,9 +1693,13 @@ extern "C" int gfxb_session_create(gfxb_engine* engine, const gfxb_session_confi
   }
   if (status == GFXB_OK && config->step_kernel == GFXB_STEP_PERSISTENT) status = build_token_loop(*s);
   if (status == GFXB_OK && config->use_graphs) status = capture_greedy(*s);
+  if (status == GFXB_OK && config->graph_verifier_batch != 0 && engine->has_mtp) {
+    status = capture_speculative(*s, config->graph_verifier_batch - 1);
+  }
   if (status == GFXB_OK) status = cuda_check(cudaStreamSynchronize(s->stream), "session setup failed");
   if (status != GFXB_OK) {
     if (s->greedy_graph) cudaGraphExecDestroy(s->greedy_graph);
+    if (s->spec_graph) cudaGraphExecDestroy(s->spec_graph);
     if (s->pinned) cudaFreeHost(s->pinned);
     cudaFree(s->arena);
     return status;
@@ -1669,6 +1713,7 @@ extern "C" int gfxb_session_destroy(gfxb_session* session) {
   cudaSetDevice(session->e->device);
   cudaStreamSynchronize(session->stream);
   if (session->greedy_graph) cudaGraphExecDestroy(session->greedy_graph);
+  if (session->spec_graph) cudaGraphExecDestroy(session->spec_graph);
   if (session->pinned) cudaFreeHost(session->pinned);
   if (session->loop_trace) cudaFree(session->loop_trace);
   cudaFree(session->arena);
@@ -1824,20 +1869,14 @@ extern "C" int gfxb_session_speculative_step(gfxb_session* session, std::uint32_
   set_positions_kernel<<<1, 1, 0, s.stream>>>(s.position, base, s.mtp_positions, mtp_base, draft_count, s.seed_token,
                                                seed_token, s.tokens);
   GFXB_TRY(launch_status("position setup failed"));
-  for (unsigned i = 0; i < draft_count; ++i) {
-    const std::uint32_t* token = i == 0 ? s.seed_token : s.draft_tokens + i - 1;
-    const __half* conditioning = i == 0 ? s.target_snapshot : s.mtp_hidden;
-    GFXB_TRY(enqueue_mtp(s, token, conditioning, s.mtp_positions + i, s.draft_tokens + i));
+  // the captured round when its draft count matches (launch_prepared_speculative_graph, :888-934)
+  if (s.spec_graph != nullptr && draft_count == s.spec_drafts) {
+    GFXB_TRY(cuda_check(cudaGraphLaunch(s.spec_graph, s.stream), "speculative graph launch failed"));
+  } else {
+    GFXB_TRY(enqueue_speculative_body(s, draft_count));
   }
-  copy_drafts_kernel<<<1, kMaxBlock, 0, s.stream>>>(s.draft_tokens, s.tokens, draft_count);
-  GFXB_TRY(launch_status("draft copy failed"));
   const unsigned batch = draft_count + 1;
-  GFXB_TRY(enqueue_forward(s, batch, s.tokens, s.position, true));
   std::uint32_t host[2 * kMaxBlock];
-  GFXB_TRY(cuda_check(cudaMemcpyAsync(s.pinned + 128, s.draft_tokens, draft_count * 4, cudaMemcpyDeviceToHost, s.stream),
-                      "draft download failed"));
-  GFXB_TRY(cuda_check(cudaMemcpyAsync(s.pinned + 160, s.selected, batch * 4, cudaMemcpyDeviceToHost, s.stream),
-                      "verifier download failed"));
   GFXB_TRY(cuda_check(cudaStreamSynchronize(s.stream), "speculative round failed"));
   std::memcpy(host, s.pinned + 128, draft_count * 4);
   std::memcpy(host + kMaxBlock, s.pinned + 160, batch * 4);

@@ -287,7 +287,13 @@ int gfxb_session_block_step(gfxb_session* session, const uint32_t* input_tokens,
 /* QwenDecodeSession::mtp_draft (qwen_runtime.cpp:1394-1419). */
 int gfxb_session_mtp_draft(gfxb_session* session, uint32_t next_token, uint32_t* draft_token);
 /* QwenDecodeSession::speculative_step (qwen_runtime.cpp:1421-1544): tokens
- * receives accepted drafts + the correction (at most draft_count + 1). */
+ * receives accepted drafts + the correction (at most draft_count + 1). When
+ * the session was created with graph_verifier_batch == draft_count + 1, the
+ * round's device work (MTP draft chain, verifier block with rollback logs,
+ * token downloads) replays one CUDA graph captured at session creation
+ * (prepare_speculative_graphs, :642-713); other draft counts run the same
+ * work eagerly. Acceptance, rollback replay and the MTP cache advance follow
+ * on the host as in the reference. */
 int gfxb_session_speculative_step(gfxb_session* session, uint32_t seed_token, unsigned draft_count,
                                   uint32_t* tokens, unsigned* token_count, unsigned* accepted_drafts);
 int gfxb_session_position(const gfxb_session* session, uint64_t* position);

@@ -109,13 +109,17 @@ def test_mtp_draft_bit_exact(oracle, small_engine):
     assert got == want
 
 
+@pytest.mark.parametrize("graph", [False, True])
 @pytest.mark.parametrize("depth", [1, 4, 8])
-def test_speculative_stream_equals_greedy(oracle, small_engine, depth):
+def test_speculative_stream_equals_greedy(oracle, small_engine, depth, graph):
     """spec-bench (src/cli/main.cpp:917-979): one greedy step, then speculative rounds; the
-    emitted stream must equal the serial greedy stream token for token."""
+    emitted stream must equal the serial greedy stream token for token, with the round's
+    device work eager or replayed from the captured speculative graph."""
+    from gfxinfer_b200 import session as gs
+
     cfg = model_config(**SMALL_MODEL)
     start = prompt_tokens(oracle, cfg.seed + 11, cfg.vocab, 1)[0]
-    spec = _session(small_engine)
+    spec = gs.QwenDecodeSession.create(small_engine, graph_verifier_batch=depth + 1 if graph else 0)
     first = spec.greedy_step(start)
     emitted, seed, proposed, accepted = [first], first, 0, 0
     while len(emitted) < 40:
@@ -133,6 +137,29 @@ def test_speculative_stream_equals_greedy(oracle, small_engine, depth):
         reference.append(token)
     assert emitted == reference
     assert spec.position() == serial.position()
+
+
+def test_speculative_graph_with_other_depths_runs_eagerly(oracle, small_engine):
+    """A session captured for 4 drafts still serves rounds of 2 drafts (eagerly), interleaved."""
+    from gfxinfer_b200 import session as gs
+
+    cfg = model_config(**SMALL_MODEL)
+    start = prompt_tokens(oracle, cfg.seed + 13, cfg.vocab, 1)[0]
+    spec = gs.QwenDecodeSession.create(small_engine, graph_verifier_batch=5)
+    first = spec.greedy_step(start)
+    emitted, seed, depth = [first], first, 4
+    while len(emitted) < 30:
+        result = spec.speculative_step(seed, depth)
+        emitted.extend(result.tokens)
+        seed = result.tokens[-1]
+        depth = 2 if depth == 4 else 4
+    serial = _session(small_engine)
+    token = serial.greedy_step(start)
+    reference = [token]
+    while len(reference) < len(emitted):
+        token = serial.greedy_step(token)
+        reference.append(token)
+    assert emitted == reference
 
 
 def test_invalid_arguments_are_rejected(small_engine):
