@@ -210,6 +210,102 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def measure_mtp(gs, np, torch, local: int, depths=(4, 8), emitted_target: int = 256) -> dict:
+    """the config-2 model plus one MTP layer, context 2048; speculative rounds
+    (MTP draft chain + causal verifier, one captured CUDA graph per depth) until 256 tokens are
+    emitted after a 64-token prompt. Emitted tokens/s over the device-timed loop (the host accept
+    step included) and the draft acceptance rate. Random-init weights: acceptance is low."""
+    cfg = dict(gs.CONFIG2, max_context=2048)
+    engine = gs.Engine.create(gs.model_config(**cfg), device=local, include_mtp=True)
+    rng = np.random.default_rng(cfg["seed"] + 3)
+    prompt = [int(t) for t in rng.integers(0, cfg["vocab"], size=64)]
+    out = {"workload": "config-3: config-2 model + 1 MTP layer (draft head = first 98304 LM-head rows), "
+                       "ctx 2048, 64-token prompt, 256 emitted tokens per depth", "depths": {}}
+    for depth in depths:
+        session = gs.QwenDecodeSession.create(engine, maximum_context_tokens=2048, graph_verifier_batch=depth + 1)
+        stream = torch.cuda.ExternalStream(session.stream(), device=torch.device("cuda", local))
+        token = None
+        for t in prompt:
+            token = session.greedy_step(t)
+            session.mtp_draft(token)  # keep the MTP cache aligned with the target (spec-bench warm-up)
+        seed = session.greedy_step(token)
+        for _ in range(2):  # warm-up rounds
+            seed = session.speculative_step(seed, depth).tokens[-1]
+        emitted = proposed = accepted = rounds = 0
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(stream)
+        while emitted < emitted_target:
+            result = session.speculative_step(seed, depth)
+            emitted += len(result.tokens)
+            proposed += result.proposed_drafts
+            accepted += result.accepted_drafts
+            rounds += 1
+            seed = result.tokens[-1]
+        stop.record(stream)
+        stop.synchronize()
+        ms = start.elapsed_time(stop)
+        out["depths"][str(depth)] = {"emitted_tokens_per_s": round(emitted / (ms / 1000.0), 3),
+                                     "emitted_tokens": emitted, "rounds": rounds,
+                                     "acceptance": round(accepted / max(proposed, 1), 4),
+                                     "ms_per_round": round(ms / rounds, 3)}
+        session.close()
+    engine.close()
+    return out
+
+
+def measure_config4(gs, np, torch, world: int, rank: int, local: int, nccl_id, steps: int, barrier) -> dict:
+    """the config-2 model with W2 MLP, W4 attention/GDN/head, A8 activations and
+    a 4096-token context, tensor-parallel over the job's GPUs. The session is filled to position
+    3968 with 32-token verifier blocks, then `steps` greedy steps run device-resident; plus the
+    per-GPU W2 MLP gate+up GEMV bandwidth."""
+    cfg = dict(gs.CONFIG2, mlp_bits=2, activation_bits=8, max_context=4096)
+    engine = gs.Engine.create(gs.model_config(**cfg), device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id,
+                              include_mtp=False)
+    session = gs.QwenDecodeSession.create(engine, maximum_context_tokens=4096)
+    stream = torch.cuda.ExternalStream(session.stream(), device=torch.device("cuda", local))
+    rng = np.random.default_rng(cfg["seed"] + 4)
+    fill = 4096 - 128
+    tokens = [int(t) for t in rng.integers(0, cfg["vocab"], size=fill)]
+    token = None
+    for i in range(0, fill, 32):
+        token = session.block_step(tokens[i:i + 32])[-1]
+    for _ in range(3):
+        token = session.greedy_step(token)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record(stream)
+    session.enqueue_greedy(token, steps)
+    stop.record(stream)
+    stop.synchronize()
+    barrier()
+    decode_ms = start.elapsed_time(stop)
+    launches = 48
+    session.enqueue_gemv(0, 8)
+    torch.cuda.synchronize()
+    start.record(stream)
+    gemv_bytes = session.enqueue_gemv(0, launches)
+    stop.record(stream)
+    stop.synchronize()
+    gemv_us = start.elapsed_time(stop) * 1000.0 / launches
+    times = torch.tensor([decode_ms, gemv_us], dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    decode_ms, gemv_us = times.tolist()
+    weight_bytes = engine.weight_bytes()
+    session.close()
+    engine.close()
+    return {"workload": "config-4: config-2 model, W2 MLP / W4 attention+GDN+head, A8, ctx 4096 "
+                        f"(decode at positions {fill + 3}..{fill + 3 + steps}), tp{world}",
+            "tokens_per_s": round(steps / (decode_ms / 1000.0), 3), "ms_per_token": round(decode_ms / steps, 4),
+            "weight_bytes_per_gpu": weight_bytes,
+            "per_gpu_GBps": round(weight_bytes / (decode_ms / steps / 1000.0) / 1e9, 1),
+            "mlp_gate_up_gemv_GBps_per_gpu": round(gemv_bytes / (gemv_us * 1e-6) / 1e9, 1),
+            "mlp_gate_up_gemv_us": round(gemv_us, 3)}
+
+
 def run_b200(args) -> None:
     import numpy as np
     import torch
@@ -336,11 +432,25 @@ def run_b200(args) -> None:
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(2)
-        print(json.dumps(line), flush=True)
     if watchdog is not None:
         watchdog.stop()
     session.close()
     engine.close()
+    extras = {}
+    if not args.no_extra:
+        config4_id = None
+        if world > 1:
+            import torch.distributed as dist
+
+            holder = [gs.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(holder, src=0)
+            config4_id = holder[0]
+        extras["config4"] = measure_config4(gs, np, torch, world, rank, local, config4_id, min(args.steps, 96), barrier)
+        if world == 1:
+            extras["mtp"] = measure_mtp(gs, np, torch, local)
+    if rank == 0:
+        line.update(extras)
+        print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
 
@@ -355,6 +465,7 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-extra", action="store_true", help="skip the config-3 (MTP) and config-4 (TP W2/A8) lines")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     if 64 + 2 * (args.warmup + args.steps) > 512:
