@@ -58,16 +58,16 @@ __global__ __launch_bounds__(256) void silu_pack_kernel(SiluPackArgs args) {
     amax = fmaxf(amax, fabsf(x[j]));
   }
   if (args.act_codes == nullptr) return;
-#pragma unroll
-  for (unsigned offset = 16; offset != 0; offset >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
+  amax = warp_amax(amax);
   const __half scale_h = act_scale_of<ActBits>(amax);
   const float scale = h2f(scale_h);
+  const float recip = __frcp_rn(scale);
   std::uint32_t word = 0;
   int code_sum = 0;
   int q[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    q[j] = act_code_of<ActBits>(x[j], scale);
+    q[j] = act_code_fast<ActBits>(x[j], scale, recip);
     word |= (static_cast<std::uint32_t>(q[j]) & 0xffu) << (8 * j);
     code_sum += q[j];
   }
@@ -79,8 +79,7 @@ __global__ __launch_bounds__(256) void silu_pack_kernel(SiluPackArgs args) {
     *reinterpret_cast<std::uint16_t*>(args.packed_a4 + group_base / 2u + 2u * lane) =
         static_cast<std::uint16_t>(packed);
   }
-#pragma unroll
-  for (unsigned offset = 16; offset != 0; offset >>= 1) code_sum += __shfl_xor_sync(0xffffffffu, code_sum, offset);
+  code_sum = warp_sum_int(code_sum);
   if (lane == 0) {
     args.act_scales[static_cast<std::size_t>(token) * groups + group] = scale_h;
     args.act_sums[static_cast<std::size_t>(token) * groups + group] = code_sum;

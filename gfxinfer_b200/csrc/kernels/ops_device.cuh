@@ -77,6 +77,36 @@ __device__ __forceinline__ int act_code_of(float x, float scale) {
   return max(-kLimit, min(kLimit, f2i_rn(__fdiv_rn(x, scale))));
 }
 
+// The same code without a division per element, for fp16 values x and fp16
+// scales (`recip` = __frcp_rn(scale), computed once per group). Exactness:
+// x and (k + 1/2) * scale lie on a common grid, so a quotient x / scale that
+// is not exactly k + 1/2 lies at least 2^-12 from it, while the fp32
+// quotient the reference rounds is within 2^-17 of the exact one; the
+// reference's rint(fp32(x / scale)) is therefore round-half-even of the exact
+// quotient. That is decided here from k = floor(x * recip) (at most one off,
+// and only next to an integer, where either k resolves the same way) and the
+// exactly rounded sign of x - (k + 1/2) * scale (one fma). Non-finite inputs
+// and zero or non-finite scales take the division.
+template <int ActBits>
+__device__ __forceinline__ int act_code_fast(float x, float scale, float recip) {
+  constexpr float kLimit = ActBits == 4 ? 7.0f : 127.0f;
+  if (!(scale > 0.0f) || !isfinite(scale) || !isfinite(x)) return act_code_of<ActBits>(x, scale);
+  const float k = floorf(__fmul_rn(x, recip));
+  const float e = fmaf(-__fadd_rn(k, 0.5f), scale, x);
+  float q = e > 0.0f ? __fadd_rn(k, 1.0f) : k;
+  if (e == 0.0f && (__float2int_rz(k) & 1) != 0) q = __fadd_rn(k, 1.0f);  // tie: the even neighbour (|k| < 2^23 here)
+  return static_cast<int>(fminf(fmaxf(q, -kLimit), kLimit));
+}
+
+// Largest |v| over the warp (NaN lanes count as 0, as fmaxf ignores NaN):
+// one redux on the bit patterns, which order like the non-negative values.
+__device__ __forceinline__ float warp_amax(float v) {
+  const float a = fabsf(v);
+  const std::uint32_t bits = a == a ? __float_as_uint(a) : 0u;
+  return __uint_as_float(__reduce_max_sync(0xffffffffu, bits));
+}
+__device__ __forceinline__ int warp_sum_int(int v) { return __reduce_add_sync(0xffffffffu, v); }
+
 // Quantize one 128-group held by four consecutive warps (element = thread
 // index within the 128) and store it into a GEMV activation pack. `max_slot`
 // and `sum_slot` hold 4 values of shared scratch per group.
@@ -84,18 +114,15 @@ template <int ActBits, class Sync>
 __device__ __forceinline__ void pack_group_128(float x, unsigned element, std::int8_t* codes, __half* scale_out,
                                                std::int32_t* sum_out, float* max_slot, int* sum_slot, Sync sync) {
   const unsigned lane = element & 31u, warp = element >> 5;
-  float amax = fabsf(x);
-#pragma unroll
-  for (unsigned offset = 16; offset != 0; offset >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
+  float amax = warp_amax(x);
   if (lane == 0) max_slot[warp] = amax;
   sync();
   amax = fmaxf(fmaxf(max_slot[0], max_slot[1]), fmaxf(max_slot[2], max_slot[3]));
   const __half scale_h = act_scale_of<ActBits>(amax);
-  const int q = act_code_of<ActBits>(x, h2f(scale_h));
+  const float scale = h2f(scale_h);
+  const int q = act_code_fast<ActBits>(x, scale, __frcp_rn(scale));
   codes[fragment_offset(element)] = static_cast<std::int8_t>(q);
-  int total = q;
-#pragma unroll
-  for (unsigned offset = 16; offset != 0; offset >>= 1) total += __shfl_xor_sync(0xffffffffu, total, offset);
+  const int total = warp_sum_int(q);
   if (lane == 0) sum_slot[warp] = total;
   sync();
   if (element == 0) {
@@ -200,22 +227,27 @@ __device__ __forceinline__ void norm_pack_body(const NormPackArgs& args, std::ui
     // groups: element (it, t) belongs to group 2*it + (t >= 128), lane-local index t % 128
 #pragma unroll
     for (unsigned it = 0; it < iterations; ++it) {
-      float amax = fabsf(values[it]);
-#pragma unroll
-      for (unsigned offset = 16; offset != 0; offset >>= 1) {
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
-      }
+      const float amax = warp_amax(values[it]);
       if (lane == 0) warp_max[it][warp] = amax;
     }
     sync();
     const unsigned half = warp >> 2;
     const std::uint32_t groups = H / kGroup;
+    // one thread per group turns the four warp maxima into the group's scale
+    // and its reciprocal, left in the group's first two slots
+    if (t < groups) {
+      float* slot = warp_max[t >> 1] + 4 * (t & 1u);
+      const float amax = fmaxf(fmaxf(slot[0], slot[1]), fmaxf(slot[2], slot[3]));
+      const float scale = h2f(act_scale_of<ActBits>(amax));
+      slot[0] = scale;
+      slot[1] = __frcp_rn(scale);
+    }
+    sync();
 #pragma unroll
     for (unsigned it = 0; it < iterations; ++it) {
-      const float amax = fmaxf(fmaxf(warp_max[it][4 * half], warp_max[it][4 * half + 1]),
-                               fmaxf(warp_max[it][4 * half + 2], warp_max[it][4 * half + 3]));
-      const __half scale_h = act_scale_of<ActBits>(amax);
-      const int q = act_code_of<ActBits>(values[it], h2f(scale_h));
+      const float scale = warp_max[it][4 * half], recip = warp_max[it][4 * half + 1];
+      const __half scale_h = f2h(scale);
+      const int q = act_code_fast<ActBits>(values[it], scale, recip);
       const std::uint32_t group = 2u * it + half;
       const std::uint32_t local = t & 127u;
       args.act_codes[row + group * kGroup + fragment_offset(local)] = static_cast<std::int8_t>(q);
@@ -226,9 +258,7 @@ __device__ __forceinline__ void norm_pack_body(const NormPackArgs& args, std::ui
               static_cast<std::uint8_t>((q & 0x0f) | ((neighbour & 0x0f) << 4));
         }
       }
-      int code_sum = q;
-#pragma unroll
-      for (unsigned offset = 16; offset != 0; offset >>= 1) code_sum += __shfl_xor_sync(0xffffffffu, code_sum, offset);
+      const int code_sum = warp_sum_int(q);
       if (lane == 0) warp_code_sums[it][warp] = code_sum;
       if (local == 0) args.act_scales[static_cast<std::size_t>(token) * groups + group] = scale_h;
     }
@@ -250,22 +280,20 @@ __device__ __forceinline__ __half silu_product(float gate, float up) { return f2
 template <int ActBits>
 __device__ __forceinline__ void pack_warp_group(const float (&x)[4], unsigned lane, std::int8_t* group_codes,
                                                 __half* scale_out, std::int32_t* sum_out) {
-  float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
-#pragma unroll
-  for (unsigned offset = 16; offset != 0; offset >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
+  const float amax = warp_amax(fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))));
   const __half scale_h = act_scale_of<ActBits>(amax);
   const float scale = h2f(scale_h);
+  const float recip = __frcp_rn(scale);
   std::uint32_t word = 0;
   int code_sum = 0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const int q = act_code_of<ActBits>(x[j], scale);
+    const int q = act_code_fast<ActBits>(x[j], scale, recip);
     word |= (static_cast<std::uint32_t>(q) & 0xffu) << (8 * j);
     code_sum += q;
   }
   *reinterpret_cast<std::uint32_t*>(group_codes + fragment_offset(4u * lane)) = word;
-#pragma unroll
-  for (unsigned offset = 16; offset != 0; offset >>= 1) code_sum += __shfl_xor_sync(0xffffffffu, code_sum, offset);
+  code_sum = warp_sum_int(code_sum);
   if (lane == 0) {
     *scale_out = scale_h;
     *sum_out = code_sum;
@@ -434,18 +462,15 @@ __device__ __forceinline__ void gdn_recurrent_tokens(const GdnRecurrentArgs& arg
       // one 128-group per value head, quantized by threads 0-127 (all threads meet the barriers)
       const std::size_t row = static_cast<std::size_t>(token) * value_elements + vh * kGdnHead;
       const std::size_t group = static_cast<std::size_t>(token) * args.value_heads + vh;
-      float amax = fabsf(y_value);
-#pragma unroll
-      for (unsigned offset = 16; offset != 0; offset >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
+      float amax = warp_amax(y_value);
       if (element_thread && lane == 0) sc.pack_max[warp] = amax;
       sync();
       amax = fmaxf(fmaxf(sc.pack_max[0], sc.pack_max[1]), fmaxf(sc.pack_max[2], sc.pack_max[3]));
       const __half scale_h = args.act_bits == 8 ? act_scale_of<8>(amax) : act_scale_of<4>(amax);
-      const int code = args.act_bits == 8 ? act_code_of<8>(y_value, h2f(scale_h)) : act_code_of<4>(y_value, h2f(scale_h));
+      const float scale = h2f(scale_h), recip = __frcp_rn(scale);
+      const int code = args.act_bits == 8 ? act_code_fast<8>(y_value, scale, recip) : act_code_fast<4>(y_value, scale, recip);
       if (element_thread) args.act_codes[row + fragment_offset(t)] = static_cast<std::int8_t>(code);
-      int total = code;
-#pragma unroll
-      for (unsigned offset = 16; offset != 0; offset >>= 1) total += __shfl_xor_sync(0xffffffffu, total, offset);
+      const int total = warp_sum_int(code);
       if (element_thread && lane == 0) sc.pack_sum[warp] = total;
       sync();
       if (t == 0) {

@@ -301,3 +301,52 @@ def test_silu_pack_bit_exact(oracle, lib):
     want_packed, want_scales, _ = oracle.quantize_a4(want.view(np.float16))
     np.testing.assert_array_equal(packed.cpu().numpy(), want_packed)
     np.testing.assert_array_equal(scales.cpu().numpy().view(np.uint16), want_scales.view(np.uint16))
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_pack_rounding_ties_bit_exact(oracle, lib, bits):
+    """The fused packers round x / scale without a division per element; near and exact
+    half-integer quotients, zero and subnormal scales must still match the reference's
+    rint(x / scale) (lowbit_gemv.hip:392-405, 428-435). The SwiGLU packer is driven with
+    gate = 32 (SiLU(32) = 32 in fp32) and up = x / 32, so it packs exactly x."""
+    rng = np.random.default_rng(11 + bits)
+    limit = 7 if bits == 4 else 127
+    groups, batch = 96, 2
+    x = np.zeros((batch, groups, 128), np.float32)
+    for b in range(batch):
+        for g in range(groups):
+            kind = g % 4
+            if kind == 3:  # tiny groups: subnormal fp16 scales (or zero)
+                s = np.float16(rng.integers(0, 4) * 2.0 ** -24)
+            else:
+                s = np.float16(rng.uniform(0.001, 0.5))
+            m = rng.integers(-2 * limit - 1, 2 * limit + 2, 128)
+            vals = (m.astype(np.float32) * np.float32(s) / 2).astype(np.float16)
+            if kind == 1:  # one fp16 ulp either side of the ties
+                vals = np.nextafter(vals, np.where(rng.random(128) < 0.5, -np.inf, np.inf).astype(np.float16))
+            vals[0] = np.float16(limit * float(s))  # pins amax, so scale = fp16(amax / limit) = s
+            x[b, g] = vals.astype(np.float32)
+    x16 = x.reshape(batch, groups * 128).astype(np.float16)
+    I = groups * 128
+    gate = np.full((batch, I), 32.0, np.float32)
+    up = (x16.astype(np.float32) / 32.0).astype(np.float32)
+    product = torch.empty((batch, I), dtype=torch.int16, device="cuda")
+    codes = torch.empty((batch, I), dtype=torch.int8, device="cuda")
+    scales = torch.empty((batch, I // 128), dtype=torch.int16, device="cuda")
+    sums = torch.empty((batch, I // 128), dtype=torch.int32, device="cuda")
+    lib.check(lib.lib().gfxb_silu_multiply_pack(_p(_dev(gate)), _p(_dev(up)), I, batch, _p(product), bits, _p(codes),
+                                                _p(scales), _p(sums), None, _stream()))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(product.cpu().numpy().view(np.uint16), x16.view(np.uint16))
+    if bits == 4:
+        _, want_scales, want_values = oracle.quantize_a4(x16)
+    else:
+        want_values, want_scales = oracle.quantize_a8(x16)
+    np.testing.assert_array_equal(scales.cpu().numpy().view(np.uint16), want_scales.view(np.uint16))
+    k = np.arange(128)
+    offset = ((k & 15) >> 2) * 32 + (k >> 5) * 8 + ((k & 31) >> 4) * 4 + (k & 3)
+    frag = codes.cpu().numpy().reshape(batch, groups, 128)
+    logical = np.empty_like(frag)
+    logical[..., k] = frag[..., offset]
+    np.testing.assert_array_equal(logical.reshape(batch, -1), want_values)
+    np.testing.assert_array_equal(sums.cpu().numpy(), want_values.reshape(batch, groups, 128).astype(np.int32).sum(-1))
