@@ -1,4 +1,4 @@
-"""Build libgfxb200.so (all CUDA kernels + the C++ host runtime) for sm_100a.
+"""Build libgfxb200.so (all CUDA kernels + the C++ host runtime) and the gfxinfer-b200 CLI for sm_100a.
 
     python -m gfxinfer_b200.build [--force] [--verbose]
 
@@ -21,6 +21,7 @@ ROOT = os.path.dirname(PACKAGE)
 CSRC = os.path.join(PACKAGE, "csrc")
 BUILD = os.path.join(PACKAGE, "_build")
 LIBRARY = os.path.join(PACKAGE, "libgfxb200.so")
+CLI = os.path.join(PACKAGE, "gfxinfer-b200")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 HOST_CXX = "/usr/bin/g++"
 NCCL_INCLUDE = "/usr/include"
@@ -78,7 +79,20 @@ def build(force: bool = False, verbose: bool = False) -> str:
         result = subprocess.run(cmd, capture_output=True, text=True)
         if result.returncode != 0:
             raise RuntimeError(f"link failed\n{result.stdout}\n{result.stderr}")
+    _build_cli(force or bool(stale), newest_header)
     return LIBRARY
+
+
+def _build_cli(force: bool, newest_header: float) -> None:
+    """The gfxinfer-b200 command line (csrc/cli/main.cpp), linked against the library."""
+    source = os.path.join(CSRC, "cli", "main.cpp")
+    if not force and os.path.exists(CLI) and os.path.getmtime(CLI) >= max(os.path.getmtime(source), newest_header):
+        return
+    cmd = [NVCC, *ARCH, *COMMON, "-o", CLI, source, f"-L{PACKAGE}", "-lgfxb200", "-lcudart",
+           "-Xlinker", "-rpath,$ORIGIN"]
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode != 0:
+        raise RuntimeError(f"CLI build failed\n{result.stdout}\n{result.stderr}")
 
 
 def main() -> None:
