@@ -352,6 +352,201 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   }
 }
 
+// ---------------------------------------------------------------------------
+// Pipelined multi-tile GEMV for batch <= 8 and tall matrices.
+//
+// A grid of a few CTAs per SM; CTA c handles tiles c, c + grid, c + 2 grid,
+// ... with two shared-memory stages: while the warps turn one tile's staged
+// groups into int32 dots and the fp32 chain runs, the next tile's codes and
+// scales are already landing (one bulk copy each, mbarrier completion). Every
+// CTA is resident from the start, so there is no second wave and no tail of
+// CTAs that only start when others exit; the weights stream continuously.
+// Arithmetic as gemv_stream_kernel (per-group int32 dots, the ordered fp32
+// chain per row), hence identical bits.
+// ---------------------------------------------------------------------------
+
+struct PipeLayout {
+  std::uint32_t weight_bytes;  // G * block
+  std::uint32_t scale_bytes;   // G * 32
+  std::uint32_t dot_bytes;     // G * 16 * B * 4
+  std::uint32_t stage_bytes;   // the three, 128-byte aligned
+  std::uint32_t act_offset;    // fp16 activation scales [B][G]
+  std::uint32_t bar_offset;
+  std::uint32_t total;
+};
+
+constexpr std::uint32_t kPipeStages = 2;
+
+__host__ __device__ inline PipeLayout pipe_layout(int bits, std::uint32_t groups, std::uint32_t batch) {
+  PipeLayout l{};
+  l.weight_bytes = groups * static_cast<std::uint32_t>(bits) * 256u;
+  l.scale_bytes = groups * 32u;
+  l.dot_bytes = groups * 16u * batch * 4u;
+  l.stage_bytes = (l.weight_bytes + l.scale_bytes + l.dot_bytes + 127u) & ~127u;
+  l.act_offset = kPipeStages * l.stage_bytes;
+  l.bar_offset = (l.act_offset + groups * batch * 2u + 15u) & ~15u;
+  l.total = l.bar_offset + kPipeStages * 8u;
+  return l;
+}
+
+template <int Bits>
+__global__ __launch_bounds__(256) void gemv_pipe_kernel(const GemvArgs args, std::uint32_t total_tiles) {
+  extern __shared__ __align__(128) std::uint8_t smem[];
+  pdl_trigger();
+  const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const unsigned gl = lane >> 2, tq = lane & 3u;
+  const std::uint32_t G = args.groups, B = args.batch;
+  constexpr std::uint32_t kBlock = Bits * 256u;
+  constexpr int kAlpha = Codec<Bits>::alpha, kBeta = Codec<Bits>::beta;
+  const PipeLayout layout = pipe_layout(Bits, G, B);
+  const std::uint32_t count = blockIdx.x < total_tiles ? (total_tiles - blockIdx.x + gridDim.x - 1u) / gridDim.x : 0u;
+  if (layout.total > dynamic_smem_bytes()) {
+    if (threadIdx.x == 0) atomicOr(&g_gemv_error, kGemvErrorSmem);
+    return;
+  }
+  std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(smem + layout.bar_offset);
+  __half* act_scales = reinterpret_cast<__half*>(smem + layout.act_offset);
+  auto stage_base = [&](std::uint32_t stage) { return smem + stage * layout.stage_bytes; };
+  // one thread stages tile i's codes and scales into stage i % 2
+  auto issue = [&](std::uint32_t i) {
+    std::uint32_t tile = blockIdx.x + i * gridDim.x;
+    const MatrixArg m = select_matrix(args, tile);
+    std::uint8_t* base = stage_base(i % kPipeStages);
+    std::uint64_t* bar = &bars[i % kPipeStages];
+    mbar_expect_tx(bar, layout.weight_bytes + layout.scale_bytes);
+    bulk_g2s(base, m.codes + static_cast<std::size_t>(tile) * G * kBlock, layout.weight_bytes, bar);
+    bulk_g2s(base + layout.weight_bytes, m.scales + static_cast<std::size_t>(tile) * G * 16u, layout.scale_bytes, bar);
+  };
+  if (threadIdx.x == 0) {
+    for (std::uint32_t s = 0; s < kPipeStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+    for (std::uint32_t i = 0; i < kPipeStages && i < count; ++i) issue(i);
+  }
+  // weights never depend on the previous kernel; the activation pack does
+  pdl_wait();
+  const std::uint32_t act_groups = args.act_stride / kGroup;
+  for (std::uint32_t i = threadIdx.x; i < G * B; i += blockDim.x) {
+    const std::uint32_t tok = i / G, g = i - tok * G;
+    act_scales[i] = args.act_scales[static_cast<std::size_t>(tok) * act_groups + g];
+  }
+  __syncthreads();
+  const std::uint32_t token = min(gl, B - 1u);
+  for (std::uint32_t i = 0; i < count; ++i) {
+    const std::uint32_t stage = i % kPipeStages;
+    std::uint32_t tile = blockIdx.x + i * gridDim.x;
+    const MatrixArg m = select_matrix(args, tile);
+    std::uint8_t* base = stage_base(stage);
+    const __half* tile_scales = reinterpret_cast<const __half*>(base + layout.weight_bytes);
+    std::int32_t* dots = reinterpret_cast<std::int32_t*>(base + layout.weight_bytes + layout.scale_bytes);
+    const bool ready = mbar_wait_bounded(&bars[stage], (i / kPipeStages) & 1u, &g_gemv_error);
+    if (ready) {
+      for (std::uint32_t g = warp; g < G; g += 8u) {
+        const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * args.act_stride +
+                                static_cast<std::size_t>(g) * kGroup + tq * 32u;
+        const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(ap));
+        const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(ap + 16));
+        const std::uint32_t t0 = 2u * tq, t1 = t0 + 1u;
+        const int s0 = t0 < B ? __ldg(args.act_sums + t0 * act_groups + g) : 0;
+        const int s1 = t1 < B ? __ldg(args.act_sums + t1 * act_groups + g) : 0;
+        LaneWords<Bits> w;
+        load_lane_shared<Bits>(base + g * kBlock, lane, w);
+        std::uint32_t a[4][4];
+        unpack(w, a);
+        int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+        mma_s8_16832(c0, a[0], b0.x, b0.y);
+        mma_s8_16832(c1, a[1], b0.z, b0.w);
+        mma_s8_16832(c0, a[2], b1.x, b1.y);
+        mma_s8_16832(c1, a[3], b1.z, b1.w);
+        const std::uint32_t row_base = g * 16u;
+        if (t0 < B) {
+          dots[(row_base + gl) * B + t0] = kAlpha * (c0[0] + c1[0]) + kBeta * s0;
+          dots[(row_base + gl + 8u) * B + t0] = kAlpha * (c0[2] + c1[2]) + kBeta * s0;
+        }
+        if (t1 < B) {
+          dots[(row_base + gl) * B + t1] = kAlpha * (c0[1] + c1[1]) + kBeta * s1;
+          dots[(row_base + gl + 8u) * B + t1] = kAlpha * (c0[3] + c1[3]) + kBeta * s1;
+        }
+      }
+    }
+    __syncthreads();
+    if (ready && threadIdx.x < 16u * B) {
+      const std::uint32_t row = threadIdx.x & 15u, tok = threadIdx.x >> 4;
+      const __half* as = act_scales + static_cast<std::size_t>(tok) * G;
+      float accumulator = 0.0f;
+      std::uint32_t g = 0;
+      for (; g + 8u <= G; g += 8u) {
+        float product[8];
+        int dot[8];
+#pragma unroll
+        for (unsigned k = 0; k < 8; ++k) {
+          product[k] = __fmul_rn(h2f(tile_scales[(g + k) * 16u + row]), h2f(as[g + k]));
+          dot[k] = dots[((g + k) * 16u + row) * B + tok];
+        }
+#pragma unroll
+        for (unsigned k = 0; k < 8; ++k) accumulator = fmaf(static_cast<float>(dot[k]), product[k], accumulator);
+      }
+      for (; g < G; ++g) {
+        const float product = __fmul_rn(h2f(tile_scales[g * 16u + row]), h2f(as[g]));
+        accumulator = fmaf(static_cast<float>(dots[(g * 16u + row) * B + tok]), product, accumulator);
+      }
+      const std::size_t index = static_cast<std::size_t>(tok) * (m.tiles * 16u) + tile * 16u + row;
+      if (m.output_f16) {
+        static_cast<__half*>(m.output)[index] = f2h(accumulator);
+      } else {
+        static_cast<float*>(m.output)[index] = accumulator;
+      }
+    }
+    __syncthreads();  // the stage's codes, scales and dots are free again
+    if (threadIdx.x == 0 && i + kPipeStages < count) issue(i + kPipeStages);
+  }
+  // no copy may still be landing when the CTA exits (only after a failed wait)
+  if (threadIdx.x == 0) {
+    for (std::uint32_t i = count > kPipeStages ? count - kPipeStages : 0u; i < count; ++i) {
+      mbar_wait_bounded(&bars[i % kPipeStages], (i / kPipeStages) & 1u, nullptr);
+    }
+  }
+}
+
+template <int Bits>
+int launch_pipe(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t stream) {
+  const PipeLayout layout = pipe_layout(Bits, args.groups, args.batch);
+  static int configured = 0;
+  static int sms = 0;
+  static std::uint32_t cached_total = 0;  // occupancy for the last layout seen
+  static int cached_blocks = 0;
+  if (configured < static_cast<int>(layout.total)) {
+    cudaError_t error = cudaFuncSetAttribute(gemv_pipe_kernel<Bits>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             200 * 1024);
+    if (error != cudaSuccess) {
+      set_error_cuda(error, "pipelined GEMV shared-memory configuration failed");
+      return GFXB_CUDA_ERROR;
+    }
+    configured = 200 * 1024;
+  }
+  int device = 0;
+  cudaGetDevice(&device);
+  if (sms == 0) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (cached_total != layout.total) {
+    int blocks = 0;
+    const cudaError_t error =
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, gemv_pipe_kernel<Bits>, 256, layout.total);
+    if (error != cudaSuccess || blocks < 1) {
+      set_error_cuda(error, "pipelined GEMV occupancy query failed");
+      return GFXB_CUDA_ERROR;
+    }
+    cached_total = layout.total;
+    cached_blocks = blocks;
+  }
+  const std::uint32_t grid = std::min<std::uint32_t>(total_tiles, static_cast<std::uint32_t>(sms * cached_blocks));
+  const cudaError_t launch = launch_kernel(gemv_pipe_kernel<Bits>, dim3(grid), dim3(256), layout.total, stream, 0u,
+                                           args, total_tiles);
+  if (launch != cudaSuccess) {
+    set_error_cuda(launch, "pipelined GEMV launch failed");
+    return GFXB_CUDA_ERROR;
+  }
+  return GFXB_OK;
+}
+
 std::uint32_t env_value(const char* name, std::uint32_t fallback) {
   const char* value = std::getenv(name);
   return value != nullptr && value[0] != '\0' ? static_cast<std::uint32_t>(std::strtoul(value, nullptr, 10)) : fallback;
@@ -1192,6 +1387,16 @@ int lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, unsigned matrix_co
   const int bits = bits_of(format);
   const unsigned grid = static_cast<unsigned>(total_tiles);
   static const bool force_v1 = env_value("GFXB_GEMV_V1", 0) != 0;
+  static const std::uint32_t pipe_mode = env_value("GFXB_GEMV_PIPE", 1);  // 0: never, 1: tall matrices, 2: always
+  if (batch <= 8 && !force_v1 && pipe_mode != 0) {
+    // tall matrices (one CTA per tile would need several waves) whose two stages leave room for two CTAs per SM
+    const PipeLayout pipe = pipe_layout(bits, args.groups, batch);
+    if ((pipe_mode == 2 || total_tiles >= tuning().min_tiles_p1) && pipe.total <= 100u * 1024u) {
+      if (bits == 2) return launch_pipe<2>(args, grid, stream);
+      if (bits == 3) return launch_pipe<3>(args, grid, stream);
+      return launch_pipe<4>(args, grid, stream);
+    }
+  }
   if (batch <= 8 && !force_v1) {
     if (bits == 2) return launch_stream<2>(args, grid, stream);
     if (bits == 3) return launch_stream<3>(args, grid, stream);
