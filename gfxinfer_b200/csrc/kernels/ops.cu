@@ -18,7 +18,12 @@ __device__ std::uint32_t g_ops_error;
 
 namespace {
 
-// residual add + RMSNorm (+ activation pack): one 256-thread CTA per token.
+// residual add + RMSNorm (+ activation pack): blockIdx.y = token; the
+// blockIdx.x-th CTA of a token writes kNormSplitIters iterations (8 groups)
+// of the outputs, each CTA computing the row's whole sum of squares, so one
+// token's normalisation and packing is spread over several SMs.
+constexpr unsigned kNormSplitIters = 4;
+
 template <int ActBits, unsigned Iterations>
 __global__ __launch_bounds__(kNormThreads) void residual_norm_pack_kernel(NormPackArgs args) {
   pdl_trigger();
@@ -26,7 +31,10 @@ __global__ __launch_bounds__(kNormThreads) void residual_norm_pack_kernel(NormPa
   __shared__ float warp_sums[8];
   __shared__ float warp_max[Iterations][8];
   __shared__ int warp_code_sums[Iterations][8];
-  norm_pack_body<ActBits, Iterations>(args, blockIdx.x, threadIdx.x, BlockSync{}, warp_sums, warp_max, warp_code_sums);
+  const unsigned begin = blockIdx.x * kNormSplitIters;
+  const unsigned end = begin + kNormSplitIters < Iterations ? begin + kNormSplitIters : Iterations;
+  norm_pack_body<ActBits, Iterations>(args, blockIdx.y, threadIdx.x, BlockSync{}, warp_sums, warp_max, warp_code_sums,
+                                      begin, end);
 }
 
 // ---------------------------------------------------------------------------
@@ -371,9 +379,10 @@ int launch_norm_pack(const NormPackArgs& args, int act_bits, unsigned batch, cud
     constexpr unsigned kIter = decltype(iter_tag)::value;
     if (iterations != kIter) return;
     launched = true;
-    if (act_bits == 0) launch_kernel(residual_norm_pack_kernel<0, kIter>, dim3(batch), dim3(kNormThreads), 0, stream, 0, args);
-    else if (act_bits == 4) launch_kernel(residual_norm_pack_kernel<4, kIter>, dim3(batch), dim3(kNormThreads), 0, stream, 0, args);
-    else launch_kernel(residual_norm_pack_kernel<8, kIter>, dim3(batch), dim3(kNormThreads), 0, stream, 0, args);
+    const dim3 grid((kIter + kNormSplitIters - 1) / kNormSplitIters, batch);
+    if (act_bits == 0) launch_kernel(residual_norm_pack_kernel<0, kIter>, grid, dim3(kNormThreads), 0, stream, 0, args);
+    else if (act_bits == 4) launch_kernel(residual_norm_pack_kernel<4, kIter>, grid, dim3(kNormThreads), 0, stream, 0, args);
+    else launch_kernel(residual_norm_pack_kernel<8, kIter>, grid, dim3(kNormThreads), 0, stream, 0, args);
   };
   try_launch(std::integral_constant<unsigned, 1>{});
   try_launch(std::integral_constant<unsigned, 2>{});

@@ -142,12 +142,17 @@ __device__ __forceinline__ void pack_group_128(float x, unsigned element, std::i
 constexpr unsigned kNormThreads = 256;
 constexpr unsigned kNormMaxIter = 64;  // H <= 16384
 
+// [it_begin, it_end) limits the outputs (residual, normalized values, pack)
+// to elements it * 256 + t of those iterations, i.e. 128-groups 2 it_begin ..
+// 2 it_end - 1; every thread still reads the whole row for the sum of squares.
 template <int ActBits, unsigned Iterations, class Sync>
 __device__ __forceinline__ void norm_pack_body(const NormPackArgs& args, std::uint32_t token, unsigned t, Sync sync,
-                                               float* warp_sums, float (*warp_max)[8], int (*warp_code_sums)[8]) {
+                                               float* warp_sums, float (*warp_max)[8], int (*warp_code_sums)[8],
+                                               unsigned it_begin = 0, unsigned it_end = Iterations) {
   const std::uint32_t H = args.elements;
   const unsigned lane = t & 31u, warp = t >> 5;
   constexpr unsigned iterations = Iterations;
+  auto mine = [&](unsigned it) { return it >= it_begin && it < it_end; };
   const std::size_t row = static_cast<std::size_t>(token) * H;
 
   float values[Iterations];
@@ -189,7 +194,9 @@ __device__ __forceinline__ void norm_pack_body(const NormPackArgs& args, std::ui
     }
     if (args.residual_out != nullptr) {
 #pragma unroll
-      for (unsigned it = 0; it < iterations; ++it) args.residual_out[row + it * kNormThreads + t] = f2h(values[it]);
+      for (unsigned it = 0; it < iterations; ++it) {
+        if (mine(it)) args.residual_out[row + it * kNormThreads + t] = f2h(values[it]);
+      }
     }
   } else if (args.update != nullptr) {
     float updates[Iterations];
@@ -203,7 +210,7 @@ __device__ __forceinline__ void norm_pack_body(const NormPackArgs& args, std::ui
     for (unsigned it = 0; it < iterations; ++it) {
       const __half rounded = f2h(__fadd_rn(values[it], updates[it]));
       values[it] = h2f(rounded);
-      if (args.residual_out != nullptr) args.residual_out[row + it * kNormThreads + t] = rounded;
+      if (args.residual_out != nullptr && mine(it)) args.residual_out[row + it * kNormThreads + t] = rounded;
     }
   } else {
 #pragma unroll
@@ -220,13 +227,14 @@ __device__ __forceinline__ void norm_pack_body(const NormPackArgs& args, std::ui
   for (unsigned it = 0; it < iterations; ++it) {
     const std::uint32_t column = it * kNormThreads + t;
     const __half y = f2h(__fmul_rn(__fmul_rn(values[it], inverse), weights[it]));
-    if (args.normalized_out != nullptr) args.normalized_out[row + column] = y;
+    if (args.normalized_out != nullptr && mine(it)) args.normalized_out[row + column] = y;
     values[it] = h2f(y);
   }
   if constexpr (ActBits != 0) {
     // groups: element (it, t) belongs to group 2*it + (t >= 128), lane-local index t % 128
 #pragma unroll
     for (unsigned it = 0; it < iterations; ++it) {
+      if (!mine(it)) continue;
       const float amax = warp_amax(values[it]);
       if (lane == 0) warp_max[it][warp] = amax;
     }
@@ -235,7 +243,7 @@ __device__ __forceinline__ void norm_pack_body(const NormPackArgs& args, std::ui
     const std::uint32_t groups = H / kGroup;
     // one thread per group turns the four warp maxima into the group's scale
     // and its reciprocal, left in the group's first two slots
-    if (t < groups) {
+    if (t < groups && mine(t >> 1)) {
       float* slot = warp_max[t >> 1] + 4 * (t & 1u);
       const float amax = fmaxf(fmaxf(slot[0], slot[1]), fmaxf(slot[2], slot[3]));
       const float scale = h2f(act_scale_of<ActBits>(amax));
@@ -245,6 +253,7 @@ __device__ __forceinline__ void norm_pack_body(const NormPackArgs& args, std::ui
     sync();
 #pragma unroll
     for (unsigned it = 0; it < iterations; ++it) {
+      if (!mine(it)) continue;
       const float scale = warp_max[it][4 * half], recip = warp_max[it][4 * half + 1];
       const __half scale_h = f2h(scale);
       const int q = act_code_fast<ActBits>(values[it], scale, recip);
@@ -263,7 +272,7 @@ __device__ __forceinline__ void norm_pack_body(const NormPackArgs& args, std::ui
       if (local == 0) args.act_scales[static_cast<std::size_t>(token) * groups + group] = scale_h;
     }
     sync();
-    for (std::uint32_t group = t; group < groups; group += kNormThreads) {
+    for (std::uint32_t group = 2 * it_begin + t; group < 2 * it_end && group < groups; group += kNormThreads) {
       const unsigned it = group >> 1, h = group & 1u;
       args.act_sums[static_cast<std::size_t>(token) * groups + group] =
           warp_code_sums[it][4 * h] + warp_code_sums[it][4 * h + 1] + warp_code_sums[it][4 * h + 2] +
