@@ -313,10 +313,35 @@ __device__ __forceinline__ void st_cluster_s32(std::uint32_t address, int value)
   asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(address), "r"(value) : "memory");
 }
 
+// Asynchronous 4-byte store into a cluster peer's shared memory whose arrival
+// is counted (4 transaction bytes) on the peer's mbarrier `remote_bar`.
+__device__ __forceinline__ void st_async_s32(std::uint32_t address, int value, std::uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.s32 [%0], %1, [%2];" ::"r"(address),
+               "r"(value), "r"(remote_bar)
+               : "memory");
+}
+
+// Wait for a phase completed by peers' st.async (cluster-scope acquire).
+__device__ __forceinline__ bool mbar_try_wait_cluster(std::uint64_t* bar, std::uint32_t parity) {
+  std::uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return done != 0;
+}
+
 // Split cluster barrier. A CTA must not touch another CTA's shared memory
 // before a cluster barrier has shown that every CTA of the cluster is running.
 __device__ __forceinline__ void cluster_arrive() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+// Arrive without ordering memory: enough when the only thing the peers must
+// see is an mbarrier initialised before a fence.mbarrier_init.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");

@@ -182,9 +182,12 @@ __global__ __launch_bounds__(256) void gemv_b200_kernel(const GemvArgs args) {
 // its 128-column groups. One thread stages the CTA's whole weight range into
 // shared memory with bulk copies (one mbarrier per 8 groups), so every byte
 // the CTA needs is in flight from the first cycle. Warps turn staged groups
-// into exact int32 dots on the tensor cores and store them into the cluster
-// leader's shared memory (DSMEM). After a cluster barrier the leader runs the
-// reference's ordered fp32 chain over all groups of the tile.
+// into exact int32 dots on the tensor cores; the other CTAs send theirs to
+// the cluster leader with asynchronous shared-memory stores whose bytes are
+// counted on one leader mbarrier, and exit. The leader then runs the
+// reference's ordered fp32 chain over all groups of the tile. No cluster
+// barrier is needed after the dots: the leader alone waits, and only for the
+// bytes it expects.
 // ---------------------------------------------------------------------------
 
 __device__ std::uint32_t g_gemv_error;
@@ -198,7 +201,7 @@ struct StreamLayout {
   std::uint32_t scale_bytes;   // G * 32
   std::uint32_t dot_bytes;     // G * 16 * B * 4
   std::uint32_t act_scale_bytes;  // G * B * 2, rounded up to 16
-  std::uint32_t bar_offset;
+  std::uint32_t bar_offset;    // chunk barriers, the scale barrier, the dots barrier
   std::uint32_t total;
 };
 
@@ -211,7 +214,7 @@ __host__ __device__ inline StreamLayout stream_layout(int bits, std::uint32_t gr
   s.dot_bytes = groups * 16u * batch * 4u;
   s.act_scale_bytes = (groups * batch * 2u + 15u) & ~15u;
   s.bar_offset = (s.weight_bytes + s.scale_bytes + s.dot_bytes + s.act_scale_bytes + 15u) & ~15u;
-  const std::uint32_t bars = (s.per_part + chunk - 1u) / chunk + 1u;
+  const std::uint32_t bars = (s.per_part + chunk - 1u) / chunk + 2u;
   s.total = s.bar_offset + bars * 8u;
   return s;
 }
@@ -226,7 +229,7 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   const MatrixArg m = select_matrix(args, tile);
   const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const unsigned gl = lane >> 2, tq = lane & 3u;
-  const std::uint32_t G = args.groups, B = args.batch, K = args.columns;
+  const std::uint32_t G = args.groups, B = args.batch;
   constexpr std::uint32_t kBlock = Bits * 256u;
   constexpr int kAlpha = Codec<Bits>::alpha, kBeta = Codec<Bits>::beta;
   const StreamLayout layout = stream_layout(Bits, G, parts, B, chunk);
@@ -240,7 +243,8 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   __half* act_scale_stage =
       reinterpret_cast<__half*>(smem + layout.weight_bytes + layout.scale_bytes + layout.dot_bytes);
   std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(smem + layout.bar_offset);
-  const std::uint32_t scale_bar = (layout.per_part + chunk - 1u) / chunk;
+  const std::uint32_t max_chunks = (layout.per_part + chunk - 1u) / chunk;
+  const std::uint32_t scale_bar = max_chunks, dots_bar = max_chunks + 1u;
 
   // Self-check of the launch geometry: every CTA of the grid sees the same
   // values, so all of them return together, before any barrier or copy.
@@ -256,11 +260,8 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   }
 
   if (threadIdx.x == 0) {
-    for (std::uint32_t c = 0; c <= scale_bar; ++c) mbar_init(&bars[c], 1);
+    for (std::uint32_t c = 0; c <= dots_bar; ++c) mbar_init(&bars[c], 1);
     fence_mbar_init();
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
     const std::uint8_t* source = m.codes + (static_cast<std::size_t>(tile) * G + g_begin) * kBlock;
     for (std::uint32_t c = 0; c < chunks; ++c) {
       const std::uint32_t bytes = min(chunk, n - chunk * c) * kBlock;
@@ -271,12 +272,15 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
       mbar_expect_tx(&bars[scale_bar], layout.scale_bytes);
       bulk_g2s(tile_scales, m.scales + static_cast<std::size_t>(tile) * G * 16u, layout.scale_bytes,
                &bars[scale_bar]);
+      // the other ranks' dots: (G - own groups) x 16 rows x B tokens x 4 bytes
+      if (parts > 1u) mbar_expect_tx(&bars[dots_bar], (G - n) * 16u * B * 4u);
     }
   }
 
-  // Every CTA of the cluster announces it is running; the wait below (before
-  // the first store into the leader's shared memory) completes this phase.
-  cluster_arrive();
+  // Every CTA of the cluster announces it is running with its barriers
+  // initialised; the wait below (before the first store into the leader's
+  // shared memory) completes this phase.
+  cluster_arrive_relaxed();
   // Weights and their scales never depend on the previous kernel; the
   // activation pack does.
   pdl_wait();
@@ -288,8 +292,18 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
     }
   }
   const std::uint32_t leader_dots = map_shared_rank(smem_addr(dots), 0);
+  const std::uint32_t leader_bar = map_shared_rank(smem_addr(&bars[dots_bar]), 0);
   const std::uint32_t token = min(gl, B - 1u);
   cluster_wait();
+  // stores dot (row, tok) of group g: locally in the leader, asynchronously elsewhere
+  auto put = [&](std::uint32_t g, std::uint32_t row, std::uint32_t tok, int value) {
+    const std::uint32_t index = (g * 16u + row) * B + tok;
+    if (part == 0) {
+      dots[index] = value;
+    } else {
+      st_async_s32(leader_dots + index * 4u, value, leader_bar);
+    }
+  };
   for (std::uint32_t local = warp; local < n; local += 8u) {
     const std::uint32_t g = g_begin + local;
     const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * args.act_stride +
@@ -305,26 +319,37 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
     load_lane_shared<Bits>(stage + local * kBlock, lane, w);
     std::uint32_t a[4][4];
     unpack(w, a);
-    int c[4] = {0, 0, 0, 0};
-    mma_s8_16832(c, a[0], b0.x, b0.y);
-    mma_s8_16832(c, a[1], b0.z, b0.w);
-    mma_s8_16832(c, a[2], b1.x, b1.y);
-    mma_s8_16832(c, a[3], b1.z, b1.w);
-    const std::uint32_t row_base = g * 16u;
+    int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+    mma_s8_16832(c0, a[0], b0.x, b0.y);
+    mma_s8_16832(c1, a[1], b0.z, b0.w);
+    mma_s8_16832(c0, a[2], b1.x, b1.y);
+    mma_s8_16832(c1, a[3], b1.z, b1.w);
     if (t0 < B) {
-      st_cluster_s32(leader_dots + ((row_base + gl) * B + t0) * 4u, kAlpha * c[0] + kBeta * s0);
-      st_cluster_s32(leader_dots + ((row_base + gl + 8u) * B + t0) * 4u, kAlpha * c[2] + kBeta * s0);
+      put(g, gl, t0, kAlpha * (c0[0] + c1[0]) + kBeta * s0);
+      put(g, gl + 8u, t0, kAlpha * (c0[2] + c1[2]) + kBeta * s0);
     }
     if (t1 < B) {
-      st_cluster_s32(leader_dots + ((row_base + gl) * B + t1) * 4u, kAlpha * c[1] + kBeta * s1);
-      st_cluster_s32(leader_dots + ((row_base + gl + 8u) * B + t1) * 4u, kAlpha * c[3] + kBeta * s1);
+      put(g, gl, t1, kAlpha * (c0[1] + c1[1]) + kBeta * s1);
+      put(g, gl + 8u, t1, kAlpha * (c0[3] + c1[3]) + kBeta * s1);
     }
   }
-  cluster_sync_all();
   if (part != 0) return;
+  __syncthreads();  // the leader's own dots and staged activation scales
   const std::uint32_t pairs = 16u * B;
   if (threadIdx.x >= pairs) return;
   if (!mbar_wait_bounded(&bars[scale_bar], 0, &g_gemv_error)) return;
+  if (parts > 1u) {
+    // Outlast every peer's own bounded waits (at most max_chunks of them), so
+    // that no peer can still be storing when this CTA exits.
+    bool arrived = false;
+    for (std::uint32_t r = 0; r < max_chunks + 2u && !arrived; ++r) {
+      for (std::uint32_t i = 0; i < kWaitLimit && !arrived; ++i) arrived = mbar_try_wait_cluster(&bars[dots_bar], 0);
+    }
+    if (!arrived) {
+      atomicOr(&g_gemv_error, kDeviceErrorTimeout);
+      return;
+    }
+  }
   const std::uint32_t row = threadIdx.x & 15u, tok = threadIdx.x >> 4;
   const __half* act_scales = act_scale_stage + static_cast<std::size_t>(tok) * G;
   float accumulator = 0.0f;

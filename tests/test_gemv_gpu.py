@@ -241,3 +241,44 @@ def test_f16_activation_rejects_bad_arguments(ops):
         ops.gfx12_f16_gemm(W4, w, s, x, 16, 256, 33)  # batch beyond 32
     with pytest.raises(GfxbError):
         ops.gfx12_f16_gemm(W4, w[1:], s, x, 16, 256, 1)  # misaligned weights
+
+
+# ---- wide matrices: K split over a cluster ----------------------------------
+# Long-K shapes with few 16-row tiles (the MLP down projection [5120 x 17408],
+# the attention/GDN output projections [5120 x 6144]) split each tile's groups
+# over a cluster of CTAs; the non-leader CTAs send their int32 dots to the
+# leader with asynchronous shared-memory stores, and the leader runs the same
+# ordered fp32 chain, so the outputs stay bit-identical to the oracle. The
+# cases cover ragged splits (G = 131, G = 17) and a single-tile matrix.
+@pytest.mark.parametrize("fmt,rows,cols,batch,bits", [
+    (W3, 5120, 17408, 1, 4),
+    (W3, 5120, 17408, 8, 4),
+    (W4, 5120, 6144, 1, 4),
+    (W4, 5120, 6144, 5, 8),
+    (W2, 1024, 16768, 3, 8),
+    (W4, 16, 2176, 2, 4),
+])
+def test_wide_k_bit_exact(oracle, ops, fmt, rows, cols, batch, bits):
+    codes, scales16, logical = _quantized(oracle, rows, cols, fmt, seed=rows + cols + batch)
+    b200, tiled = _device_b200(ops, codes, scales16, rows, cols, fmt)
+    x16 = _activations(batch, cols, seed=cols + batch)
+    got = _run_gemv(ops, fmt, b200, tiled, rows, cols, x16, bits)
+    if bits == 4:
+        _, a_scales, a = oracle.quantize_a4(x16)
+    else:
+        a, a_scales = oracle.quantize_a8(x16)
+    np.testing.assert_array_equal(got.view(np.uint32), oracle.gemv(logical, scales16, a, a_scales).view(np.uint32))
+
+
+@pytest.mark.parametrize("parts", ["1", "2", "4", "8"])
+def test_cluster_splits_bit_exact(parts):
+    """Every cluster size of the streaming GEMV, in a fresh process (the size is
+    read once per process): G = 17 over 8 CTAs leaves two CTAs without groups."""
+    import os
+    import subprocess
+    import sys
+
+    env = dict(os.environ, GFXB_GEMV_PARTS=parts)
+    child = os.path.join(os.path.dirname(os.path.abspath(__file__)), "gemv_split_child.py")
+    result = subprocess.run([sys.executable, child], env=env, capture_output=True, text=True, timeout=600)
+    assert result.returncode == 0, result.stdout + result.stderr
