@@ -237,7 +237,16 @@ __global__ __launch_bounds__(256) void qk_norm_rope_kernel(QkRopeArgs args) {
 
 constexpr unsigned kChunk = kAttentionChunk;
 
+// One CTA per (chunk of 128 positions, KV head, token); warp w < group is
+// query head kvh * group + w. The chunk's key and value rows (512 B each)
+// are staged into shared memory once for the whole GQA group by bulk copies
+// that every thread helps issue, so the CTA waits for one memory round trip
+// instead of one per eight rows and warp; the values land while the scores
+// and the softmax run.
+constexpr std::uint32_t kAttentionStageBytes = 2u * kChunk * 256u * 2u;
+
 __global__ __launch_bounds__(256) void attention_chunk_kernel(AttentionArgs args) {
+  extern __shared__ __align__(128) std::uint8_t stage[];
   pdl_trigger();
   pdl_wait();
   const unsigned group = args.q_heads / args.kv_heads;
@@ -250,23 +259,49 @@ __global__ __launch_bounds__(256) void attention_chunk_kernel(AttentionArgs args
   __shared__ float scores[8][kChunk];
   __shared__ float alphas[8][kChunk];
   __shared__ float betas[8][kChunk];
-  if (warp >= group) return;
-  const unsigned h = kvh * group + warp;
-  float* partial =
-      args.partials + ((static_cast<std::size_t>(token) * args.q_heads + h) * args.max_chunks + chunk) * 258u;
+  __shared__ __align__(8) std::uint64_t bars[2];  // keys, values
   if (chunk >= chunks) return;
+  if (count > args.capacity) {
+    if (threadIdx.x == 0) atomicOr(&g_ops_error, 8u);
+    return;
+  }
   const std::uint64_t begin = static_cast<std::uint64_t>(chunk) * kChunk;
   const std::uint64_t remaining = count - begin;
   const std::uint32_t n = remaining < kChunk ? static_cast<std::uint32_t>(remaining) : kChunk;
-  if (count > args.capacity) {
-    if (lane == 0) atomicOr(&g_ops_error, 8u);
-    return;
+  __half* keys = reinterpret_cast<__half*>(stage);
+  __half* values = keys + kChunk * 256u;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_expect_tx(&bars[0], n * 512u);
+    mbar_expect_tx(&bars[1], n * 512u);
   }
   const std::size_t row_stride = static_cast<std::size_t>(args.kv_heads) * 256u;
-  attention_chunk_warp(args.query + (static_cast<std::size_t>(token) * args.q_heads + h) * 256u,
-                       args.key_cache + (begin * args.kv_heads + kvh) * 256u,
-                       args.value_cache + (begin * args.kv_heads + kvh) * 256u, row_stride, n, lane, scores[warp],
-                       alphas[warp], betas[warp], partial);
+  for (std::uint32_t i = threadIdx.x; i < 2u * n; i += blockDim.x) {
+    const bool is_value = i >= n;
+    const std::uint32_t row = is_value ? i - n : i;
+    const __half* source = (is_value ? args.value_cache : args.key_cache) + (begin + row) * row_stride + kvh * 256u;
+    bulk_g2s((is_value ? values : keys) + row * 256u, source, 512u, &bars[is_value ? 1 : 0]);
+  }
+  if (warp < group) {
+    const unsigned h = kvh * group + warp;
+    float* partial =
+        args.partials + ((static_cast<std::size_t>(token) * args.q_heads + h) * args.max_chunks + chunk) * 258u;
+    if (mbar_wait_bounded(&bars[0], 0, &g_ops_error)) {
+      attention_chunk_warp<true>(args.query + (static_cast<std::size_t>(token) * args.q_heads + h) * 256u, keys,
+                                 values, 256u, n, lane, scores[warp], alphas[warp], betas[warp], partial, &bars[1]);
+      if (lane == 0 && !mbar_try_wait(&bars[1], 0)) atomicOr(&g_ops_error, kDeviceErrorTimeout);
+    }
+  }
+  // no copy may still be landing when the CTA exits (only after a failed wait)
+  if (threadIdx.x == 0) {
+    mbar_wait_bounded(&bars[0], 0, nullptr);
+    mbar_wait_bounded(&bars[1], 0, nullptr);
+  }
 }
 
 __global__ __launch_bounds__(256) void attention_merge_kernel(AttentionArgs args) {
@@ -488,7 +523,18 @@ int launch_attention(const AttentionArgs& args, unsigned batch, cudaStream_t str
   const std::uint32_t max_chunks = args.device_base_position != nullptr
                                        ? args.max_chunks
                                        : static_cast<std::uint32_t>((args.base_token_count + batch - 1 + kChunk - 1) / kChunk);
-  launch_kernel(attention_chunk_kernel, dim3(dim3(max_chunks, args.kv_heads, batch)), dim3(256), 0, stream, 0, args);
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t error = cudaFuncSetAttribute(attention_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(kAttentionStageBytes));
+    if (error != cudaSuccess) {
+      set_error_cuda(error, "attention shared-memory configuration failed");
+      return GFXB_CUDA_ERROR;
+    }
+    configured = true;
+  }
+  launch_kernel(attention_chunk_kernel, dim3(dim3(max_chunks, args.kv_heads, batch)), dim3(256),
+                kAttentionStageBytes, stream, 0, args);
   int status = launch_status("attention chunk launch failed");
   if (status != GFXB_OK) return status;
   launch_kernel(attention_merge_kernel, dim3(dim3(args.q_heads, batch)), dim3(256), 0, stream, 0, args);

@@ -534,10 +534,23 @@ __device__ __forceinline__ __half qk_norm_rope_value(float value, const std::uin
 // serial update.
 // ---------------------------------------------------------------------------
 
+// K/V rows come from global memory (L2 loads: the cache was appended inside
+// the running grid or just before) or, with Staged, from shared memory where
+// the caller has placed them; the arithmetic is the same either way.
+template <bool Staged = false>
+__device__ __forceinline__ uint4 kv_row_load(const __half* p) {
+  if constexpr (Staged) {
+    return *reinterpret_cast<const uint4*>(p);
+  } else {
+    return ld_cg16(p);
+  }
+}
+
+template <bool Staged = false>
 __device__ __forceinline__ void attention_chunk_warp(const __half* q_row, const __half* key_base,
                                                      const __half* value_base, std::size_t row_stride, std::uint32_t n,
                                                      unsigned lane, float* scores, float* alphas, float* betas,
-                                                     float* partial) {
+                                                     float* partial, std::uint64_t* value_ready = nullptr) {
   float qf[8];
   {
     const uint4 raw = *reinterpret_cast<const uint4*>(q_row + 8u * lane);
@@ -552,7 +565,7 @@ __device__ __forceinline__ void attention_chunk_warp(const __half* q_row, const 
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const std::uint32_t p = p0 + i < n ? p0 + i : 0u;
-      raw[i] = ld_cg16(keys + p * row_stride);
+      raw[i] = kv_row_load<Staged>(keys + p * row_stride);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -594,6 +607,7 @@ __device__ __forceinline__ void attention_chunk_warp(const __half* q_row, const 
   }
   const float chunk_max = __shfl_sync(0xffffffffu, previous, 31);
   __syncwarp();
+  if (value_ready != nullptr && !mbar_wait_bounded(value_ready, 0, nullptr)) n = 0;  // staged values landed
   float den = 0.0f;
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   const __half* values = value_base + 8u * lane;
@@ -602,7 +616,7 @@ __device__ __forceinline__ void attention_chunk_warp(const __half* q_row, const 
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const std::uint32_t p = p0 + i < n ? p0 + i : 0u;
-      raw[i] = ld_cg16(values + p * row_stride);
+      raw[i] = kv_row_load<Staged>(values + p * row_stride);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {

@@ -1,8 +1,9 @@
 """Child process of test_cluster_splits_bit_exact (tests/test_gemv_gpu.py).
 
 Runs the GEMV over shapes whose group counts do not divide evenly by the
-cluster size the parent chose through the environment, and compares every
-output bit with the oracle. Exit status 0 when all match.
+cluster size (or by the pipelined kernel's K-chunks) that the parent chose
+through the environment, and compares every output bit with the oracle.
+Exit status 0 when all match.
 """
 import os
 import sys
@@ -21,7 +22,8 @@ def main() -> int:
 
     ops.require_sm100(0)
     oracle = Oracle()
-    cases = [(W3, 48, 17 * 128, 1), (W4, 32, 3 * 128, 8), (W2, 160, 40 * 128, 5), (W3, 16, 128, 2)]
+    cases = [(W3, 48, 17 * 128, 1), (W4, 32, 3 * 128, 8), (W2, 160, 40 * 128, 5), (W3, 16, 128, 2),
+             (W4, 48, 40 * 128, 2), (W3, 32, 136 * 128, 3), (W2, 16, 131 * 128, 8)]
     for fmt, rows, cols, batch in cases:
         rng = np.random.default_rng(rows * 7 + cols + batch)
         w = rng.normal(0.0, 0.02, size=(rows, cols)).astype(np.float32)
