@@ -720,9 +720,14 @@ int gdn_mixer(gfxb_session& s, const Layer& L, unsigned batch, bool record) {
   cv.appended_log = record ? s.conv_log + static_cast<std::size_t>(L.state_index) * kMaxBlock * sh.channels : nullptr;
   cv.channels = sh.channels;
   cv.batch = batch;
-  GFXB_TRY(launch_gdn_conv(cv, s.stream));
   GdnRecurrentArgs g;
-  g.qkv = s.conv_out;
+  // the conv runs inside the recurrent kernel when a key head's value heads fit one cluster
+  if (sh.nv / sh.nk <= 8) {
+    g.conv = cv;
+  } else {
+    GFXB_TRY(launch_gdn_conv(cv, s.stream));
+    g.qkv = s.conv_out;
+  }
   g.z = s.proj_z;
   g.a = s.proj_a + sh.vh0;
   g.b = s.proj_b + sh.vh0;

@@ -129,6 +129,7 @@ __global__ void gdn_conv_kernel(GdnConvArgs args) {
 // and SiLU(z) gate.
 // ---------------------------------------------------------------------------
 
+template <bool FusedConv>
 __global__ __launch_bounds__(kGdnThreads) void gdn_recurrent_kernel(GdnRecurrentArgs args) {
   pdl_trigger();
   pdl_wait();
@@ -136,7 +137,7 @@ __global__ __launch_bounds__(kGdnThreads) void gdn_recurrent_kernel(GdnRecurrent
   const unsigned vh = blockIdx.x, t = threadIdx.x;
   float S[kGdnRows];
   gdn_load_state(args, vh, t, S);
-  gdn_recurrent_tokens(args, vh, t, S, BlockSync{}, scratch);
+  gdn_recurrent_tokens<BlockSync, FusedConv>(args, vh, t, S, BlockSync{}, scratch);
   gdn_store_state(args, vh, t, S);
 }
 
@@ -458,13 +459,25 @@ int launch_gdn_conv(const GdnConvArgs& args, cudaStream_t stream) {
 }
 
 int launch_gdn_recurrent(const GdnRecurrentArgs& args, cudaStream_t stream) {
-  if (args.qkv == nullptr || args.z == nullptr || args.a == nullptr || args.b == nullptr || args.a_log == nullptr ||
+  if (args.z == nullptr || args.a == nullptr || args.b == nullptr || args.a_log == nullptr ||
       args.dt_bias == nullptr || args.norm_weight == nullptr || args.initial_state == nullptr ||
       args.final_state == nullptr || args.output == nullptr || args.batch == 0 || args.key_heads == 0 ||
       args.value_heads == 0 || args.value_heads % args.key_heads != 0) {
     return fail(GFXB_INVALID_ARGUMENT, "invalid GDN recurrent arguments");
   }
-  launch_kernel(gdn_recurrent_kernel, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, 0, args);
+  if (args.conv.projected != nullptr) {
+    // one cluster per key head: its value heads share the q/k conv channels
+    const unsigned ratio = args.value_heads / args.key_heads;
+    if (ratio > 8 || args.conv.weight == nullptr || args.conv.initial_state == nullptr ||
+        args.conv.final_state == nullptr) {
+      return fail(GFXB_INVALID_ARGUMENT, "fused GDN conv needs its weights and states and at most 8 value heads "
+                                         "per key head");
+    }
+    launch_kernel(gdn_recurrent_kernel<true>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, ratio, args);
+  } else {
+    if (args.qkv == nullptr) return fail(GFXB_INVALID_ARGUMENT, "invalid GDN recurrent arguments");
+    launch_kernel(gdn_recurrent_kernel<false>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, 0, args);
+  }
   return launch_status("GDN recurrent launch failed");
 }
 

@@ -80,6 +80,11 @@ struct GdnRecurrentArgs {
   std::int8_t* act_codes = nullptr;
   __half* act_scales = nullptr;
   std::int32_t* act_sums = nullptr;
+  // optional causal conv fused in front (conv.projected != nullptr): the CTAs
+  // of one key head's value heads run as a cluster, each convolves the q/k/v
+  // channels it reads, and `qkv` is unused; conv.output and conv.channels are
+  // ignored (the channel count follows from the head counts)
+  GdnConvArgs conv;
 };
 
 struct GdnRestoreArgs {

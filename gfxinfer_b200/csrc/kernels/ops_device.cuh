@@ -341,6 +341,7 @@ struct GdnScratch {
   float query[kGdnHead];
   float key[kGdnHead];
   float mixed[kGdnHead];
+  float value[kGdnHead];  // fused conv: this token's value vector
   float sums[3][4];
   float gates[2];  // decay, beta
   float pack_max[4];
@@ -363,7 +364,34 @@ __device__ __forceinline__ void gdn_store_state(const GdnRecurrentArgs& args, un
   for (unsigned k = 0; k < kGdnRows; ++k) final_state[(row0 + k) * kGdnHead + column] = S[k];
 }
 
-template <class Sync>
+// Causal-conv taps and weights of one channel, for the fused conv.
+struct ConvChannel {
+  __half taps[4];
+  float w[4];
+  __device__ __forceinline__ void load(const GdnConvArgs& conv, std::size_t channel) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) taps[i] = conv.initial_state[channel * 4u + i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = bf2f(conv.weight[channel * 4u + i]);
+  }
+  __device__ __forceinline__ void store(const GdnConvArgs& conv, std::size_t channel) const {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) conv.final_state[channel * 4u + i] = taps[i];
+  }
+  // one token: the same step as gdn_conv_kernel, including its log entry
+  __device__ __forceinline__ float step(const GdnConvArgs& conv, std::size_t index, bool log) {
+    const float y = h2f(gdn_conv_step(taps, w, ld_cg(conv.projected + index)));
+    if (log && conv.appended_log != nullptr) conv.appended_log[index] = taps[3];
+    return y;
+  }
+};
+
+// With FusedConv the CTA convolves its own channels (element thread t: q and
+// k channel t of key head kh, value channel t of head vh) instead of reading
+// a conv output; the conv state of the shared q/k channels is written by the
+// first value head of the key head only, after a cluster barrier that every
+// CTA of the key head reaches once it has read the initial state.
+template <class Sync, bool FusedConv = false>
 __device__ __forceinline__ void gdn_recurrent_tokens(const GdnRecurrentArgs& args, unsigned vh, unsigned t,
                                                      float (&S)[kGdnRows], Sync sync, GdnScratch& sc) {
   const unsigned lane = t & 31u, warp = t >> 5;
@@ -378,13 +406,32 @@ __device__ __forceinline__ void gdn_recurrent_tokens(const GdnRecurrentArgs& arg
   const float dt_bias = bf2f(args.dt_bias[vh]);
   const float norm_weight = element_thread ? bf2f(args.norm_weight[t]) : 0.0f;
   const std::uint32_t ab_stride = args.ab_stride != 0 ? args.ab_stride : args.value_heads;
+  const bool qk_owner = vh % ratio == 0;  // writes the shared q/k conv state and logs
+  const std::size_t q_channel = kh * kGdnHead + t, k_channel = key_elements + kh * kGdnHead + t;
+  const std::size_t v_channel = 2u * key_elements + vh * kGdnHead + t;
+  ConvChannel cq, ck, cv;
+  if constexpr (FusedConv) {
+    if (element_thread) {
+      cq.load(args.conv, q_channel);
+      ck.load(args.conv, k_channel);
+      cv.load(args.conv, v_channel);
+    }
+    cluster_arrive();  // this CTA has read the initial conv state
+  }
 
   for (std::uint32_t token = 0; token < args.batch; ++token) {
     const __half* qkv = args.qkv + static_cast<std::size_t>(token) * channels;
     float q = 0.0f, k = 0.0f;
     if (element_thread) {
-      q = h2f(ld_cg(qkv + kh * kGdnHead + t));
-      k = h2f(ld_cg(qkv + key_elements + kh * kGdnHead + t));
+      if constexpr (FusedConv) {
+        const std::size_t row = static_cast<std::size_t>(token) * channels;
+        q = cq.step(args.conv, row + q_channel, qk_owner);
+        k = ck.step(args.conv, row + k_channel, qk_owner);
+        sc.value[t] = cv.step(args.conv, row + v_channel, true);
+      } else {
+        q = h2f(ld_cg(qkv + kh * kGdnHead + t));
+        k = h2f(ld_cg(qkv + key_elements + kh * kGdnHead + t));
+      }
       const float qs = warp_sum_down(__fmul_rn(q, q));
       const float ks = warp_sum_down(__fmul_rn(k, k));
       if (lane == 0) {
@@ -429,7 +476,12 @@ __device__ __forceinline__ void gdn_recurrent_tokens(const GdnRecurrentArgs& arg
     }
     float delta = 0.0f;
     if (half == 1) {
-      const float value = h2f(ld_cg(qkv + 2u * key_elements + vh * kGdnHead + column));
+      float value;
+      if constexpr (FusedConv) {
+        value = sc.value[column];
+      } else {
+        value = h2f(ld_cg(qkv + 2u * key_elements + vh * kGdnHead + column));
+      }
       delta = __fmul_rn(__fsub_rn(value, memory), beta);
       if (args.delta_log != nullptr) {
         args.delta_log[static_cast<std::size_t>(token) * value_elements + vh * kGdnHead + column] = delta;
@@ -488,6 +540,16 @@ __device__ __forceinline__ void gdn_recurrent_tokens(const GdnRecurrentArgs& arg
       }
     }
     sync();  // query/key/mixed/sums are rewritten by the next token
+  }
+  if constexpr (FusedConv) {
+    cluster_wait();  // every CTA of the key head has read the initial conv state
+    if (element_thread) {
+      cv.store(args.conv, v_channel);
+      if (qk_owner) {
+        cq.store(args.conv, q_channel);
+        ck.store(args.conv, k_channel);
+      }
+    }
   }
 }
 
