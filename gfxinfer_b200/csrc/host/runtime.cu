@@ -28,6 +28,7 @@
 #include "host/artifact_internal.h"
 #include "kernels/common.cuh"
 #include "kernels/ops.cuh"
+#include "kernels/peer.cuh"
 #include "kernels/token_loop.cuh"
 
 namespace gfxb {
@@ -517,6 +518,12 @@ int build_weights(gfxb_engine& e, Planner& plan, bool generate, WeightSource& sr
 struct gfxb_session {
   gfxb_engine* e = nullptr;
   gfxb_session_config cfg{};
+  // tensor parallelism: the peer all-reduce's exchange buffers (own + mapped peers) and call counters
+  std::uint8_t* peer_buffer = nullptr;
+  std::uint8_t* exchange_peers[8] = {};
+  std::uint32_t* peer_epochs = nullptr;
+  std::uint32_t exchange_slot_floats = 0;
+  bool peer_reduce = false;
   std::byte* arena = nullptr;
   std::size_t arena_bytes = 0;
   cudaStream_t stream = nullptr;
@@ -597,8 +604,101 @@ int gemv(gfxb_session& s, const std::vector<std::pair<const QMatrix*, void*>>& m
 
 int all_reduce(gfxb_session& s, float* buffer, std::size_t count) {
   if (s.e->shard.tp == 1) return GFXB_OK;
+  if (s.peer_reduce && count % 4 == 0 && count <= s.exchange_slot_floats) {
+    PeerReduceArgs a;
+    a.data = buffer;
+    a.count = static_cast<std::uint32_t>(count);
+    a.rank = s.e->shard.rank;
+    a.ranks = s.e->shard.tp;
+    for (std::uint32_t r = 0; r < a.ranks; ++r) a.buffers[r] = s.exchange_peers[r];
+    a.epochs = s.peer_epochs;
+    a.slot_floats = s.exchange_slot_floats;
+    return launch_peer_all_reduce(a, s.stream);
+  }
   return nccl_check(nccl().all_reduce(buffer, buffer, count, ncclFloat, ncclSum, s.e->comm, s.stream),
                     "NCCL all-reduce failed");
+}
+
+// Peer all-reduce setup (collective over the TP ranks, NCCL for the exchange):
+// allocate and clear this rank's exchange buffer, gather every rank's IPC
+// handle, map the peers' buffers, then agree (a min-reduction of a success
+// flag) so that either every rank uses the peer path or none does.
+// GFXB_PEER_ALLREDUCE=1 selects it; NCCL otherwise.
+int setup_peer_reduce(gfxb_session& s) {
+  const Shard& sh = s.e->shard;
+  if (sh.tp == 1) return GFXB_OK;
+  const char* env = std::getenv("GFXB_PEER_ALLREDUCE");
+  if (env == nullptr || env[0] != '1') return GFXB_OK;
+  int ok = 1;
+  s.exchange_slot_floats = kMaxBlock * s.e->cfg.hidden;
+  const std::size_t bytes = peer_exchange_bytes(sh.tp, s.exchange_slot_floats);
+  cudaIpcMemHandle_t mine{};
+  if (ok) ok = cudaMalloc(&s.peer_buffer, bytes) == cudaSuccess ? 1 : 0;
+  if (ok) ok = cudaMalloc(&s.peer_epochs, kPeerCtas * sizeof(std::uint32_t)) == cudaSuccess ? 1 : 0;
+  if (ok) ok = cudaMemset(s.peer_buffer, 0, bytes) == cudaSuccess ? 1 : 0;
+  if (ok) ok = cudaMemset(s.peer_epochs, 0, kPeerCtas * sizeof(std::uint32_t)) == cudaSuccess ? 1 : 0;
+  if (ok) ok = cudaIpcGetMemHandle(&mine, s.peer_buffer) == cudaSuccess ? 1 : 0;
+  cudaGetLastError();
+  // gather the handles (64 bytes each) and the flags through device memory
+  std::uint8_t* staging = nullptr;
+  const std::size_t handle_bytes = sizeof(cudaIpcMemHandle_t);
+  GFXB_TRY(cuda_check(cudaMalloc(&staging, handle_bytes * (sh.tp + 1) + 8), "peer setup staging failed"));
+  std::vector<std::uint8_t> handles(handle_bytes * sh.tp);
+  int status = cuda_check(cudaMemcpy(staging + handle_bytes * sh.tp, &mine, handle_bytes, cudaMemcpyHostToDevice),
+                          "peer setup copy failed");
+  if (status == GFXB_OK) {
+    status = nccl_check(nccl().all_gather(staging + handle_bytes * sh.tp, staging, handle_bytes, ncclUint8,
+                                          s.e->comm, s.stream),
+                        "NCCL all-gather of IPC handles failed");
+  }
+  if (status == GFXB_OK) status = cuda_check(cudaStreamSynchronize(s.stream), "peer setup failed");
+  if (status == GFXB_OK) {
+    status = cuda_check(cudaMemcpy(handles.data(), staging, handles.size(), cudaMemcpyDeviceToHost),
+                        "peer setup copy failed");
+  }
+  for (std::uint32_t r = 0; status == GFXB_OK && ok && r < sh.tp; ++r) {
+    if (r == sh.rank) {
+      s.exchange_peers[r] = s.peer_buffer;
+      continue;
+    }
+    cudaIpcMemHandle_t handle;
+    std::memcpy(&handle, handles.data() + handle_bytes * r, handle_bytes);
+    void* mapped = nullptr;
+    if (cudaIpcOpenMemHandle(&mapped, handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = 0;
+      break;
+    }
+    s.exchange_peers[r] = static_cast<std::uint8_t*>(mapped);
+  }
+  // every rank must take the same path
+  std::int32_t agreed = ok;
+  if (status == GFXB_OK) {
+    status = cuda_check(cudaMemcpy(staging, &agreed, sizeof agreed, cudaMemcpyHostToDevice), "peer setup copy failed");
+  }
+  if (status == GFXB_OK) {
+    status = nccl_check(nccl().all_reduce(staging, staging, 1, ncclInt32, ncclMin, s.e->comm, s.stream),
+                        "NCCL agreement on the peer all-reduce failed");
+  }
+  if (status == GFXB_OK) status = cuda_check(cudaStreamSynchronize(s.stream), "peer setup failed");
+  if (status == GFXB_OK) {
+    status = cuda_check(cudaMemcpy(&agreed, staging, sizeof agreed, cudaMemcpyDeviceToHost), "peer setup copy failed");
+  }
+  cudaFree(staging);
+  s.peer_reduce = status == GFXB_OK && agreed == 1;
+  return status;
+}
+
+void release_peer_reduce(gfxb_session& s) {
+  for (std::uint32_t r = 0; r < 8; ++r) {
+    if (s.exchange_peers[r] != nullptr && s.exchange_peers[r] != s.peer_buffer) cudaIpcCloseMemHandle(s.exchange_peers[r]);
+    s.exchange_peers[r] = nullptr;
+  }
+  if (s.peer_buffer != nullptr) cudaFree(s.peer_buffer);
+  if (s.peer_epochs != nullptr) cudaFree(s.peer_epochs);
+  s.peer_buffer = nullptr;
+  s.peer_epochs = nullptr;
+  s.peer_reduce = false;
 }
 
 int norm_pack(gfxb_session& s, const __half* residual, const float* update, __half* residual_out,
@@ -1693,6 +1793,7 @@ extern "C" int gfxb_session_create(gfxb_engine* engine, const gfxb_session_confi
     status = cuda_check(cudaMallocHost(reinterpret_cast<void**>(&s->pinned), 256 * sizeof(std::uint32_t)),
                         "pinned staging allocation failed");
   }
+  if (status == GFXB_OK) status = setup_peer_reduce(*s);
   if (status == GFXB_OK && config->step_kernel > GFXB_STEP_PERSISTENT) {
     status = fail(GFXB_INVALID_ARGUMENT, "unknown step kernel");
   }
@@ -1706,6 +1807,7 @@ extern "C" int gfxb_session_create(gfxb_engine* engine, const gfxb_session_confi
     if (s->greedy_graph) cudaGraphExecDestroy(s->greedy_graph);
     if (s->spec_graph) cudaGraphExecDestroy(s->spec_graph);
     if (s->pinned) cudaFreeHost(s->pinned);
+    release_peer_reduce(*s);
     cudaFree(s->arena);
     return status;
   }
@@ -1721,6 +1823,7 @@ extern "C" int gfxb_session_destroy(gfxb_session* session) {
   if (session->spec_graph) cudaGraphExecDestroy(session->spec_graph);
   if (session->pinned) cudaFreeHost(session->pinned);
   if (session->loop_trace) cudaFree(session->loop_trace);
+  release_peer_reduce(*session);
   cudaFree(session->arena);
   delete session;
   return GFXB_OK;
@@ -2042,10 +2145,11 @@ extern "C" int gfxb_session_trace_step(gfxb_session* session, std::uint32_t inpu
 
 extern "C" int gfxb_read_device_errors(std::uint32_t* flags) {
   if (flags == nullptr) return fail(GFXB_INVALID_ARGUMENT, "null argument");
-  std::uint32_t a = 0, b = 0;
+  std::uint32_t a = 0, b = 0, c = 0;
   GFXB_TRY(read_gemv_error(&a, true));
   GFXB_TRY(read_ops_error(&b, true));
-  *flags = a | b;
+  GFXB_TRY(read_peer_errors(&c));
+  *flags = a | b | c;
   return GFXB_OK;
 }
 
