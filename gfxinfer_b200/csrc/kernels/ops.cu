@@ -132,6 +132,14 @@ __global__ void gdn_conv_kernel(GdnConvArgs args) {
 template <bool FusedConv>
 __global__ __launch_bounds__(kGdnThreads) void gdn_recurrent_kernel(GdnRecurrentArgs args) {
   pdl_trigger();
+  // The head's 64 KB state slice is pulled into L2 before waiting for the
+  // previous kernel: a prefetch is only a hint (L2 stays coherent with any
+  // later write, e.g. a rollback replay), and the loads below then hit L2.
+  if (threadIdx.x < 4u) {
+    const std::uint8_t* slice = reinterpret_cast<const std::uint8_t*>(args.initial_state) +
+                                (static_cast<std::size_t>(blockIdx.x) * kGdnHead * kGdnHead + threadIdx.x * 4096u) * 4u;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(slice), "r"(16384u) : "memory");
+  }
   pdl_wait();
   __shared__ GdnScratch scratch;
   const unsigned vh = blockIdx.x, t = threadIdx.x;
