@@ -378,6 +378,187 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
 }
 
 // ---------------------------------------------------------------------------
+// Cascaded split-K GEMV for 2 <= batch <= 8 (the causal verifier's widths).
+//
+// Same split as gemv_stream_kernel (a cluster of P CTAs per 16-row tile, CTA p
+// owns a contiguous range of the tile's groups), but no CTA gathers the whole
+// tile's dots, whose buffer grows with the batch (70 KB at 136 groups x 8
+// tokens) and would cut the CTAs per SM. CTA p keeps the dots of its own
+// groups, and its 16 x B chain threads run their segment of the ordered fp32
+// chain: CTA 0 starts it at zero, CTA p > 0 starts from the accumulators CTA
+// p - 1 sends with st.async (bytes counted on this CTA's mbarrier) and sends
+// its own on; the last CTA writes the outputs. The fma sequence per (row,
+// token) is the one over all groups in ascending order, hence identical bits.
+// ---------------------------------------------------------------------------
+
+struct CascadeLayout {
+  std::uint32_t per_part;      // groups per cluster rank
+  std::uint32_t weight_bytes;  // per_part * block
+  std::uint32_t scale_offset;  // own groups' scales [per_part][16] fp16
+  std::uint32_t dot_offset;    // own groups' dots [per_part][16][B] int32
+  std::uint32_t act_offset;    // own groups' activation scales [B][per_part] fp16
+  std::uint32_t acc_offset;    // incoming accumulators [16 * B] fp32
+  std::uint32_t bar_offset;    // chunk barriers, the scale barrier, the accumulator barrier
+  std::uint32_t total;
+};
+
+__host__ __device__ inline CascadeLayout cascade_layout(int bits, std::uint32_t groups, std::uint32_t parts,
+                                                        std::uint32_t batch, std::uint32_t chunk) {
+  CascadeLayout l{};
+  l.per_part = (groups + parts - 1u) / parts;
+  l.weight_bytes = l.per_part * static_cast<std::uint32_t>(bits) * 256u;
+  l.scale_offset = l.weight_bytes;
+  l.dot_offset = l.scale_offset + ((l.per_part * 32u + 15u) & ~15u);
+  l.act_offset = l.dot_offset + l.per_part * 16u * batch * 4u;
+  l.acc_offset = (l.act_offset + l.per_part * batch * 2u + 15u) & ~15u;
+  l.bar_offset = (l.acc_offset + 16u * batch * 4u + 15u) & ~15u;
+  const std::uint32_t bars = (l.per_part + chunk - 1u) / chunk + 2u;
+  l.total = l.bar_offset + bars * 8u;
+  return l;
+}
+
+template <int Bits>
+__global__ __launch_bounds__(256) void gemv_cascade_kernel(const GemvArgs args, std::uint32_t parts,
+                                                           std::uint32_t chunk) {
+  extern __shared__ __align__(128) std::uint8_t smem[];
+  pdl_trigger();
+  const std::uint32_t part = cluster_ctarank();
+  std::uint32_t tile = blockIdx.x / parts;
+  const MatrixArg m = select_matrix(args, tile);
+  const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const unsigned gl = lane >> 2, tq = lane & 3u;
+  const std::uint32_t G = args.groups, B = args.batch;
+  constexpr std::uint32_t kBlock = Bits * 256u;
+  constexpr int kAlpha = Codec<Bits>::alpha, kBeta = Codec<Bits>::beta;
+  const CascadeLayout layout = cascade_layout(Bits, G, parts, B, chunk);
+  const std::uint32_t g_begin = min(G, part * layout.per_part);
+  const std::uint32_t n = min(G, g_begin + layout.per_part) - g_begin;
+  const std::uint32_t chunks = (n + chunk - 1u) / chunk;
+  const std::uint32_t max_chunks = (layout.per_part + chunk - 1u) / chunk;
+  std::uint8_t* stage = smem;
+  __half* own_scales = reinterpret_cast<__half*>(smem + layout.scale_offset);
+  std::int32_t* dots = reinterpret_cast<std::int32_t*>(smem + layout.dot_offset);
+  __half* act_scale_stage = reinterpret_cast<__half*>(smem + layout.act_offset);
+  float* acc_in = reinterpret_cast<float*>(smem + layout.acc_offset);
+  std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(smem + layout.bar_offset);
+  const std::uint32_t scale_bar = max_chunks, acc_bar = max_chunks + 1u;
+
+  // Self-check of the launch geometry (uniform over the cluster: all return together).
+  {
+    std::uint32_t bad = 0;
+    if (cluster_nctarank() != parts || part >= parts || B < 1u || B > 8u) bad |= kGemvErrorCluster;
+    if (layout.total > dynamic_smem_bytes()) bad |= kGemvErrorSmem;
+    if (tile >= m.tiles) bad |= kGemvErrorTile;
+    if (bad != 0) {
+      if (threadIdx.x == 0) atomicOr(&g_gemv_error, bad);
+      return;
+    }
+  }
+
+  if (threadIdx.x == 0) {
+    for (std::uint32_t c = 0; c <= acc_bar; ++c) mbar_init(&bars[c], 1);
+    fence_mbar_init();
+    const std::uint8_t* source = m.codes + (static_cast<std::size_t>(tile) * G + g_begin) * kBlock;
+    for (std::uint32_t c = 0; c < chunks; ++c) {
+      const std::uint32_t bytes = min(chunk, n - chunk * c) * kBlock;
+      mbar_expect_tx(&bars[c], bytes);
+      bulk_g2s(stage + chunk * c * kBlock, source + chunk * c * kBlock, bytes, &bars[c]);
+    }
+    if (n != 0u) {
+      mbar_expect_tx(&bars[scale_bar], n * 32u);
+      bulk_g2s(own_scales, m.scales + (static_cast<std::size_t>(tile) * G + g_begin) * 16u, n * 32u,
+               &bars[scale_bar]);
+    }
+    // the previous rank's accumulators: 16 rows x B tokens x 4 bytes
+    if (part > 0u) mbar_expect_tx(&bars[acc_bar], 16u * B * 4u);
+  }
+  // every CTA of the cluster is running with its barriers initialised before
+  // the first store into another CTA's shared memory (the wait below)
+  cluster_arrive_relaxed();
+  pdl_wait();
+  const std::uint32_t act_groups = args.act_stride / kGroup;
+  for (std::uint32_t i = threadIdx.x; i < n * B; i += blockDim.x) {
+    const std::uint32_t tok = i / n, local = i - tok * n;
+    act_scale_stage[i] = args.act_scales[static_cast<std::size_t>(tok) * act_groups + g_begin + local];
+  }
+  const std::uint32_t next_acc = map_shared_rank(smem_addr(acc_in), part + 1u < parts ? part + 1u : part);
+  const std::uint32_t next_bar = map_shared_rank(smem_addr(&bars[acc_bar]), part + 1u < parts ? part + 1u : part);
+  const std::uint32_t token = min(gl, B - 1u);
+  cluster_wait();
+  bool ok = true;
+  for (std::uint32_t local = warp; local < n; local += 8u) {
+    const std::uint32_t g = g_begin + local;
+    const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * args.act_stride +
+                            static_cast<std::size_t>(g) * kGroup + tq * 32u;
+    const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(ap));
+    const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(ap + 16));
+    const std::uint32_t t0 = 2u * tq, t1 = t0 + 1u;
+    const int s0 = t0 < B ? __ldg(args.act_sums + t0 * act_groups + g) : 0;
+    const int s1 = t1 < B ? __ldg(args.act_sums + t1 * act_groups + g) : 0;
+    if (!mbar_wait_bounded(&bars[local / chunk], 0, &g_gemv_error)) {
+      ok = false;
+      break;
+    }
+    LaneWords<Bits> w;
+    load_lane_shared<Bits>(stage + local * kBlock, lane, w);
+    std::uint32_t a[4][4];
+    unpack(w, a);
+    int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+    mma_s8_16832(c0, a[0], b0.x, b0.y);
+    mma_s8_16832(c1, a[1], b0.z, b0.w);
+    mma_s8_16832(c0, a[2], b1.x, b1.y);
+    mma_s8_16832(c1, a[3], b1.z, b1.w);
+    const std::uint32_t row_base = local * 16u;
+    if (t0 < B) {
+      dots[(row_base + gl) * B + t0] = kAlpha * (c0[0] + c1[0]) + kBeta * s0;
+      dots[(row_base + gl + 8u) * B + t0] = kAlpha * (c0[2] + c1[2]) + kBeta * s0;
+    }
+    if (t1 < B) {
+      dots[(row_base + gl) * B + t1] = kAlpha * (c0[1] + c1[1]) + kBeta * s1;
+      dots[(row_base + gl + 8u) * B + t1] = kAlpha * (c0[3] + c1[3]) + kBeta * s1;
+    }
+  }
+  ok = __syncthreads_and(ok);  // also publishes the dots and the staged activation scales
+  if (threadIdx.x >= 16u * B) return;
+  const std::uint32_t row = threadIdx.x & 15u, tok = threadIdx.x >> 4;
+  if (ok && n != 0u && !mbar_wait_bounded(&bars[scale_bar], 0, &g_gemv_error)) ok = false;
+  float accumulator = 0.0f;
+  if (part > 0u) {
+    // Outlast the bounded waits of every earlier rank (their copies and their
+    // own accumulator waits, each longer than the one before), so that none
+    // can still be sending when this CTA exits.
+    bool arrived = false;
+    for (std::uint32_t r = 0; r < (max_chunks + 3u) * (part + 1u) && !arrived; ++r) {
+      for (std::uint32_t i = 0; i < kWaitLimit && !arrived; ++i) arrived = mbar_try_wait_cluster(&bars[acc_bar], 0);
+    }
+    if (!arrived) {
+      atomicOr(&g_gemv_error, kDeviceErrorTimeout);
+      return;
+    }
+    accumulator = acc_in[threadIdx.x];
+  }
+  if (ok) {
+    const __half* as = act_scale_stage + static_cast<std::size_t>(tok) * n;
+    for (std::uint32_t local = 0; local < n; ++local) {
+      const float product = __fmul_rn(h2f(own_scales[local * 16u + row]), h2f(as[local]));
+      accumulator = fmaf(static_cast<float>(dots[(local * 16u + row) * B + tok]), product, accumulator);
+    }
+  }
+  if (part + 1u < parts) {
+    // the next rank continues the chain (sent even after a failed wait, so that it does not stall)
+    st_async_s32(next_acc + threadIdx.x * 4u, __float_as_int(accumulator), next_bar);
+    return;
+  }
+  if (!ok) return;
+  const std::size_t index = static_cast<std::size_t>(tok) * (m.tiles * 16u) + tile * 16u + row;
+  if (m.output_f16) {
+    static_cast<__half*>(m.output)[index] = f2h(accumulator);
+  } else {
+    static_cast<float*>(m.output)[index] = accumulator;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Pipelined multi-tile GEMV for batch <= 8 and tall matrices.
 //
 // A grid of a few CTAs per SM; CTA c handles tiles c, c + grid, c + 2 grid,
@@ -582,6 +763,7 @@ struct StreamTuning {
   std::uint32_t parts = env_value("GFXB_GEMV_PARTS", 0);
   std::uint32_t chunk = std::max<std::uint32_t>(1u, env_value("GFXB_GEMV_CHUNK", 8));
   std::uint32_t min_tiles_p1 = env_value("GFXB_GEMV_P1_TILES", 1024);
+  std::uint32_t cascade = env_value("GFXB_GEMV_CASCADE", 1);  // 0: several tokens gather in one CTA too
 };
 
 const StreamTuning& tuning() {
@@ -596,6 +778,29 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
   if (tune.parts != 0) parts = tune.parts;
   while (parts > 1u && parts > args.groups) parts >>= 1;
   const std::uint32_t chunk = tune.chunk;
+  if (parts > 1u && tune.cascade != 0 && (args.batch >= 3u || (args.batch == 2u && args.groups > 64u))) {
+    // several tokens: the chain passes from rank to rank instead of gathering every dot in one CTA
+    // (measured on B200: faster from 3 tokens on, and at 2 tokens for long K)
+    const CascadeLayout layout = cascade_layout(Bits, args.groups, parts, args.batch, chunk);
+    static bool cascade_configured = false;
+    if (!cascade_configured) {
+      const cudaError_t error = cudaFuncSetAttribute(gemv_cascade_kernel<Bits>,
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (error != cudaSuccess) {
+        set_error_cuda(error, "GEMV shared-memory configuration failed");
+        return GFXB_CUDA_ERROR;
+      }
+      cascade_configured = true;
+    }
+    if (layout.total > 200u * 1024u) return fail(GFXB_UNSUPPORTED, "GEMV shape exceeds shared memory");
+    const cudaError_t error = launch_kernel(gemv_cascade_kernel<Bits>, dim3(total_tiles * parts), dim3(256),
+                                            layout.total, stream, parts, args, parts, chunk);
+    if (error != cudaSuccess) {
+      set_error_cuda(error, "cascaded GEMV launch failed");
+      return GFXB_CUDA_ERROR;
+    }
+    return GFXB_OK;
+  }
   const StreamLayout layout = stream_layout(Bits, args.groups, parts, args.batch, chunk);
   static int configured_bytes = 0;
   if (static_cast<int>(layout.total) > configured_bytes) {
