@@ -378,7 +378,7 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
 }
 
 // ---------------------------------------------------------------------------
-// Cascaded split-K GEMV for 2 <= batch <= 8 (the causal verifier's widths).
+// Cascaded split-K GEMV for 2 <= batch <= 16 (the causal verifier's widths).
 //
 // Same split as gemv_stream_kernel (a cluster of P CTAs per 16-row tile, CTA p
 // owns a contiguous range of the tile's groups), but no CTA gathers the whole
@@ -417,7 +417,7 @@ __host__ __device__ inline CascadeLayout cascade_layout(int bits, std::uint32_t 
   return l;
 }
 
-template <int Bits>
+template <int Bits, int NB>  // NB blocks of 8 tokens
 __global__ __launch_bounds__(256) void gemv_cascade_kernel(const GemvArgs args, std::uint32_t parts,
                                                            std::uint32_t chunk) {
   extern __shared__ __align__(128) std::uint8_t smem[];
@@ -446,7 +446,7 @@ __global__ __launch_bounds__(256) void gemv_cascade_kernel(const GemvArgs args, 
   // Self-check of the launch geometry (uniform over the cluster: all return together).
   {
     std::uint32_t bad = 0;
-    if (cluster_nctarank() != parts || part >= parts || B < 1u || B > 8u) bad |= kGemvErrorCluster;
+    if (cluster_nctarank() != parts || part >= parts || B < 1u || (B + 7u) / 8u != NB) bad |= kGemvErrorCluster;
     if (layout.total > dynamic_smem_bytes()) bad |= kGemvErrorSmem;
     if (tile >= m.tiles) bad |= kGemvErrorTile;
     if (bad != 0) {
@@ -483,18 +483,10 @@ __global__ __launch_bounds__(256) void gemv_cascade_kernel(const GemvArgs args, 
   }
   const std::uint32_t next_acc = map_shared_rank(smem_addr(acc_in), part + 1u < parts ? part + 1u : part);
   const std::uint32_t next_bar = map_shared_rank(smem_addr(&bars[acc_bar]), part + 1u < parts ? part + 1u : part);
-  const std::uint32_t token = min(gl, B - 1u);
   cluster_wait();
   bool ok = true;
   for (std::uint32_t local = warp; local < n; local += 8u) {
     const std::uint32_t g = g_begin + local;
-    const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * args.act_stride +
-                            static_cast<std::size_t>(g) * kGroup + tq * 32u;
-    const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(ap));
-    const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(ap + 16));
-    const std::uint32_t t0 = 2u * tq, t1 = t0 + 1u;
-    const int s0 = t0 < B ? __ldg(args.act_sums + t0 * act_groups + g) : 0;
-    const int s1 = t1 < B ? __ldg(args.act_sums + t1 * act_groups + g) : 0;
     if (!mbar_wait_bounded(&bars[local / chunk], 0, &g_gemv_error)) {
       ok = false;
       break;
@@ -503,19 +495,31 @@ __global__ __launch_bounds__(256) void gemv_cascade_kernel(const GemvArgs args, 
     load_lane_shared<Bits>(stage + local * kBlock, lane, w);
     std::uint32_t a[4][4];
     unpack(w, a);
-    int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
-    mma_s8_16832(c0, a[0], b0.x, b0.y);
-    mma_s8_16832(c1, a[1], b0.z, b0.w);
-    mma_s8_16832(c0, a[2], b1.x, b1.y);
-    mma_s8_16832(c1, a[3], b1.z, b1.w);
     const std::uint32_t row_base = local * 16u;
-    if (t0 < B) {
-      dots[(row_base + gl) * B + t0] = kAlpha * (c0[0] + c1[0]) + kBeta * s0;
-      dots[(row_base + gl + 8u) * B + t0] = kAlpha * (c0[2] + c1[2]) + kBeta * s0;
-    }
-    if (t1 < B) {
-      dots[(row_base + gl) * B + t1] = kAlpha * (c0[1] + c1[1]) + kBeta * s1;
-      dots[(row_base + gl + 8u) * B + t1] = kAlpha * (c0[3] + c1[3]) + kBeta * s1;
+    // tokens in blocks of 8 (the mma's N), the unpacked weights reused
+#pragma unroll
+    for (std::uint32_t tb = 0; tb < 8u * NB; tb += 8u) {
+      const std::uint32_t token = min(tb + gl, B - 1u);
+      const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * args.act_stride +
+                              static_cast<std::size_t>(g) * kGroup + tq * 32u;
+      const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(ap));
+      const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(ap + 16));
+      const std::uint32_t t0 = tb + 2u * tq, t1 = t0 + 1u;
+      const int s0 = t0 < B ? __ldg(args.act_sums + t0 * act_groups + g) : 0;
+      const int s1 = t1 < B ? __ldg(args.act_sums + t1 * act_groups + g) : 0;
+      int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+      mma_s8_16832(c0, a[0], b0.x, b0.y);
+      mma_s8_16832(c1, a[1], b0.z, b0.w);
+      mma_s8_16832(c0, a[2], b1.x, b1.y);
+      mma_s8_16832(c1, a[3], b1.z, b1.w);
+      if (t0 < B) {
+        dots[(row_base + gl) * B + t0] = kAlpha * (c0[0] + c1[0]) + kBeta * s0;
+        dots[(row_base + gl + 8u) * B + t0] = kAlpha * (c0[2] + c1[2]) + kBeta * s0;
+      }
+      if (t1 < B) {
+        dots[(row_base + gl) * B + t1] = kAlpha * (c0[1] + c1[1]) + kBeta * s1;
+        dots[(row_base + gl + 8u) * B + t1] = kAlpha * (c0[3] + c1[3]) + kBeta * s1;
+      }
     }
   }
   ok = __syncthreads_and(ok);  // also publishes the dots and the staged activation scales
@@ -771,6 +775,10 @@ const StreamTuning& tuning() {
   return t;
 }
 
+// launch_stream's answer when no streaming kernel takes the shape (more than 8
+// tokens without a cluster split): the caller uses the one-CTA-per-tile kernel.
+constexpr int kNoStreamPath = -1;
+
 template <int Bits>
 int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t stream) {
   const StreamTuning& tune = tuning();
@@ -778,14 +786,19 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
   if (tune.parts != 0) parts = tune.parts;
   while (parts > 1u && parts > args.groups) parts >>= 1;
   const std::uint32_t chunk = tune.chunk;
+  if (args.batch > 8u && (parts == 1u || tune.cascade == 0)) return kNoStreamPath;
   if (parts > 1u && tune.cascade != 0 && (args.batch >= 3u || (args.batch == 2u && args.groups > 64u))) {
     // several tokens: the chain passes from rank to rank instead of gathering every dot in one CTA
     // (measured on B200: faster from 3 tokens on, and at 2 tokens for long K)
     const CascadeLayout layout = cascade_layout(Bits, args.groups, parts, args.batch, chunk);
     static bool cascade_configured = false;
     if (!cascade_configured) {
-      const cudaError_t error = cudaFuncSetAttribute(gemv_cascade_kernel<Bits>,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      cudaError_t error = cudaFuncSetAttribute(gemv_cascade_kernel<Bits, 1>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (error == cudaSuccess) {
+        error = cudaFuncSetAttribute(gemv_cascade_kernel<Bits, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024);
+      }
       if (error != cudaSuccess) {
         set_error_cuda(error, "GEMV shared-memory configuration failed");
         return GFXB_CUDA_ERROR;
@@ -793,8 +806,11 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
       cascade_configured = true;
     }
     if (layout.total > 200u * 1024u) return fail(GFXB_UNSUPPORTED, "GEMV shape exceeds shared memory");
-    const cudaError_t error = launch_kernel(gemv_cascade_kernel<Bits>, dim3(total_tiles * parts), dim3(256),
-                                            layout.total, stream, parts, args, parts, chunk);
+    const cudaError_t error =
+        args.batch > 8u ? launch_kernel(gemv_cascade_kernel<Bits, 2>, dim3(total_tiles * parts), dim3(256),
+                                        layout.total, stream, parts, args, parts, chunk)
+                        : launch_kernel(gemv_cascade_kernel<Bits, 1>, dim3(total_tiles * parts), dim3(256),
+                                        layout.total, stream, parts, args, parts, chunk);
     if (error != cudaSuccess) {
       set_error_cuda(error, "cascaded GEMV launch failed");
       return GFXB_CUDA_ERROR;
@@ -1627,10 +1643,11 @@ int lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, unsigned matrix_co
       return launch_pipe<4>(args, grid, stream);
     }
   }
-  if (batch <= 8 && !force_v1) {
-    if (bits == 2) return launch_stream<2>(args, grid, stream);
-    if (bits == 3) return launch_stream<3>(args, grid, stream);
-    return launch_stream<4>(args, grid, stream);
+  if (batch <= 16 && !force_v1) {
+    const int status = bits == 2   ? launch_stream<2>(args, grid, stream)
+                       : bits == 3 ? launch_stream<3>(args, grid, stream)
+                                   : launch_stream<4>(args, grid, stream);
+    if (status != kNoStreamPath) return status;
   }
   if (bits == 2) launch_gemv_bits<2>(args, grid, stream);
   else if (bits == 3) launch_gemv_bits<3>(args, grid, stream);

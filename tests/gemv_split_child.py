@@ -23,7 +23,8 @@ def main() -> int:
     ops.require_sm100(0)
     oracle = Oracle()
     cases = [(W3, 48, 17 * 128, 1), (W4, 32, 3 * 128, 8), (W2, 160, 40 * 128, 5), (W3, 16, 128, 2),
-             (W4, 48, 40 * 128, 2), (W3, 32, 136 * 128, 3), (W2, 16, 131 * 128, 8)]
+             (W4, 48, 40 * 128, 2), (W3, 32, 136 * 128, 3), (W2, 16, 131 * 128, 8), (W3, 48, 17 * 128, 12),
+             (W4, 32, 40 * 128, 16)]
     for fmt, rows, cols, batch in cases:
         rng = np.random.default_rng(rows * 7 + cols + batch)
         w = rng.normal(0.0, 0.02, size=(rows, cols)).astype(np.float32)

@@ -248,8 +248,10 @@ def test_f16_activation_rejects_bad_arguments(ops):
 # the attention/GDN output projections [5120 x 6144]) split each tile's groups
 # over a cluster of CTAs; the non-leader CTAs send their int32 dots to the
 # leader with asynchronous shared-memory stores, and the leader runs the same
-# ordered fp32 chain, so the outputs stay bit-identical to the oracle. The
-# cases cover ragged splits (G = 131, G = 17) and a single-tile matrix.
+# ordered fp32 chain, so the outputs stay bit-identical to the oracle. From 3
+# tokens on, the ranks instead pass the chain's accumulators along (two
+# 8-token mma blocks beyond 8 tokens). The cases cover ragged splits (G = 131,
+# G = 17), a single-tile matrix and 9 and 16 tokens.
 @pytest.mark.parametrize("fmt,rows,cols,batch,bits", [
     (W3, 5120, 17408, 1, 4),
     (W3, 5120, 17408, 8, 4),
@@ -257,6 +259,8 @@ def test_f16_activation_rejects_bad_arguments(ops):
     (W4, 5120, 6144, 5, 8),
     (W2, 1024, 16768, 3, 8),
     (W4, 16, 2176, 2, 4),
+    (W3, 1024, 17408, 9, 4),
+    (W4, 5120, 6144, 16, 8),
 ])
 def test_wide_k_bit_exact(oracle, ops, fmt, rows, cols, batch, bits):
     codes, scales16, logical = _quantized(oracle, rows, cols, fmt, seed=rows + cols + batch)
