@@ -786,6 +786,8 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
   if (tune.parts != 0) parts = tune.parts;
   while (parts > 1u && parts > args.groups) parts >>= 1;
   const std::uint32_t chunk = tune.chunk;
+  // beyond 8 tokens tall matrices split in two as well: the cascade then takes them
+  if (args.batch > 8u && parts == 1u && tune.parts == 0 && args.groups >= 2u) parts = 2u;
   if (args.batch > 8u && (parts == 1u || tune.cascade == 0)) return kNoStreamPath;
   if (parts > 1u && tune.cascade != 0 && (args.batch >= 3u || (args.batch == 2u && args.groups > 64u))) {
     // several tokens: the chain passes from rank to rank instead of gathering every dot in one CTA

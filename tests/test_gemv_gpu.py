@@ -56,7 +56,7 @@ def _run_gemv(ops, fmt, b200, tiled, rows, cols, x16, bits, f16_out=False):
     return out.cpu().numpy()
 
 
-@pytest.mark.parametrize("batch", [1, 5])
+@pytest.mark.parametrize("batch", [1, 5, 9])
 @pytest.mark.parametrize("bits", [4, 8])
 def test_config0_w3_gemv_bit_exact(oracle, ops, batch, bits):
     rows, cols = 17408, 5120
