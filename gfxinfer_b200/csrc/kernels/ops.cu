@@ -129,7 +129,7 @@ __global__ void gdn_conv_kernel(GdnConvArgs args) {
 // and SiLU(z) gate.
 // ---------------------------------------------------------------------------
 
-template <bool FusedConv>
+template <bool FusedConv, bool Block>
 __global__ __launch_bounds__(kGdnThreads) void gdn_recurrent_kernel(GdnRecurrentArgs args) {
   pdl_trigger();
   // The head's 64 KB state slice is pulled into L2 before waiting for the
@@ -141,11 +141,16 @@ __global__ __launch_bounds__(kGdnThreads) void gdn_recurrent_kernel(GdnRecurrent
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(slice), "r"(16384u) : "memory");
   }
   pdl_wait();
-  __shared__ GdnScratch scratch;
   const unsigned vh = blockIdx.x, t = threadIdx.x;
   float S[kGdnRows];
   gdn_load_state(args, vh, t, S);
-  gdn_recurrent_tokens<BlockSync, FusedConv>(args, vh, t, S, BlockSync{}, scratch);
+  if constexpr (Block) {  // up to kGdnBlockMax tokens: the three-phase form
+    __shared__ GdnBlockScratch scratch;
+    gdn_recurrent_block<FusedConv>(args, vh, t, S, scratch);
+  } else {
+    __shared__ GdnScratch scratch;
+    gdn_recurrent_tokens<BlockSync, FusedConv>(args, vh, t, S, BlockSync{}, scratch);
+  }
   gdn_store_state(args, vh, t, S);
 }
 
@@ -481,10 +486,20 @@ int launch_gdn_recurrent(const GdnRecurrentArgs& args, cudaStream_t stream) {
       return fail(GFXB_INVALID_ARGUMENT, "fused GDN conv needs its weights and states and at most 8 value heads "
                                          "per key head");
     }
-    launch_kernel(gdn_recurrent_kernel<true>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, ratio, args);
+    if (args.batch >= 2u && args.batch <= kGdnBlockMax) {  // a verifier block: the three-phase form
+      launch_kernel(gdn_recurrent_kernel<true, true>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, ratio,
+                    args);
+    } else {
+      launch_kernel(gdn_recurrent_kernel<true, false>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, ratio,
+                    args);
+    }
   } else {
     if (args.qkv == nullptr) return fail(GFXB_INVALID_ARGUMENT, "invalid GDN recurrent arguments");
-    launch_kernel(gdn_recurrent_kernel<false>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, 0, args);
+    if (args.batch >= 2u && args.batch <= kGdnBlockMax) {  // a verifier block: the three-phase form
+      launch_kernel(gdn_recurrent_kernel<false, true>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, 0, args);
+    } else {
+      launch_kernel(gdn_recurrent_kernel<false, false>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, 0, args);
+    }
   }
   return launch_status("GDN recurrent launch failed");
 }

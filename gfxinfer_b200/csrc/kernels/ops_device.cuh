@@ -554,6 +554,215 @@ __device__ __forceinline__ void gdn_recurrent_tokens(const GdnRecurrentArgs& arg
 }
 
 // ---------------------------------------------------------------------------
+// The same GDN step for a block of up to kGdnBlockMax tokens, in three phases:
+// (1) for every token, the conv (serial over tokens per channel), the q/k
+// L2 norms and the decay/beta gates, none of which depend on the state; (2)
+// the delta-rule recurrence, the only serial part, which each (column, half)
+// thread pair runs for all tokens without a CTA barrier; (3) for every token,
+// the output RMSNorm, SiLU(z) gate and A4/A8 pack. Every value is computed
+// by the same operations in the same order as gdn_recurrent_tokens, so the
+// results are identical; only the barriers per token are gone.
+// ---------------------------------------------------------------------------
+
+constexpr unsigned kGdnBlockMax = 16;
+
+struct GdnBlockScratch {
+  float query[kGdnBlockMax][kGdnHead];  // raw, then normalized
+  float key[kGdnBlockMax][kGdnHead];
+  float value[kGdnBlockMax][kGdnHead];
+  float mixed[kGdnBlockMax][kGdnHead];
+  float sums[kGdnBlockMax][3][4];       // q, k, output sums of squares per warp
+  float gates[kGdnBlockMax][2];         // decay, beta
+  float pack_max[kGdnBlockMax][4];
+  int pack_sum[kGdnBlockMax][4];
+};
+
+template <bool FusedConv>
+__device__ __forceinline__ void gdn_recurrent_block(const GdnRecurrentArgs& args, unsigned vh, unsigned t,
+                                                    float (&S)[kGdnRows], GdnBlockScratch& sc) {
+  const unsigned lane = t & 31u, warp = t >> 5;
+  const bool element_thread = t < kGdnHead;
+  const unsigned column = t >> 1, half = t & 1u, row0 = half * kGdnRows;
+  const unsigned ratio = args.value_heads / args.key_heads;
+  const unsigned kh = vh / ratio;
+  const unsigned key_elements = args.key_heads * kGdnHead;
+  const unsigned value_elements = args.value_heads * kGdnHead;
+  const unsigned channels = 2u * key_elements + value_elements;
+  const std::uint32_t B = args.batch;
+  const float a_log = bf2f(args.a_log[vh]);
+  const float dt_bias = bf2f(args.dt_bias[vh]);
+  const float norm_weight = element_thread ? bf2f(args.norm_weight[t]) : 0.0f;
+  const std::uint32_t ab_stride = args.ab_stride != 0 ? args.ab_stride : args.value_heads;
+  const bool qk_owner = vh % ratio == 0;
+  const std::size_t q_channel = kh * kGdnHead + t, k_channel = key_elements + kh * kGdnHead + t;
+  const std::size_t v_channel = 2u * key_elements + vh * kGdnHead + t;
+  ConvChannel cq, ck, cv;
+  if constexpr (FusedConv) {
+    if (element_thread) {
+      cq.load(args.conv, q_channel);
+      ck.load(args.conv, k_channel);
+      cv.load(args.conv, v_channel);
+    }
+    cluster_arrive();  // this CTA has read the initial conv state
+  }
+  // ---- phase 1: inputs, norms and gates of every token ----
+  if (element_thread) {
+    for (std::uint32_t token = 0; token < B; ++token) {
+      float q, k, v;
+      if constexpr (FusedConv) {
+        const std::size_t row = static_cast<std::size_t>(token) * channels;
+        q = cq.step(args.conv, row + q_channel, qk_owner);
+        k = ck.step(args.conv, row + k_channel, qk_owner);
+        v = cv.step(args.conv, row + v_channel, true);
+      } else {
+        const __half* qkv = args.qkv + static_cast<std::size_t>(token) * channels;
+        q = h2f(ld_cg(qkv + kh * kGdnHead + t));
+        k = h2f(ld_cg(qkv + key_elements + kh * kGdnHead + t));
+        v = h2f(ld_cg(qkv + 2u * key_elements + vh * kGdnHead + t));
+      }
+      sc.query[token][t] = q;
+      sc.key[token][t] = k;
+      sc.value[token][t] = v;
+      const float qs = warp_sum_down(__fmul_rn(q, q));
+      const float ks = warp_sum_down(__fmul_rn(k, k));
+      if (lane == 0) {
+        sc.sums[token][0][warp] = qs;
+        sc.sums[token][1][warp] = ks;
+      }
+    }
+  } else if (t - kGdnHead < B) {
+    // thread 128 + i: the gates of token i, meanwhile
+    const std::uint32_t token = t - kGdnHead;
+    const float a_value = __fadd_rn(ld_cg(args.a + static_cast<std::size_t>(token) * ab_stride + vh), dt_bias);
+    const float softplus = a_value > 20.0f ? a_value : gx_log1pf(gx_expf(a_value));
+    const float g = __fmul_rn(-gx_expf(a_log), softplus);
+    const float decay = gx_expf(g);
+    sc.gates[token][0] = decay;
+    sc.gates[token][1] = gx_sigmoid(ld_cg(args.b + static_cast<std::size_t>(token) * ab_stride + vh));
+    if (args.decay_log != nullptr) args.decay_log[static_cast<std::size_t>(token) * args.value_heads + vh] = decay;
+  }
+  __syncthreads();
+  if (element_thread) {
+    for (std::uint32_t token = 0; token < B; ++token) {
+      const float inv_q =
+          __fmul_rn(inv_sqrt_rn(__fadd_rn(tree_of_eight(sc.sums[token][0], 4), 1.0e-6f)), 0.08838834764831845f);
+      const float inv_k = inv_sqrt_rn(__fadd_rn(tree_of_eight(sc.sums[token][1], 4), 1.0e-6f));
+      const float kn = __fmul_rn(sc.key[token][t], inv_k);
+      sc.query[token][t] = __fmul_rn(sc.query[token][t], inv_q);
+      sc.key[token][t] = kn;
+      if (args.key_log != nullptr && qk_owner) {
+        args.key_log[static_cast<std::size_t>(token) * key_elements + kh * kGdnHead + t] = kn;
+      }
+    }
+  }
+  __syncthreads();
+  // ---- phase 2: the recurrence (one thread pair per state column, no CTA barrier) ----
+  for (std::uint32_t token = 0; token < B; ++token) {
+    const float decay = sc.gates[token][0], beta = sc.gates[token][1];
+    const float* key = sc.key[token];
+    const float* query = sc.query[token];
+    float memory = 0.0f;
+#pragma unroll
+    for (unsigned kk = 0; kk < kGdnRows; ++kk) {
+      S[kk] = __fmul_rn(S[kk], decay);
+      if (half == 0) memory = fmaf(S[kk], key[kk], memory);
+    }
+    const float carried = __shfl_up_sync(0xffffffffu, memory, 1);
+    if (half == 1) {
+      memory = carried;
+#pragma unroll
+      for (unsigned kk = 0; kk < kGdnRows; ++kk) memory = fmaf(S[kk], key[kGdnRows + kk], memory);
+    }
+    float delta = 0.0f;
+    if (half == 1) {
+      delta = __fmul_rn(__fsub_rn(sc.value[token][column], memory), beta);
+      if (args.delta_log != nullptr) {
+        args.delta_log[static_cast<std::size_t>(token) * value_elements + vh * kGdnHead + column] = delta;
+      }
+    }
+    delta = __shfl_sync(0xffffffffu, delta, lane | 1u);
+    float mixed = 0.0f;
+#pragma unroll
+    for (unsigned kk = 0; kk < kGdnRows; ++kk) {
+      S[kk] = fmaf(key[row0 + kk], delta, S[kk]);
+      if (half == 0) mixed = fmaf(S[kk], query[kk], mixed);
+    }
+    const float mixed_carried = __shfl_up_sync(0xffffffffu, mixed, 1);
+    if (half == 1) {
+      mixed = mixed_carried;
+#pragma unroll
+      for (unsigned kk = 0; kk < kGdnRows; ++kk) mixed = fmaf(S[kk], query[kGdnRows + kk], mixed);
+      sc.mixed[token][column] = mixed;
+    }
+  }
+  __syncthreads();
+  // ---- phase 3: output norm, gate and pack of every token ----
+  if (element_thread) {
+    for (std::uint32_t token = 0; token < B; ++token) {
+      const float m = sc.mixed[token][t];
+      const float os = warp_sum_down(__fmul_rn(m, m));
+      if (lane == 0) sc.sums[token][2][warp] = os;
+    }
+  }
+  __syncthreads();
+  for (std::uint32_t token = 0; token < B; ++token) {
+    float y_value = 0.0f;
+    if (element_thread) {
+      const float m = sc.mixed[token][t];
+      const float inv_o = inv_sqrt_rn(__fadd_rn(__fdiv_rn(tree_of_eight(sc.sums[token][2], 4), 128.0f), 1.0e-6f));
+      const float z = ld_cg(args.z + static_cast<std::size_t>(token) * value_elements + vh * kGdnHead + t);
+      const float normalized = __fmul_rn(__fmul_rn(m, inv_o), norm_weight);
+      const __half y = f2h(__fmul_rn(normalized, gx_silu(z)));
+      args.output[static_cast<std::size_t>(token) * value_elements + vh * kGdnHead + t] = y;
+      y_value = h2f(y);
+    }
+    if (element_thread) sc.mixed[token][t] = y_value;  // its own slot: the packer reads y here
+    if (args.act_bits != 0) {
+      const float amax = warp_amax(y_value);
+      if (element_thread && lane == 0) sc.pack_max[token][warp] = amax;
+    }
+  }
+  if (args.act_bits != 0) {
+    __syncthreads();
+    if (element_thread) {
+      for (std::uint32_t token = 0; token < B; ++token) {
+        const std::size_t row = static_cast<std::size_t>(token) * value_elements + vh * kGdnHead;
+        const float* pm = sc.pack_max[token];
+        const float amax = fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]));
+        const __half scale_h = args.act_bits == 8 ? act_scale_of<8>(amax) : act_scale_of<4>(amax);
+        const float scale = h2f(scale_h), recip = __frcp_rn(scale);
+        const float y_value = sc.mixed[token][t];
+        const int code =
+            args.act_bits == 8 ? act_code_fast<8>(y_value, scale, recip) : act_code_fast<4>(y_value, scale, recip);
+        args.act_codes[row + fragment_offset(t)] = static_cast<std::int8_t>(code);
+        const int total = warp_sum_int(code);
+        if (lane == 0) sc.pack_sum[token][warp] = total;
+      }
+    }
+    __syncthreads();
+    if (t < B) {
+      const std::uint32_t token = t;
+      const float* pm = sc.pack_max[token];
+      const float amax = fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]));
+      const std::size_t group = static_cast<std::size_t>(token) * args.value_heads + vh;
+      args.act_scales[group] = args.act_bits == 8 ? act_scale_of<8>(amax) : act_scale_of<4>(amax);
+      args.act_sums[group] = sc.pack_sum[token][0] + sc.pack_sum[token][1] + sc.pack_sum[token][2] +
+                             sc.pack_sum[token][3];
+    }
+  }
+  if constexpr (FusedConv) {
+    cluster_wait();  // every CTA of the key head has read the initial conv state
+    if (element_thread) {
+      cv.store(args.conv, v_channel);
+      if (qk_owner) {
+        cq.store(args.conv, q_channel);
+        ck.store(args.conv, k_channel);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Q/K RMSNorm(1+w) + NeoX RoPE for one 256-wide head (qwen_ops.hip:599-696).
 // 256 threads; thread d returns output element d. `normalized` (256 floats)
 // and `warp_sums` (8) are shared scratch, free again when this returns.

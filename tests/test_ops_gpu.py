@@ -104,7 +104,7 @@ def _gpu_gdn(lib, inputs, nk, nv, batch, logs=False):
     return cpu(out).view(np.uint16), cpu(final), cpu(key_log), cpu(delta_log), cpu(decay_log)
 
 
-@pytest.mark.parametrize("batch", [1, 3, 32])
+@pytest.mark.parametrize("batch", [1, 3, 16, 17, 32])  # 2 to 16 tokens: the three-phase block form
 def test_gdn_recurrent_config1_bit_exact(oracle, lib, batch):
     nk, nv = 16, 48
     rng = np.random.default_rng(batch)
