@@ -43,7 +43,10 @@ def _kernels_per_step(cfg: dict, tp: int) -> int:
     layers = cfg["layers"]
     attention = layers // cfg["attention_interval"]
     gdn = layers - attention
-    per_gdn, per_attention = 9, 10  # see gfxinfer_b200/csrc/host/runtime.cu enqueue_forward
+    # see gfxinfer_b200/csrc/host/runtime.cu enqueue_forward: a GDN layer is in-projection GEMV, recurrent step
+    # (causal conv inside), out-projection, norm, gate/up, SiLU pack, down, norm; an attention layer has q/k/v,
+    # Q/K norm + RoPE, attention chunk and merge, o_proj, then the same five
+    per_gdn, per_attention = 8, 10
     head = 1 + 2 + (2 if tp > 1 else 0)  # LM-head GEMV, argmax (2), TP exchange/select
     return 1 + gdn * per_gdn + attention * per_attention + head + 1  # embed+norm ... advance
 
