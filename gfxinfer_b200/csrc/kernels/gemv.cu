@@ -768,6 +768,7 @@ struct StreamTuning {
   std::uint32_t chunk = std::max<std::uint32_t>(1u, env_value("GFXB_GEMV_CHUNK", 8));
   std::uint32_t min_tiles_p1 = env_value("GFXB_GEMV_P1_TILES", 1024);
   std::uint32_t cascade = env_value("GFXB_GEMV_CASCADE", 1);  // 0: several tokens gather in one CTA too
+  std::uint32_t tall_cascade = std::max<std::uint32_t>(2u, env_value("GFXB_GEMV_TALL_CASCADE", 9));  // tokens from which tall matrices split in two
 };
 
 const StreamTuning& tuning() {
@@ -787,7 +788,7 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
   while (parts > 1u && parts > args.groups) parts >>= 1;
   const std::uint32_t chunk = tune.chunk;
   // beyond 8 tokens tall matrices split in two as well: the cascade then takes them
-  if (args.batch > 8u && parts == 1u && tune.parts == 0 && args.groups >= 2u) parts = 2u;
+  if (args.batch >= tune.tall_cascade && parts == 1u && tune.parts == 0 && args.groups >= 2u) parts = 2u;
   if (args.batch > 8u && (parts == 1u || tune.cascade == 0)) return kNoStreamPath;
   if (parts > 1u && tune.cascade != 0 && (args.batch >= 3u || (args.batch == 2u && args.groups > 64u))) {
     // several tokens: the chain passes from rank to rank instead of gathering every dot in one CTA
@@ -1636,7 +1637,7 @@ int lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, unsigned matrix_co
   const unsigned grid = static_cast<unsigned>(total_tiles);
   static const bool force_v1 = env_value("GFXB_GEMV_V1", 0) != 0;
   static const std::uint32_t pipe_mode = env_value("GFXB_GEMV_PIPE", 1);  // 0: never, 1: tall matrices, 2: always
-  if (batch <= 8 && !force_v1 && pipe_mode != 0) {
+  if (batch <= 8 && batch < tuning().tall_cascade && !force_v1 && pipe_mode != 0) {
     // tall matrices (one CTA per tile would need several waves) whose two stages leave room for two CTAs per SM
     const PipeLayout pipe = pipe_layout(bits, args.groups, batch);
     if ((pipe_mode == 2 || total_tiles >= tuning().min_tiles_p1) && pipe.total <= 100u * 1024u) {
