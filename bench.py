@@ -150,9 +150,11 @@ def _dist():
 
 
 class CpuSample:
-    """The reference path's CPU implementation on this host: the oracle's scalar forward (C, OpenMP over
-    all host cores). The model holds 4 of the 64 config-2 layers (3 GDN + 1 attention, the repeating unit)
-    and the full LM head at full width; per token, layer time is scaled x16 to the full depth."""
+    """The reference path's CPU implementation on this host: the oracle's C forward (OpenMP over all host
+    cores, AVX2 integer group dots), the reference having no CPU forward of its own. Every token runs all 64
+    config-2 layers (48 GDN + 16 attention, each with its own recurrent state and KV cache) and the full LM
+    head; the weights of 4 layers (the repeating 3 GDN + 1 attention unit) are reused 16 times so that the
+    model fits host memory. Each step is one whole greedy token, timed by the host clock."""
 
     def __init__(self) -> None:
         sys.path.insert(0, os.path.join(ROOT, "tests"))
@@ -160,28 +162,27 @@ class CpuSample:
 
         self.oracle = Oracle()
         self.cores = int(self.oracle.lib.or_set_threads(os.cpu_count() or 1))
-        cfg = model_config(layers=4, max_context=64)
+        cfg = model_config(max_context=512)
         start = time.perf_counter()
-        self.model = OracleModel(self.oracle, cfg, include_mtp=False)
+        self.model = OracleModel(self.oracle, cfg, include_mtp=False, resident_layers=4)
         self.build_seconds = time.perf_counter() - start
         self.token = 1
-        self.scale = 64 / 4
 
     def step(self) -> float:
-        """One sampled token; returns the extrapolated seconds per full 64-layer token."""
-        layer0, head0, _ = self.model.timing()
+        """One full greedy token (64 layers + LM head + argmax); returns its seconds."""
+        start = time.perf_counter()
         self.token = self.model.greedy_step(self.token)
-        layer1, head1, _ = self.model.timing()
-        return (layer1 - layer0) * self.scale + (head1 - head0)
+        return time.perf_counter() - start
 
     def describe(self, tokens: int) -> str:
-        return (f"{tokens} greedy tokens through 4 of 64 config-2 layers (3 GDN + 1 attention) and the full "
-                f"LM head (vocab 151936) at full width, scalar C forward on {self.cores} threads; layer time "
-                f"x16 + head time per token")
+        return (f"{tokens} greedy tokens, each through all 64 config-2 layers (weights of 4 layers reused 16x) "
+                f"and the full LM head (vocab 151936), C forward with AVX2 integer dots on {self.cores} threads, "
+                f"host clock per token")
 
 
-def cpu_baseline(tokens: int = 2) -> dict:
+def cpu_baseline(tokens: int = 5) -> dict:
     sample = CpuSample()
+    sample.step()  # first-touch warm-up
     seconds = [sample.step() for _ in range(tokens)]
     value = 1.0 / statistics.mean(seconds)
     return {"value": round(value, 4), "unit": UNIT, "cores": sample.cores, "kind": "port",
@@ -209,7 +210,8 @@ def run_reference(args) -> None:
                        "global_batch": 1, "seq_len": 512, "parallelism": "cpu"},
             "cpu_baseline": {"value": round(tokens_per_s, 4), "unit": UNIT, "cores": sample.cores, "kind": "port",
                              "sample": sample.describe(args.steps)},
-            "e2e": {"value": round(tokens_per_s, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(tokens_per_s, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "timed_seconds": round(sum(seconds), 3), "model_build_seconds": round(sample.build_seconds, 3)}
     print(json.dumps(line), flush=True)
 
 
@@ -307,6 +309,27 @@ def measure_config4(gs, np, torch, world: int, rank: int, local: int, nccl_id, s
             "per_gpu_GBps": round(weight_bytes / (decode_ms / steps / 1000.0) / 1e9, 1),
             "mlp_gate_up_gemv_GBps_per_gpu": round(gemv_bytes / (gemv_us * 1e-6) / 1e9, 1),
             "mlp_gate_up_gemv_us": round(gemv_us, 3)}
+
+
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one W3A4 MLP gate+up launch, from the ncu
+# capture summarised in profiles/gemv_pipe_w3_gate_up_config2_ncu.md.
+GATE_UP_DRAM_BYTES = None
+
+
+def measure_config0(peak: float) -> dict:
+    """BASELINE config 0 on the device: the W3A4 [17408 x 5120] GEMV at batch 1 and 5 (bench-gemv's
+    workload: six weight copies rotated so every launch reads HBM, launches replayed from a CUDA
+    graph, CUDA events), against the north star's >= 60 % of HBM roofline."""
+    from gfxinfer_b200 import bench_gemv
+
+    out = {"workload": "config-0 W3A4 GEMV [17408x5120], fp16 group scales, A4 activations, fp32 out",
+           "peak_GBps": peak}
+    for batch in (1, 5):
+        r = bench_gemv.run("w3", 17408, 5120, batch, "a4", 60, 6, True)
+        out[f"b{batch}"] = {"us": r["mean_launch_us"], "GBps": r["algorithmic_GBps"],
+                            "packed_code_GBps": r["packed_GBps"], "algorithmic_bytes": r["algorithmic_bytes"],
+                            "frac": round(r["algorithmic_GBps"] / peak, 4)}
+    return out
 
 
 def run_b200(args) -> None:
@@ -426,7 +449,8 @@ def run_b200(args) -> None:
             "gpu_launches": _kernels_per_step(cfg, world) * args.steps,
             "roofline": {"bound": "hbm", "kernel": "W3A4 MLP gate+up GEMV [2x17408x5120] (one launch)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_source": peak_note, "traffic": None,
+                         "frac": round(achieved / peak, 4), "peak_source": peak_note,
+                         "traffic": GATE_UP_DRAM_BYTES,
                          "algorithmic_bytes_per_launch": gemv_bytes, "launch_us": round(gemv_us, 3)},
             "decode_roofline": {"weight_bytes_per_token_per_gpu": per_step_bytes,
                                 "achieved_GBps_per_gpu": round(per_step_bytes / (device_ms / args.steps / 1000.0) / 1e9, 1),
@@ -434,7 +458,7 @@ def run_b200(args) -> None:
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(2)
+            line["cpu_baseline"] = cpu_baseline(5)
     if watchdog is not None:
         watchdog.stop()
     session.close()
@@ -451,6 +475,7 @@ def run_b200(args) -> None:
         extras["config4"] = measure_config4(gs, np, torch, world, rank, local, config4_id, min(args.steps, 96), barrier)
         if world == 1:
             extras["mtp"] = measure_mtp(gs, np, torch, local)
+            extras["config0"] = measure_config0(line["roofline"]["peak"])
     if rank == 0:
         line.update(extras)
         print(json.dumps(line), flush=True)

@@ -105,6 +105,9 @@ SIGNATURES: dict[str, tuple] = {
     "gfxb_session_block_step": (c_int, [P, POINTER(c_uint32), c_uint, POINTER(c_uint32)]),
     "gfxb_session_mtp_draft": (c_int, [P, c_uint32, POINTER(c_uint32)]),
     "gfxb_session_speculative_step": (c_int, [P, c_uint32, c_uint, POINTER(c_uint32), POINTER(c_uint), POINTER(c_uint)]),
+    "gfxb_session_speculative_step_with_drafts": (c_int, [P, c_uint32, POINTER(c_uint32), c_uint, POINTER(c_uint32),
+                                                          POINTER(c_uint), POINTER(c_uint)]),
+    "gfxb_session_prefill": (c_int, [P, POINTER(c_uint32), c_size_t, POINTER(c_uint32)]),
     "gfxb_session_position": (c_int, [P, POINTER(c_uint64)]),
     "gfxb_session_enqueue_greedy": (c_int, [P, c_uint32, c_uint]),
     "gfxb_session_sync": (c_int, [P]),

@@ -549,6 +549,7 @@ struct gfxb_session {
   // MTP
   __half *mtp_hidden = nullptr, *mtp_input = nullptr, *mtp_embed = nullptr, *target_snapshot = nullptr;
   std::uint32_t* draft_tokens = nullptr;  // [kMaxBlock]
+  std::uint32_t* external_drafts = nullptr;  // [kMaxBlock] caller-supplied drafts
   std::uint64_t* mtp_positions = nullptr; // [kMaxBlock]
   std::uint32_t* seed_token = nullptr;
   // states
@@ -898,7 +899,7 @@ __global__ void exchange_kernel(const float* values, const std::uint32_t* indice
 }
 
 int head_argmax(gfxb_session& s, const QMatrix& head_rows, std::uint32_t rows, std::uint32_t* out_tokens,
-                unsigned batch) {
+                unsigned batch, std::size_t act_offset = 0) {
   const Shard& sh = s.e->shard;
   QMatrix head = head_rows;
   if (rows == 0) {
@@ -908,7 +909,7 @@ int head_argmax(gfxb_session& s, const QMatrix& head_rows, std::uint32_t rows, s
     GFXB_TRY(cuda_check(cudaMemsetAsync(s.exchange, 0xff, kMaxBlock * 2 * sizeof(std::uint32_t), s.stream), "memset"));
   } else {
     head.rows = rows;
-    GFXB_TRY(gemv(s, {{&head, s.logits}}, batch));
+    GFXB_TRY(gemv(s, {{&head, s.logits}}, batch, act_offset));
     ArgmaxArgs a;
     a.logits = s.logits;
     a.row_stride = rows;
@@ -928,11 +929,16 @@ int head_argmax(gfxb_session& s, const QMatrix& head_rows, std::uint32_t rows, s
   return launch_status("argmax selection failed");
 }
 
+// Which tokens of a block get the LM head and argmax: all of them (greedy and
+// block steps, the verifier), the last one only (the final block of a
+// prefill) or none (the other prefill blocks).
+enum class Head { all, last, none };
+
 // The causal block forward (qwen_runtime.cpp:349-544, 1264-1392): tokens and
 // base position are read from device memory, so the same launch sequence
 // serves the eager path and captured graphs.
 int enqueue_forward(gfxb_session& s, unsigned batch, const std::uint32_t* device_tokens,
-                    const std::uint64_t* device_position, bool record) {
+                    const std::uint64_t* device_position, bool record, Head head = Head::all) {
   gfxb_engine& e = *s.e;
   const gfxb_model_config& c = e.cfg;
   __half* current = s.hidden[0];
@@ -954,6 +960,10 @@ int enqueue_forward(gfxb_session& s, unsigned batch, const std::uint32_t* device
     std::swap(current, next);
   }
   s.last_hidden = current + static_cast<std::size_t>(batch - 1) * c.hidden;
+  if (head == Head::none) return GFXB_OK;
+  if (head == Head::last) {
+    return head_argmax(s, e.lm_head, e.shard.vocab, s.selected, 1, static_cast<std::size_t>(batch - 1) * c.hidden);
+  }
   return head_argmax(s, e.lm_head, e.shard.vocab, s.selected, batch);
 }
 
@@ -1250,11 +1260,17 @@ int enqueue_greedy_step(gfxb_session& s) {
 // drafts and verifier tokens copied to pinned host memory. Reads only device
 // scalars (positions, seed) set before it runs, so it can be captured once
 // and replayed every round (prepare_speculative_graphs, :642-713).
-int enqueue_speculative_body(gfxb_session& s, unsigned drafts) {
+int enqueue_speculative_body(gfxb_session& s, unsigned drafts, bool external = false) {
   for (unsigned i = 0; i < drafts; ++i) {
     const std::uint32_t* token = i == 0 ? s.seed_token : s.draft_tokens + i - 1;
     const __half* conditioning = i == 0 ? s.target_snapshot : s.mtp_hidden;
     GFXB_TRY(enqueue_mtp(s, token, conditioning, s.mtp_positions + i, s.draft_tokens + i));
+  }
+  if (external) {
+    // the caller's drafts replace the MTP proposals; the MTP cache keeps the chain's entries
+    GFXB_TRY(cuda_check(cudaMemcpyAsync(s.draft_tokens, s.external_drafts, drafts * sizeof(std::uint32_t),
+                                        cudaMemcpyDeviceToDevice, s.stream),
+                        "external draft copy failed"));
   }
   copy_drafts_kernel<<<1, kMaxBlock, 0, s.stream>>>(s.draft_tokens, s.tokens, drafts);
   GFXB_TRY(launch_status("draft copy failed"));
@@ -1340,6 +1356,7 @@ int allocate_session(gfxb_session& s, bool place) {
   s.mtp_embed = plan.take<__half>(H);
   s.target_snapshot = plan.take<__half>(H);
   s.draft_tokens = plan.take<std::uint32_t>(B);
+  s.external_drafts = plan.take<std::uint32_t>(B);
   s.mtp_positions = plan.take<std::uint64_t>(B);
   s.seed_token = plan.take<std::uint32_t>(1);
   const std::size_t conv_elems = static_cast<std::size_t>(e.gdn_layers) * sh.channels * 4;
@@ -1956,12 +1973,12 @@ extern "C" int gfxb_session_mtp_draft(gfxb_session* session, std::uint32_t next_
   return GFXB_OK;
 }
 
-extern "C" int gfxb_session_speculative_step(gfxb_session* session, std::uint32_t seed_token, unsigned draft_count,
-                                             std::uint32_t* tokens, unsigned* token_count, unsigned* accepted_out) {
-  if (session == nullptr || tokens == nullptr || token_count == nullptr || accepted_out == nullptr) {
-    return fail(GFXB_INVALID_ARGUMENT, "null argument");
-  }
-  gfxb_session& s = *session;
+namespace {
+
+// One speculative round (qwen_runtime.cpp:1421-1544). drafts == nullptr: the
+// MTP chain's proposals are verified; otherwise the caller's.
+int speculative_round(gfxb_session& s, std::uint32_t seed_token, unsigned draft_count, const std::uint32_t* drafts,
+                      std::uint32_t* tokens, unsigned* token_count, unsigned* accepted_out) {
   if (!s.e->has_mtp) return fail(GFXB_UNSUPPORTED, "engine was created without the MTP layer");
   if (!s.have_last_hidden || draft_count == 0 || draft_count >= kMaxBlock || seed_token >= s.e->cfg.vocab ||
       s.mtp_position + 1 != s.host_position ||
@@ -1977,8 +1994,14 @@ extern "C" int gfxb_session_speculative_step(gfxb_session* session, std::uint32_
   set_positions_kernel<<<1, 1, 0, s.stream>>>(s.position, base, s.mtp_positions, mtp_base, draft_count, s.seed_token,
                                                seed_token, s.tokens);
   GFXB_TRY(launch_status("position setup failed"));
-  // the captured round when its draft count matches (launch_prepared_speculative_graph, :888-934)
-  if (s.spec_graph != nullptr && draft_count == s.spec_drafts) {
+  if (drafts != nullptr) {
+    std::memcpy(s.pinned + 192, drafts, draft_count * sizeof(std::uint32_t));
+    GFXB_TRY(cuda_check(cudaMemcpyAsync(s.external_drafts, s.pinned + 192, draft_count * sizeof(std::uint32_t),
+                                        cudaMemcpyHostToDevice, s.stream),
+                        "draft upload failed"));
+    GFXB_TRY(enqueue_speculative_body(s, draft_count, true));
+  } else if (s.spec_graph != nullptr && draft_count == s.spec_drafts) {
+    // the captured round when its draft count matches (launch_prepared_speculative_graph, :888-934)
     GFXB_TRY(cuda_check(cudaGraphLaunch(s.spec_graph, s.stream), "speculative graph launch failed"));
   } else {
     GFXB_TRY(enqueue_speculative_body(s, draft_count));
@@ -2037,6 +2060,55 @@ extern "C" int gfxb_session_speculative_step(gfxb_session* session, std::uint32_
   tokens[accepted] = host[kMaxBlock + accepted];
   *token_count = accepted + 1;
   *accepted_out = accepted;
+  return GFXB_OK;
+}
+
+}  // namespace
+
+extern "C" int gfxb_session_speculative_step(gfxb_session* session, std::uint32_t seed_token, unsigned draft_count,
+                                             std::uint32_t* tokens, unsigned* token_count, unsigned* accepted_out) {
+  if (session == nullptr || tokens == nullptr || token_count == nullptr || accepted_out == nullptr) {
+    return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  }
+  return speculative_round(*session, seed_token, draft_count, nullptr, tokens, token_count, accepted_out);
+}
+
+extern "C" int gfxb_session_speculative_step_with_drafts(gfxb_session* session, std::uint32_t seed_token,
+                                                         const std::uint32_t* drafts, unsigned draft_count,
+                                                         std::uint32_t* tokens, unsigned* token_count,
+                                                         unsigned* accepted_out) {
+  if (session == nullptr || drafts == nullptr || tokens == nullptr || token_count == nullptr ||
+      accepted_out == nullptr) {
+    return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  }
+  if (draft_count >= kMaxBlock || !valid_tokens(*session, drafts, draft_count)) {
+    return fail(GFXB_INVALID_ARGUMENT, "drafts must be 1..31 valid token ids");
+  }
+  return speculative_round(*session, seed_token, draft_count, drafts, tokens, token_count, accepted_out);
+}
+
+extern "C" int gfxb_session_prefill(gfxb_session* session, const std::uint32_t* tokens, std::size_t count,
+                                    std::uint32_t* next_token) {
+  if (session == nullptr || tokens == nullptr || next_token == nullptr) {
+    return fail(GFXB_INVALID_ARGUMENT, "null argument");
+  }
+  gfxb_session& s = *session;
+  if (count == 0 || count > s.cfg.maximum_context_tokens - s.host_position || !valid_tokens(s, tokens, static_cast<unsigned>(count))) {
+    return fail(GFXB_INVALID_ARGUMENT, "prompt must hold valid tokens within the context limit");
+  }
+  // causal blocks of up to 32 tokens; the LM head runs for the prompt's last token only
+  for (std::size_t done = 0; done < count;) {
+    const unsigned n = static_cast<unsigned>(std::min<std::size_t>(kMaxBlock, count - done));
+    const bool last = done + n == count;
+    GFXB_TRY(upload_step(s, tokens + done, n));
+    GFXB_TRY(enqueue_forward(s, n, s.tokens, s.position, false, last ? Head::last : Head::none));
+    if (!last) GFXB_TRY(cuda_check(cudaStreamSynchronize(s.stream), "prefill block failed"));
+    s.host_position += n;
+    done += n;
+  }
+  GFXB_TRY(download_tokens(s, s.selected, next_token, 1));
+  s.have_last_hidden = true;
+  s.mtp_chain_active = false;
   return GFXB_OK;
 }
 

@@ -1,5 +1,7 @@
 // C ABI wrappers of the decode-path operators (include/gfxb/gfxb.h), the
 // counterparts of the reference's qwen_ops.h launchers.
+#include <mutex>
+
 #include "common.cuh"
 #include "ops.cuh"
 
@@ -211,12 +213,9 @@ extern "C" int gfxb_argmax(const float* logits, const std::uint32_t* token_ids, 
 // holds it until the process exits.
 // ---------------------------------------------------------------------------
 
-#include <mutex>
-
 namespace {
 
 constexpr std::size_t kStaticAttentionScratchBytes = std::size_t{4} << 20;
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float g_static_attention_scratch[kStaticAttentionScratchBytes / sizeof(float)];
 
@@ -228,16 +227,11 @@ void* g_static_scratch_address[kMaxDevices] = {};
 // per device, with that device current, and cached.
 int static_scratch_address(void** address) {
   int device = 0;
-  cudaError_t error = cudaGetDevice(&device);
-  if (error != cudaSuccess) {
-    set_error_cuda(error, "cudaGetDevice failed");
-    return GFXB_CUDA_ERROR;
-  }
-  if (device < 0 || device >= kMaxDevices) return fail(GFXB_UNSUPPORTED, "device index beyond the static scratch table");
+  GFXB_TRY(current_device(&device));
   std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
   if (g_static_scratch_address[device] == nullptr) {
     void* pointer = nullptr;
-    error = cudaGetSymbolAddress(&pointer, g_static_attention_scratch);
+    const cudaError_t error = cudaGetSymbolAddress(&pointer, g_static_attention_scratch);
     if (error != cudaSuccess) {
       set_error_cuda(error, "cudaGetSymbolAddress of the static attention scratch failed");
       return GFXB_CUDA_ERROR;
@@ -256,6 +250,11 @@ extern "C" int gfxb_gated_attention_static_scratch(const std::uint16_t* query, c
                                                    const std::uint64_t* device_base_position, std::size_t capacity,
                                                    unsigned q_heads, unsigned kv_heads, unsigned batch,
                                                    void* stream) {
+  // the shape limits of launch_attention first, so that the size product below cannot wrap
+  if (batch == 0 || batch > 32 || kv_heads == 0 || q_heads == 0 || q_heads % kv_heads != 0 ||
+      q_heads / kv_heads > 8 || capacity == 0 || capacity > (std::size_t{1} << 32)) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid gated attention arguments");
+  }
   const std::size_t needed = attention_partial_bytes(q_heads, capacity, batch);
   if (needed > kStaticAttentionScratchBytes) {
     return fail(GFXB_INVALID_ARGUMENT,

@@ -7,8 +7,10 @@
 // oracle reproduce kernel outputs bit for bit.
 #pragma once
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 #include <utility>
 
 #include <cuda_fp16.h>
@@ -190,6 +192,42 @@ __device__ __forceinline__ void mma_s8_16832(int (&c)[4], const std::uint32_t (&
 }
 
 inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
+
+// ---- per-device set-up -------------------------------------------------------
+// cudaFuncSetAttribute and occupancy answers belong to the device that is
+// current when they are made, so launchers keep them per device. Thread-safe:
+// the first caller on a device runs the set-up under a lock, later callers
+// only read an atomic flag.
+
+constexpr int kMaxDevices = 64;
+
+// The current device, checked against kMaxDevices.
+int current_device(int* device);
+
+class DeviceOnce {
+ public:
+  // Runs configure(device) once for the current device; a failed set-up is
+  // retried by the next call.
+  template <typename Configure>
+  int run(Configure&& configure) {
+    int device = 0;
+    const int status = current_device(&device);
+    if (status != GFXB_OK) return status;
+    if (done_[device].load(std::memory_order_acquire) != 0) return GFXB_OK;
+    std::lock_guard<std::mutex> lock(mutex_);
+    if (done_[device].load(std::memory_order_relaxed) != 0) return GFXB_OK;
+    const int result = configure(device);
+    if (result == GFXB_OK) done_[device].store(1, std::memory_order_release);
+    return result;
+  }
+
+ private:
+  std::mutex mutex_;
+  std::atomic<std::uint8_t> done_[kMaxDevices] = {};
+};
+
+// The current device's SM count (queried once per device).
+int device_sm_count(int* sms);
 
 // ---- programmatic dependent launch -------------------------------------------
 // Every kernel of the decode chain lets its successor launch early

@@ -15,6 +15,8 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <map>
+#include <mutex>
 
 #include "codec.cuh"
 #include "common.cuh"
@@ -720,32 +722,38 @@ __global__ __launch_bounds__(256) void gemv_pipe_kernel(const GemvArgs args, std
 template <int Bits>
 int launch_pipe(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t stream) {
   const PipeLayout layout = pipe_layout(Bits, args.groups, args.batch);
-  static int configured = 0;
-  static int sms = 0;
-  static std::uint32_t cached_total = 0;  // occupancy for the last layout seen
-  static int cached_blocks = 0;
-  if (configured < static_cast<int>(layout.total)) {
-    cudaError_t error = cudaFuncSetAttribute(gemv_pipe_kernel<Bits>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             200 * 1024);
+  static DeviceOnce configured;
+  GFXB_TRY(configured.run([](int) {
+    const cudaError_t error = cudaFuncSetAttribute(gemv_pipe_kernel<Bits>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (error != cudaSuccess) {
       set_error_cuda(error, "pipelined GEMV shared-memory configuration failed");
-      return GFXB_CUDA_ERROR;
+      return static_cast<int>(GFXB_CUDA_ERROR);
     }
-    configured = 200 * 1024;
-  }
+    return static_cast<int>(GFXB_OK);
+  }));
+  int sms = 0;
+  GFXB_TRY(device_sm_count(&sms));
+  // resident CTAs per SM for each (device, shared-memory size) seen
+  static std::mutex occupancy_mutex;
+  static std::map<std::pair<int, std::uint32_t>, int> occupancy;
   int device = 0;
-  cudaGetDevice(&device);
-  if (sms == 0) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  if (cached_total != layout.total) {
-    int blocks = 0;
-    const cudaError_t error =
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, gemv_pipe_kernel<Bits>, 256, layout.total);
-    if (error != cudaSuccess || blocks < 1) {
-      set_error_cuda(error, "pipelined GEMV occupancy query failed");
-      return GFXB_CUDA_ERROR;
+  GFXB_TRY(current_device(&device));
+  int cached_blocks = 0;
+  {
+    std::lock_guard<std::mutex> lock(occupancy_mutex);
+    const auto found = occupancy.find({device, layout.total});
+    if (found != occupancy.end()) {
+      cached_blocks = found->second;
+    } else {
+      const cudaError_t error =
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&cached_blocks, gemv_pipe_kernel<Bits>, 256, layout.total);
+      if (error != cudaSuccess || cached_blocks < 1) {
+        set_error_cuda(error, "pipelined GEMV occupancy query failed");
+        return GFXB_CUDA_ERROR;
+      }
+      occupancy[{device, layout.total}] = cached_blocks;
     }
-    cached_total = layout.total;
-    cached_blocks = blocks;
   }
   const std::uint32_t grid = std::min<std::uint32_t>(total_tiles, static_cast<std::uint32_t>(sms * cached_blocks));
   const cudaError_t launch = launch_kernel(gemv_pipe_kernel<Bits>, dim3(grid), dim3(256), layout.total, stream, 0u,
@@ -794,8 +802,8 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
     // several tokens: the chain passes from rank to rank instead of gathering every dot in one CTA
     // (measured on B200: faster from 3 tokens on, and at 2 tokens for long K)
     const CascadeLayout layout = cascade_layout(Bits, args.groups, parts, args.batch, chunk);
-    static bool cascade_configured = false;
-    if (!cascade_configured) {
+    static DeviceOnce cascade_configured;
+    GFXB_TRY(cascade_configured.run([](int) {
       cudaError_t error = cudaFuncSetAttribute(gemv_cascade_kernel<Bits, 1>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
       if (error == cudaSuccess) {
@@ -804,10 +812,10 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
       }
       if (error != cudaSuccess) {
         set_error_cuda(error, "GEMV shared-memory configuration failed");
-        return GFXB_CUDA_ERROR;
+        return static_cast<int>(GFXB_CUDA_ERROR);
       }
-      cascade_configured = true;
-    }
+      return static_cast<int>(GFXB_OK);
+    }));
     if (layout.total > 200u * 1024u) return fail(GFXB_UNSUPPORTED, "GEMV shape exceeds shared memory");
     const cudaError_t error =
         args.batch > 8u ? launch_kernel(gemv_cascade_kernel<Bits, 2>, dim3(total_tiles * parts), dim3(256),
@@ -821,16 +829,16 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
     return GFXB_OK;
   }
   const StreamLayout layout = stream_layout(Bits, args.groups, parts, args.batch, chunk);
-  static int configured_bytes = 0;
-  if (static_cast<int>(layout.total) > configured_bytes) {
+  static DeviceOnce configured;
+  GFXB_TRY(configured.run([](int) {
     const cudaError_t error = cudaFuncSetAttribute(gemv_stream_kernel<Bits>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (error != cudaSuccess) {
       set_error_cuda(error, "GEMV shared-memory configuration failed");
-      return GFXB_CUDA_ERROR;
+      return static_cast<int>(GFXB_CUDA_ERROR);
     }
-    configured_bytes = 200 * 1024;
-  }
+    return static_cast<int>(GFXB_OK);
+  }));
   if (layout.total > 200u * 1024u) return fail(GFXB_UNSUPPORTED, "GEMV shape exceeds shared memory");
   cudaLaunchConfig_t config{};
   config.gridDim = dim3(total_tiles * parts);

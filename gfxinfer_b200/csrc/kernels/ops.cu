@@ -559,16 +559,16 @@ int launch_attention(const AttentionArgs& args, unsigned batch, cudaStream_t str
   const std::uint32_t max_chunks = args.device_base_position != nullptr
                                        ? args.max_chunks
                                        : static_cast<std::uint32_t>((args.base_token_count + batch - 1 + kChunk - 1) / kChunk);
-  static bool configured = false;
-  if (!configured) {
+  static DeviceOnce configured;
+  GFXB_TRY(configured.run([](int) {
     const cudaError_t error = cudaFuncSetAttribute(attention_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    static_cast<int>(kAttentionStageBytes));
     if (error != cudaSuccess) {
       set_error_cuda(error, "attention shared-memory configuration failed");
-      return GFXB_CUDA_ERROR;
+      return static_cast<int>(GFXB_CUDA_ERROR);
     }
-    configured = true;
-  }
+    return static_cast<int>(GFXB_OK);
+  }));
   launch_kernel(attention_chunk_kernel, dim3(dim3(max_chunks, args.kv_heads, batch)), dim3(256),
                 kAttentionStageBytes, stream, 0, args);
   int status = launch_status("attention chunk launch failed");

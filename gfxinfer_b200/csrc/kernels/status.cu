@@ -37,6 +37,33 @@ int launch_status(const char* context) {
   return error == cudaErrorMemoryAllocation ? GFXB_OUT_OF_MEMORY : GFXB_CUDA_ERROR;
 }
 
+int current_device(int* device) {
+  const cudaError_t error = cudaGetDevice(device);
+  if (error != cudaSuccess) {
+    set_error_cuda(error, "cudaGetDevice failed");
+    return GFXB_CUDA_ERROR;
+  }
+  if (*device < 0 || *device >= kMaxDevices) return fail(GFXB_UNSUPPORTED, "device index beyond the per-device tables");
+  return GFXB_OK;
+}
+
+int device_sm_count(int* sms) {
+  static std::atomic<int> counts[kMaxDevices] = {};
+  int device = 0;
+  GFXB_TRY(current_device(&device));
+  int count = counts[device].load(std::memory_order_relaxed);
+  if (count == 0) {
+    const cudaError_t error = cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
+    if (error != cudaSuccess || count <= 0) {
+      set_error_cuda(error, "SM count query failed");
+      return GFXB_CUDA_ERROR;
+    }
+    counts[device].store(count, std::memory_order_relaxed);
+  }
+  *sms = count;
+  return GFXB_OK;
+}
+
 }  // namespace gfxb
 
 extern "C" const char* gfxb_last_error_message(void) { return gfxb::g_last_error.c_str(); }

@@ -148,13 +148,31 @@ class QwenDecodeSession:
         check(lib().gfxb_session_mtp_draft(self._handle, next_token, ctypes.byref(out)))
         return out.value
 
-    def speculative_step(self, seed_token: int, draft_count: int) -> SpeculativeStepResult:
+    def speculative_step(self, seed_token: int, draft_count: int,
+                         drafts: list[int] | None = None) -> SpeculativeStepResult:
+        """One MTP speculative round; with `drafts`, the round verifies those tokens instead of the
+        MTP proposals (gfxb_session_speculative_step_with_drafts)."""
         out = (ctypes.c_uint32 * 32)()
         count = ctypes.c_uint()
         accepted = ctypes.c_uint()
-        check(lib().gfxb_session_speculative_step(self._handle, seed_token, draft_count, out, ctypes.byref(count),
-                                                  ctypes.byref(accepted)))
+        if drafts is None:
+            check(lib().gfxb_session_speculative_step(self._handle, seed_token, draft_count, out, ctypes.byref(count),
+                                                      ctypes.byref(accepted)))
+        else:
+            draft_count = len(drafts)
+            arr = (ctypes.c_uint32 * max(draft_count, 1))(*drafts)
+            check(lib().gfxb_session_speculative_step_with_drafts(self._handle, seed_token, arr, draft_count, out,
+                                                                  ctypes.byref(count), ctypes.byref(accepted)))
         return SpeculativeStepResult(list(out)[:count.value], draft_count, accepted.value)
+
+    def prefill(self, tokens: list[int]) -> int:
+        """Chunked prefill of a prompt (32-token causal blocks, LM head on the last token only);
+        returns the argmax after the prompt's last token."""
+        n = len(tokens)
+        arr = (ctypes.c_uint32 * max(n, 1))(*tokens)
+        out = ctypes.c_uint32()
+        check(lib().gfxb_session_prefill(self._handle, arr, n, ctypes.byref(out)))
+        return out.value
 
     def position(self) -> int:
         out = ctypes.c_uint64()

@@ -296,6 +296,25 @@ int gfxb_session_mtp_draft(gfxb_session* session, uint32_t next_token, uint32_t*
  * on the host as in the reference. */
 int gfxb_session_speculative_step(gfxb_session* session, uint32_t seed_token, unsigned draft_count,
                                   uint32_t* tokens, unsigned* token_count, unsigned* accepted_drafts);
+/* speculative_step verifying the caller's drafts instead of the MTP chain's
+ * proposals (no counterpart in the reference, whose drafts always come from
+ * its MTP layer): for callers with a drafter of their own (prompt lookup,
+ * n-gram tables, a separate draft model) and for tests that need rounds
+ * with full or partial acceptance. The MTP chain still runs, so the MTP
+ * cache stays aligned with the target as after a regular round. The round
+ * runs eagerly (never from the captured speculative graph). drafts: 1..31
+ * token ids. Acceptance, rollback and commit are those of
+ * gfxb_session_speculative_step. */
+int gfxb_session_speculative_step_with_drafts(gfxb_session* session, uint32_t seed_token, const uint32_t* drafts,
+                                              unsigned draft_count, uint32_t* tokens, unsigned* token_count,
+                                              unsigned* accepted_drafts);
+/* Chunked prefill, replacing the reference CLI's token-by-token prompt loop
+ * (src/cli/main.cpp:1056-1070): the prompt runs as causal blocks of up to 32
+ * tokens (the block_step forward, qwen_runtime.cpp:1320-1392) and the LM head
+ * runs only for its last token, whose argmax is written to next_token. The
+ * session state afterwards equals that after greedy_step over every prompt
+ * token. */
+int gfxb_session_prefill(gfxb_session* session, const uint32_t* tokens, size_t count, uint32_t* next_token);
 int gfxb_session_position(const gfxb_session* session, uint64_t* position);
 /* Device-resident decode: enqueue `steps` greedy steps on the session stream,
  * each step's argmax feeding the next, no host synchronisation. The host

@@ -896,14 +896,38 @@ uint32_t or_prompt_token(uint64_t seed, uint32_t vocab, uint32_t index) {
 }
 
 /* ======================================================================== */
-/* scalar forward (qwen_runtime.cpp:349-419, 715-867, 1264-1318)            */
+/* scalar forward (qwen_runtime.cpp:349-419, 715-867, 1264-1392)            */
+/*                                                                          */
+/* Tokens run in layer-major blocks of up to OR_BLOCK tokens, the order of  */
+/* the reference's causal block_step: every projection of a layer is       */
+/* applied to all of the block's tokens with one pass over the weights, the */
+/* recurrent and attention steps then run token by token. The arithmetic of */
+/* each token is the serial greedy step's, so a block gives the same bits   */
+/* as the same tokens stepped one at a time.                                */
 /* ======================================================================== */
 
+#define OR_BLOCK 64u
+
+/* A quantized matrix held packed so that the full-size models fit in host
+ * memory: 2 bits per code for W2 (the reference code c, q = 2c - 3) and a
+ * two's-complement nibble q for W3 and W4. Within each 128-column group,
+ * byte j holds columns (8/bits)*j + k at bit k*bits, k = 0 .. 8/bits - 1, so
+ * that the GEMV dots each bit plane against the matching activation plane. */
 typedef struct {
   size_t rows, columns;
-  int8_t* q;          /* logical signed codes [rows][columns] */
+  unsigned bits;      /* storage bits per code: 2 or 4 */
+  uint8_t* packed;    /* [rows][columns * bits / 8] */
   uint16_t* scales;   /* fp16 [rows][columns/128] */
 } or_matrix;
+
+static inline int matrix_code(const or_matrix* m, size_t row, size_t column) {
+  const unsigned per_byte = 8u / m->bits, group_bytes = GROUP / per_byte;
+  const size_t g = column / GROUP, c = column % GROUP;
+  const uint8_t byte = m->packed[row * (m->columns / per_byte) + g * group_bytes + c / per_byte];
+  const unsigned k = (unsigned)(c % per_byte);
+  if (m->bits == 2) return 2 * (int)((byte >> (2u * k)) & 3u) - 3;
+  return k == 0 ? (int)(int8_t)(uint8_t)(byte << 4) >> 4 : (int)(int8_t)byte >> 4;
+}
 
 typedef struct {
   int attention;
@@ -919,6 +943,7 @@ typedef struct {
 struct or_model {
   or_model_config cfg;
   int has_mtp;
+  unsigned resident_layers; /* layers with their own weights; layer i uses those of i % resident_layers */
   or_layer* layers;
   or_layer mtp;
   or_matrix embedding, lm_head, fc;
@@ -930,14 +955,19 @@ struct or_model {
   float *rope_cos, *rope_sin;
   size_t position, mtp_position;
   int mtp_chain_active;
-  /* activations */
+  /* activations, [OR_BLOCK][width] each */
   uint16_t *hidden, *next_hidden, *normalized, *post_attention, *post_normalized;
   uint16_t *conv_out, *mixer_out, *query, *key, *attn_out, *activated, *last_hidden, *mtp_hidden;
   uint16_t *mtp_concat, *mtp_input;
   float *proj_main, *proj_z, *proj_a, *proj_b, *proj_k, *proj_v, *update, *gate, *up, *logits;
-  int8_t* act_codes;
-  uint16_t* act_scales;
-  uint8_t* act_packed;
+  const float* last_logits;
+  int8_t* act_planes;    /* [OR_BLOCK][widest]: codes in bit-plane order */
+  int32_t* act_sums;     /* [OR_BLOCK][widest/128]: code sum per group */
+  uint16_t* act_scales;  /* [OR_BLOCK][widest/128] */
+  float* act_scale_values; /* [OR_BLOCK][widest/128]: the fp16 scales as floats */
+  int8_t* act_codes;     /* [widest] one token's codes */
+  uint8_t* act_packed;   /* [widest/2] */
+  size_t widest;
   double layer_seconds, head_seconds;
   size_t tokens;
 };
@@ -947,21 +977,153 @@ static void matrix_create(or_matrix* m, uint64_t seed, uint32_t tensor, size_t r
   const int format = format_of_bits(bits);
   m->rows = rows;
   m->columns = columns;
-  m->q = (int8_t*)malloc(rows * columns);
+  m->bits = format == OR_W2 ? 2u : 4u;
+  const unsigned per_byte = 8u / m->bits, group_bytes = GROUP / per_byte;
+  const size_t row_bytes = columns / per_byte;
+  m->packed = (uint8_t*)calloc(rows * row_bytes, 1);
   m->scales = (uint16_t*)malloc(rows * (columns / GROUP) * sizeof(uint16_t));
 #pragma omp parallel for schedule(static)
   for (long long r = 0; r < (long long)rows; ++r) {
+    uint8_t* row = m->packed + (size_t)r * row_bytes;
     for (size_t c = 0; c < columns; ++c) {
       const size_t index = (size_t)r * columns + c;
-      m->q[index] = (int8_t)or_decode_value(synthetic_code(seed, tensor, index, format), format);
+      const uint8_t code = synthetic_code(seed, tensor, index, format);
+      const int q = or_decode_value(code, format);
+      const size_t g = c / GROUP, within = c % GROUP;
+      const unsigned k = (unsigned)(within % per_byte);
+      const uint8_t stored = format == OR_W2 ? code : (uint8_t)(q & 15);
+      row[g * group_bytes + within / per_byte] |= (uint8_t)(stored << (k * m->bits));
     }
   }
   or_gen_scales(seed, tensor, rows * (columns / GROUP), format, m->scales);
 }
 
 static void matrix_free(or_matrix* m) {
-  free(m->q);
+  free(m->packed);
   free(m->scales);
+}
+
+/* Integer dot of one packed 128-group with one token's activation planes:
+ * sum over the group of q * a, exact in int32. Nibbles: q = (n ^ 8) - 8 with
+ * n ^ 8 in [0, 15]; W2: q = 2c - 3 with c in [0, 3]. The unsigned part runs
+ * on 8-bit multiply-adds (16-bit pair sums stay below 2^15) and the offset
+ * comes from the group's activation sum. */
+#if defined(__AVX2__)
+#include <immintrin.h>
+static inline int hsum_epi32(__m256i v) {
+  __m128i x = _mm_add_epi32(_mm256_castsi256_si128(v), _mm256_extracti128_si256(v, 1));
+  x = _mm_add_epi32(x, _mm_shuffle_epi32(x, 0x4e));
+  x = _mm_add_epi32(x, _mm_shuffle_epi32(x, 0xb1));
+  return _mm_cvtsi128_si32(x);
+}
+static inline int group_dot4(const uint8_t* w, const int8_t* p, int sum) {
+  const __m256i low = _mm256_set1_epi8(0x0f), eight = _mm256_set1_epi8(0x08);
+  const __m256i b0 = _mm256_loadu_si256((const __m256i*)w);
+  const __m256i b1 = _mm256_loadu_si256((const __m256i*)(w + 32));
+  const __m256i u0 = _mm256_xor_si256(_mm256_and_si256(b0, low), eight);
+  const __m256i u1 = _mm256_xor_si256(_mm256_and_si256(b1, low), eight);
+  const __m256i u2 = _mm256_xor_si256(_mm256_and_si256(_mm256_srli_epi16(b0, 4), low), eight);
+  const __m256i u3 = _mm256_xor_si256(_mm256_and_si256(_mm256_srli_epi16(b1, 4), low), eight);
+  __m256i d = _mm256_maddubs_epi16(u0, _mm256_loadu_si256((const __m256i*)p));
+  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(u1, _mm256_loadu_si256((const __m256i*)(p + 32))));
+  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(u2, _mm256_loadu_si256((const __m256i*)(p + 64))));
+  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(u3, _mm256_loadu_si256((const __m256i*)(p + 96))));
+  return hsum_epi32(_mm256_madd_epi16(d, _mm256_set1_epi16(1))) - 8 * sum;
+}
+static inline int group_dot2(const uint8_t* w, const int8_t* p, int sum) {
+  const __m256i three = _mm256_set1_epi8(0x03);
+  const __m256i b = _mm256_loadu_si256((const __m256i*)w);
+  __m256i d = _mm256_maddubs_epi16(_mm256_and_si256(b, three), _mm256_loadu_si256((const __m256i*)p));
+  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(_mm256_and_si256(_mm256_srli_epi16(b, 2), three),
+                                               _mm256_loadu_si256((const __m256i*)(p + 32))));
+  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(_mm256_and_si256(_mm256_srli_epi16(b, 4), three),
+                                               _mm256_loadu_si256((const __m256i*)(p + 64))));
+  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(_mm256_and_si256(_mm256_srli_epi16(b, 6), three),
+                                               _mm256_loadu_si256((const __m256i*)(p + 96))));
+  return 2 * hsum_epi32(_mm256_madd_epi16(d, _mm256_set1_epi16(1))) - 3 * sum;
+}
+#else
+static inline int group_dot4(const uint8_t* w, const int8_t* p, int sum) {
+  int dot = 0;
+  for (unsigned j = 0; j < 64; ++j) {
+    dot += (int)((w[j] & 15) ^ 8) * (int)p[j] + (int)(((w[j] >> 4) & 15) ^ 8) * (int)p[64 + j];
+  }
+  return dot - 8 * sum;
+}
+static inline int group_dot2(const uint8_t* w, const int8_t* p, int sum) {
+  int dot = 0;
+  for (unsigned j = 0; j < 32; ++j) {
+    for (unsigned k = 0; k < 4; ++k) dot += (int)((w[j] >> (2 * k)) & 3) * (int)p[32 * k + j];
+  }
+  return 2 * dot - 3 * sum;
+}
+#endif
+
+/* Quantizes `count` fp16 rows of width K (launch_matrix's activation step,
+ * qwen_runtime.cpp:78-148) into the model's plane/sum/scale buffers. */
+static void quantize_rows(or_model* m, const uint16_t* input, size_t K, unsigned count, unsigned bits_per_code) {
+  const unsigned per_byte = 8u / bits_per_code, group_bytes = GROUP / per_byte;
+  const size_t groups = K / GROUP;
+  for (unsigned t = 0; t < count; ++t) {
+    const uint16_t* x = input + (size_t)t * K;
+    uint16_t* scales = m->act_scales + (size_t)t * (m->widest / GROUP);
+    if (m->cfg.activation_bits == 8) {
+      or_quantize_activation_i8(x, K, 1, m->act_codes, scales);
+    } else {
+      or_quantize_activation_i4(x, K, 1, m->act_packed, scales);
+      or_unpack_a4(m->act_packed, K, m->act_codes);
+    }
+    int8_t* planes = m->act_planes + (size_t)t * m->widest;
+    int32_t* sums = m->act_sums + (size_t)t * (m->widest / GROUP);
+    float* scale_values = m->act_scale_values + (size_t)t * (m->widest / GROUP);
+    for (size_t g = 0; g < groups; ++g) {
+      scale_values[g] = or_f16_to_f32(scales[g]);
+      int sum = 0;
+      for (unsigned k = 0; k < per_byte; ++k) {
+        for (unsigned j = 0; j < group_bytes; ++j) {
+          const int8_t a = m->act_codes[g * GROUP + per_byte * j + k];
+          planes[g * GROUP + k * group_bytes + j] = a;
+          sum += a;
+        }
+      }
+      sums[g] = sum;
+    }
+  }
+}
+
+/* y[t][r] for the first `rows` rows and `count` tokens: per 128-group an exact
+ * int32 dot, then fp32 fma(dot, ws * as, acc) over the groups in ascending
+ * order (or_gemv_int's arithmetic, lowbit_gemv.hip:490-537). Quantizes the
+ * input first. */
+static void apply_block_rows(or_model* m, const or_matrix* w, size_t rows, const uint16_t* input,
+                             unsigned count, float* output) {
+  const size_t K = w->columns, groups = K / GROUP;
+  quantize_rows(m, input, K, count, w->bits);
+  const unsigned per_byte = 8u / w->bits, group_bytes = GROUP / per_byte;
+  const size_t row_bytes = K / per_byte, stride = m->widest, scale_stride = m->widest / GROUP;
+#pragma omp parallel for schedule(static)
+  for (long long r = 0; r < (long long)rows; ++r) {
+    const uint8_t* row = w->packed + (size_t)r * row_bytes;
+    float accumulator[OR_BLOCK];
+    for (unsigned t = 0; t < count; ++t) accumulator[t] = 0.0f;
+    for (size_t g = 0; g < groups; ++g) {
+      const uint8_t* b = row + g * group_bytes;
+      const float ws = or_f16_to_f32(w->scales[(size_t)r * groups + g]);
+      for (unsigned t = 0; t < count; ++t) {
+        const int8_t* p = m->act_planes + (size_t)t * stride + g * GROUP;
+        const int sum = m->act_sums[(size_t)t * scale_stride + g];
+        const int dot = w->bits == 4 ? group_dot4(b, p, sum) : group_dot2(b, p, sum);
+        const float product = ws * m->act_scale_values[(size_t)t * scale_stride + g];
+        accumulator[t] = fmaf((float)dot, product, accumulator[t]);
+      }
+    }
+    for (unsigned t = 0; t < count; ++t) output[(size_t)t * rows + (size_t)r] = accumulator[t];
+  }
+}
+
+static void apply_block(or_model* m, const or_matrix* w, const uint16_t* input, unsigned count,
+                        float* output) {
+  apply_block_rows(m, w, w->rows, input, count, output);
 }
 
 static uint16_t* bf16_create(uint64_t seed, uint32_t tensor, size_t count, float lo, float hi) {
@@ -970,8 +1132,7 @@ static uint16_t* bf16_create(uint64_t seed, uint32_t tensor, size_t count, float
   return values;
 }
 
-static void layer_create(or_model* m, or_layer* L, uint32_t layer_id, int attention,
-                         int mtp_layer) {
+static void layer_create(or_model* m, or_layer* L, uint32_t layer_id, int attention) {
   const or_model_config* c = &m->cfg;
   const uint64_t s = c->seed;
   L->attention = attention;
@@ -980,7 +1141,6 @@ static void layer_create(or_model* m, or_layer* L, uint32_t layer_id, int attent
   matrix_create(&L->gate, s, tensor_id(layer_id, K_GATE), c->intermediate, c->hidden, c->mlp_bits);
   matrix_create(&L->up, s, tensor_id(layer_id, K_UP), c->intermediate, c->hidden, c->mlp_bits);
   matrix_create(&L->down, s, tensor_id(layer_id, K_DOWN), c->hidden, c->intermediate, c->mlp_bits);
-  (void)mtp_layer;
   if (attention) {
     matrix_create(&L->q, s, tensor_id(layer_id, K_Q), (size_t)c->q_heads * 512, c->hidden, c->proj_bits);
     matrix_create(&L->k, s, tensor_id(layer_id, K_K), (size_t)c->kv_heads * 256, c->hidden, c->proj_bits);
@@ -1031,24 +1191,29 @@ static int is_attention_layer(const or_model_config* c, uint32_t layer) {
   return (layer + 1) % c->attention_interval == 0;
 }
 
-or_model* or_model_create(const or_model_config* config, int include_mtp) {
+static or_model* model_create(const or_model_config* config, int include_mtp, unsigned resident) {
   or_model* m = (or_model*)calloc(1, sizeof(or_model));
   m->cfg = *config;
   m->has_mtp = include_mtp;
   const or_model_config* c = &m->cfg;
   const uint64_t s = c->seed;
+  m->resident_layers = resident == 0 || resident > c->layers ? c->layers : resident;
   m->layers = (or_layer*)calloc(c->layers, sizeof(or_layer));
   unsigned gdn_count = 0, attention_count = 0;
   for (uint32_t i = 0; i < c->layers; ++i) {
     const int attention = is_attention_layer(c, i);
-    layer_create(m, &m->layers[i], i, attention, 0);
+    if (i < m->resident_layers) {
+      layer_create(m, &m->layers[i], i, attention);
+    } else {
+      m->layers[i] = m->layers[i % m->resident_layers];
+    }
     m->layers[i].state_index = attention ? attention_count++ : gdn_count++;
   }
   matrix_create(&m->embedding, s, tensor_id(LAYER_GLOBAL, G_EMBEDDING), c->vocab, c->hidden, c->emb_bits);
   matrix_create(&m->lm_head, s, tensor_id(LAYER_GLOBAL, G_LM_HEAD), c->vocab, c->hidden, c->head_bits);
   m->final_norm = bf16_create(s, tensor_id(LAYER_GLOBAL, G_FINAL_NORM), c->hidden, -0.1f, 0.1f);
   if (include_mtp) {
-    layer_create(m, &m->mtp, LAYER_MTP, 1, 1);
+    layer_create(m, &m->mtp, LAYER_MTP, 1);
     matrix_create(&m->fc, s, tensor_id(LAYER_MTP, K_FC), c->hidden, (size_t)2 * c->hidden, c->proj_bits);
     m->pre_emb_norm = bf16_create(s, tensor_id(LAYER_MTP, K_PRE_EMB_NORM), c->hidden, -0.1f, 0.1f);
     m->pre_hidden_norm = bf16_create(s, tensor_id(LAYER_MTP, K_PRE_HIDDEN_NORM), c->hidden, -0.1f, 0.1f);
@@ -1065,45 +1230,62 @@ or_model* or_model_create(const or_model_config* config, int include_mtp) {
   m->rope_cos = (float*)malloc((size_t)c->max_context * 32 * sizeof(float));
   m->rope_sin = (float*)malloc((size_t)c->max_context * 32 * sizeof(float));
   or_rope_table(c->max_context, 64, 10000000.0f, m->rope_cos, m->rope_sin);
-  const size_t H = c->hidden, I = c->intermediate;
+  const size_t H = c->hidden, I = c->intermediate, B = OR_BLOCK;
   size_t widest = I > channels ? I : channels;
   if ((size_t)c->q_heads * 512 > widest) widest = (size_t)c->q_heads * 512;
-  if (c->vocab > widest) widest = c->vocab;
   if (2 * H > widest) widest = 2 * H;
-  m->hidden = (uint16_t*)calloc(H, 2);
-  m->next_hidden = (uint16_t*)calloc(H, 2);
-  m->normalized = (uint16_t*)calloc(H, 2);
-  m->post_attention = (uint16_t*)calloc(H, 2);
-  m->post_normalized = (uint16_t*)calloc(H, 2);
+  m->widest = widest;
+  m->hidden = (uint16_t*)calloc(B * H, 2);
+  m->next_hidden = (uint16_t*)calloc(B * H, 2);
+  m->normalized = (uint16_t*)calloc(B * H, 2);
+  m->post_attention = (uint16_t*)calloc(B * H, 2);
+  m->post_normalized = (uint16_t*)calloc(B * H, 2);
   m->last_hidden = (uint16_t*)calloc(H, 2);
   m->mtp_hidden = (uint16_t*)calloc(H, 2);
   m->mtp_input = (uint16_t*)calloc(H, 2);
   m->mtp_concat = (uint16_t*)calloc(2 * H, 2);
-  m->conv_out = (uint16_t*)calloc(channels, 2);
-  m->mixer_out = (uint16_t*)calloc(widest, 2);
-  m->query = (uint16_t*)calloc((size_t)c->q_heads * 256, 2);
+  m->conv_out = (uint16_t*)calloc(B * channels, 2);
+  m->mixer_out = (uint16_t*)calloc(B * widest, 2);
+  m->query = (uint16_t*)calloc(B * c->q_heads * 256, 2);
   m->key = (uint16_t*)calloc(kv, 2);
-  m->attn_out = (uint16_t*)calloc((size_t)c->q_heads * 256, 2);
-  m->activated = (uint16_t*)calloc(I, 2);
-  m->proj_main = (float*)calloc(widest, 4);
-  m->proj_z = (float*)calloc((size_t)c->gdn_value_heads * 128, 4);
-  m->proj_a = (float*)calloc(c->gdn_value_heads, 4);
-  m->proj_b = (float*)calloc(c->gdn_value_heads, 4);
-  m->proj_k = (float*)calloc(kv, 4);
-  m->proj_v = (float*)calloc(kv, 4);
-  m->update = (float*)calloc(H, 4);
-  m->gate = (float*)calloc(I, 4);
-  m->up = (float*)calloc(I, 4);
-  m->logits = (float*)calloc(c->vocab, 4);
+  m->attn_out = (uint16_t*)calloc(B * c->q_heads * 256, 2);
+  m->activated = (uint16_t*)calloc(B * I, 2);
+  m->proj_main = (float*)calloc(B * widest, 4);
+  m->proj_z = (float*)calloc(B * c->gdn_value_heads * 128, 4);
+  m->proj_a = (float*)calloc(B * c->gdn_value_heads, 4);
+  m->proj_b = (float*)calloc(B * c->gdn_value_heads, 4);
+  m->proj_k = (float*)calloc(B * kv, 4);
+  m->proj_v = (float*)calloc(B * kv, 4);
+  m->update = (float*)calloc(B * H, 4);
+  m->gate = (float*)calloc(B * I, 4);
+  m->up = (float*)calloc(B * I, 4);
+  m->logits = (float*)calloc(B * (size_t)c->vocab, 4);
+  m->last_logits = m->logits;
+  m->act_planes = (int8_t*)calloc(B * widest, 1);
+  m->act_sums = (int32_t*)calloc(B * (widest / GROUP), 4);
+  m->act_scales = (uint16_t*)calloc(B * (widest / GROUP), 2);
+  m->act_scale_values = (float*)calloc(B * (widest / GROUP), 4);
   m->act_codes = (int8_t*)calloc(widest, 1);
-  m->act_scales = (uint16_t*)calloc(widest / GROUP + 1, 2);
   m->act_packed = (uint8_t*)calloc(widest / 2 + 1, 1);
   return m;
 }
 
+or_model* or_model_create(const or_model_config* config, int include_mtp) {
+  return model_create(config, include_mtp, 0);
+}
+
+/* CPU-baseline model: every layer runs (64 layer applications per token for
+ * config 2, each with its own recurrent state and KV cache), but only the
+ * first `resident_layers` layers hold weights of their own; layer i reuses
+ * those of layer i % resident_layers. The per-token work is the full
+ * model's; the host memory is that of `resident_layers` layers. */
+or_model* or_model_create_cycled(const or_model_config* config, unsigned resident_layers) {
+  return model_create(config, 0, resident_layers);
+}
+
 void or_model_destroy(or_model* m) {
   if (!m) return;
-  for (uint32_t i = 0; i < m->cfg.layers; ++i) layer_free(&m->layers[i]);
+  for (uint32_t i = 0; i < m->resident_layers; ++i) layer_free(&m->layers[i]);
   free(m->layers);
   matrix_free(&m->embedding);
   matrix_free(&m->lm_head);
@@ -1121,87 +1303,95 @@ void or_model_destroy(or_model* m) {
                      m->mtp_hidden, m->mtp_input, m->mtp_concat, m->conv_out, m->mixer_out,
                      m->query, m->key, m->attn_out, m->activated, m->proj_main, m->proj_z,
                      m->proj_a, m->proj_b, m->proj_k, m->proj_v, m->update, m->gate, m->up,
-                     m->logits, m->act_codes, m->act_scales, m->act_packed};
+                     m->logits, m->act_planes, m->act_sums, m->act_scales, m->act_scale_values, m->act_codes,
+                     m->act_packed};
   for (size_t i = 0; i < sizeof buffers / sizeof buffers[0]; ++i) free(buffers[i]);
   free(m);
-}
-
-/* Activation quantization + integer GEMV (launch_matrix, qwen_runtime.cpp:78-148). */
-static void apply_matrix(or_model* m, const or_matrix* w, const uint16_t* input, float* output) {
-  const size_t K = w->columns;
-  if (m->cfg.activation_bits == 8) {
-    or_quantize_activation_i8(input, K, 1, m->act_codes, m->act_scales);
-  } else {
-    or_quantize_activation_i4(input, K, 1, m->act_packed, m->act_scales);
-    or_unpack_a4(m->act_packed, K, m->act_codes);
-  }
-  or_gemv_int(w->q, w->scales, w->rows, K, m->act_codes, m->act_scales, 1, output);
 }
 
 static void embed(const or_model* m, uint32_t token, uint16_t* out) {
   const or_matrix* e = &m->embedding;
   const size_t groups = e->columns / GROUP;
   for (size_t c = 0; c < e->columns; ++c) {
-    out[c] = or_f32_to_f16((float)e->q[(size_t)token * e->columns + c] *
+    out[c] = or_f32_to_f16((float)matrix_code(e, token, c) *
                            or_f16_to_f32(e->scales[(size_t)token * groups + c / GROUP]));
   }
 }
 
+/* q/k/v, Q/K norm + RoPE, KV append, gated attention, o_proj for `count`
+ * tokens at positions base .. base + count - 1 (qwen_runtime.cpp:372-404). */
 static void attention_block(or_model* m, const or_layer* L, uint16_t* key_cache,
-                            uint16_t* value_cache, size_t position, int stop_after_append) {
+                            uint16_t* value_cache, size_t base, unsigned count) {
   const or_model_config* c = &m->cfg;
-  apply_matrix(m, &L->q, m->normalized, m->proj_main);
-  apply_matrix(m, &L->k, m->normalized, m->proj_k);
-  apply_matrix(m, &L->v, m->normalized, m->proj_v);
-  or_qk_norm_rope(m->proj_main, 512, L->q_norm, c->q_heads, position, m->rope_cos, m->rope_sin, 64, m->query);
-  or_qk_norm_rope(m->proj_k, 256, L->k_norm, c->kv_heads, position, m->rope_cos, m->rope_sin, 64, m->key);
-  const size_t kv = (size_t)c->kv_heads * 256;
-  for (size_t i = 0; i < kv; ++i) {
-    key_cache[position * kv + i] = m->key[i];
-    value_cache[position * kv + i] = or_f32_to_f16(m->proj_v[i]);
+  const size_t kv = (size_t)c->kv_heads * 256, qw = (size_t)c->q_heads * 512, qo = (size_t)c->q_heads * 256;
+  const size_t H = c->hidden;
+  apply_block(m, &L->q, m->normalized, count, m->proj_main);
+  apply_block(m, &L->k, m->normalized, count, m->proj_k);
+  apply_block(m, &L->v, m->normalized, count, m->proj_v);
+  for (unsigned t = 0; t < count; ++t) {
+    const size_t position = base + t;
+    or_qk_norm_rope(m->proj_main + t * qw, 512, L->q_norm, c->q_heads, position, m->rope_cos, m->rope_sin, 64,
+                    m->query + t * qo);
+    or_qk_norm_rope(m->proj_k + t * kv, 256, L->k_norm, c->kv_heads, position, m->rope_cos, m->rope_sin, 64,
+                    m->key);
+    for (size_t i = 0; i < kv; ++i) {
+      key_cache[position * kv + i] = m->key[i];
+      value_cache[position * kv + i] = or_f32_to_f16(m->proj_v[t * kv + i]);
+    }
   }
-  if (stop_after_append) return;
-  or_gated_attention(m->query, m->proj_main, key_cache, value_cache, position + 1, c->q_heads,
-                     c->kv_heads, m->attn_out);
-  apply_matrix(m, &L->out, m->attn_out, m->update);
+  for (unsigned t = 0; t < count; ++t) {
+    or_gated_attention(m->query + t * qo, m->proj_main + t * qw, key_cache, value_cache, base + t + 1,
+                       c->q_heads, c->kv_heads, m->attn_out + t * qo);
+  }
+  (void)H;
+  apply_block(m, &L->out, m->attn_out, count, m->update);
 }
 
-static void mlp_block(or_model* m, const or_layer* L) {
+static void mlp_block(or_model* m, const or_layer* L, unsigned count) {
   const or_model_config* c = &m->cfg;
-  apply_matrix(m, &L->gate, m->post_normalized, m->gate);
-  apply_matrix(m, &L->up, m->post_normalized, m->up);
-  or_silu_multiply_f16(m->gate, m->up, c->intermediate, m->activated);
-  apply_matrix(m, &L->down, m->activated, m->update);
+  const size_t I = c->intermediate;
+  apply_block(m, &L->gate, m->post_normalized, count, m->gate);
+  apply_block(m, &L->up, m->post_normalized, count, m->up);
+  for (unsigned t = 0; t < count; ++t) {
+    or_silu_multiply_f16(m->gate + t * I, m->up + t * I, I, m->activated + t * I);
+  }
+  apply_block(m, &L->down, m->activated, count, m->update);
 }
 
-/* qwen_runtime.cpp:349-419 */
+/* One decoder layer over `count` tokens (qwen_runtime.cpp:349-419); m->normalized
+ * holds the layer's normalized input, `input` the residual stream. */
 static void run_layer(or_model* m, const or_layer* L, const uint16_t* input, uint16_t* output,
-                      const uint16_t* next_norm) {
+                      const uint16_t* next_norm, unsigned count) {
   const or_model_config* c = &m->cfg;
   const float eps = 1.0e-6f;
+  const size_t H = c->hidden;
   if (L->attention) {
     const size_t stride = (size_t)c->max_context * c->kv_heads * 256;
     attention_block(m, L, m->key_caches + L->state_index * stride,
-                    m->value_caches + L->state_index * stride, m->position, 0);
+                    m->value_caches + L->state_index * stride, m->position, count);
   } else {
     const size_t channels = (size_t)2 * c->gdn_key_heads * 128 + (size_t)c->gdn_value_heads * 128;
-    apply_matrix(m, &L->qkv, m->normalized, m->proj_main);
-    apply_matrix(m, &L->z, m->normalized, m->proj_z);
-    apply_matrix(m, &L->a, m->normalized, m->proj_a);
-    apply_matrix(m, &L->b, m->normalized, m->proj_b);
+    apply_block(m, &L->qkv, m->normalized, count, m->proj_main);
+    apply_block(m, &L->z, m->normalized, count, m->proj_z);
+    apply_block(m, &L->a, m->normalized, count, m->proj_a);
+    apply_block(m, &L->b, m->normalized, count, m->proj_b);
     or_gdn_conv_update(m->proj_main, L->conv, m->conv_states + L->state_index * channels * 4,
-                       m->conv_out, NULL, channels, 1);
+                       m->conv_out, NULL, channels, count);
     or_gdn_recurrent(m->conv_out, m->proj_z, m->proj_a, m->proj_b, L->a_log, L->dt_bias,
                      L->gdn_norm,
                      m->gdn_states + (size_t)L->state_index * c->gdn_value_heads * 128 * 128,
-                     m->mixer_out, NULL, NULL, NULL, c->gdn_key_heads, c->gdn_value_heads, 1);
-    apply_matrix(m, &L->out, m->mixer_out, m->update);
+                     m->mixer_out, NULL, NULL, NULL, c->gdn_key_heads, c->gdn_value_heads, count);
+    apply_block(m, &L->out, m->mixer_out, count, m->update);
   }
-  or_residual_add_rms_norm(input, m->update, L->post_norm, c->hidden, eps, 1, m->post_attention,
-                           m->post_normalized);
-  mlp_block(m, L);
-  or_residual_add_rms_norm(m->post_attention, m->update, next_norm, c->hidden, eps, 1, output,
-                           m->normalized);
+  for (unsigned t = 0; t < count; ++t) {
+    or_residual_add_rms_norm(input + t * H, m->update + t * H, L->post_norm, H, eps, 1,
+                             m->post_attention + t * H, m->post_normalized + t * H);
+  }
+  mlp_block(m, L, count);
+  for (unsigned t = 0; t < count; ++t) {
+    or_residual_add_rms_norm(m->post_attention + t * H, m->update + t * H, next_norm, H, eps, 1,
+                             output + t * H, m->normalized + t * H);
+  }
 }
 
 static double now_seconds(void) {
@@ -1210,40 +1400,77 @@ static double now_seconds(void) {
   return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
 }
 
-/* qwen_runtime.cpp:1264-1318 (argmax over the full synthetic vocabulary). */
-int or_model_greedy_step(or_model* m, uint32_t token, uint32_t* next_token) {
+/* The causal forward of `count` <= OR_BLOCK tokens at the current position
+ * (qwen_runtime.cpp:1264-1392): heads = 0 skips the LM head (prefill), 1
+ * applies it to the last token only, 2 to every token. outputs receives the
+ * argmax tokens of the tokens whose head ran (argmax over the full synthetic
+ * vocabulary). */
+static void forward_block(or_model* m, const uint32_t* tokens, unsigned count, int heads, uint32_t* outputs) {
   const or_model_config* c = &m->cfg;
-  if (m->position >= c->max_context || token >= c->vocab) return 1;
+  const size_t H = c->hidden;
   const double t0 = now_seconds();
-  embed(m, token, m->hidden);
-  or_rms_norm(m->hidden, m->layers[0].input_norm, c->hidden, 1.0e-6f, 1, m->normalized);
+  for (unsigned t = 0; t < count; ++t) {
+    embed(m, tokens[t], m->hidden + t * H);
+    or_rms_norm(m->hidden + t * H, m->layers[0].input_norm, H, 1.0e-6f, 1, m->normalized + t * H);
+  }
   uint16_t* current = m->hidden;
   uint16_t* next = m->next_hidden;
   for (uint32_t i = 0; i < c->layers; ++i) {
     const uint16_t* next_norm = i + 1 < c->layers ? m->layers[i + 1].input_norm : m->final_norm;
-    run_layer(m, &m->layers[i], current, next, next_norm);
+    run_layer(m, &m->layers[i], current, next, next_norm, count);
     uint16_t* swap = current;
     current = next;
     next = swap;
   }
-  memcpy(m->last_hidden, current, c->hidden * sizeof(uint16_t));
-  if (current != m->hidden) memcpy(m->hidden, current, c->hidden * sizeof(uint16_t));
+  memcpy(m->last_hidden, current + (size_t)(count - 1) * H, H * sizeof(uint16_t));
+  if (current != m->hidden) memcpy(m->hidden, current, (size_t)count * H * sizeof(uint16_t));
   const double t1 = now_seconds();
-  apply_matrix(m, &m->lm_head, m->normalized, m->logits);
-  *next_token = or_argmax(m->logits, c->vocab);
+  if (heads == 2) {
+    apply_block(m, &m->lm_head, m->normalized, count, m->logits);
+    for (unsigned t = 0; t < count; ++t) outputs[t] = or_argmax(m->logits + (size_t)t * c->vocab, c->vocab);
+    m->last_logits = m->logits + (size_t)(count - 1) * c->vocab;
+  } else if (heads == 1) {
+    apply_block(m, &m->lm_head, m->normalized + (size_t)(count - 1) * H, 1, m->logits);
+    outputs[count - 1] = or_argmax(m->logits, c->vocab);
+    m->last_logits = m->logits;
+  }
   m->head_seconds += now_seconds() - t1;
   m->layer_seconds += t1 - t0;
-  m->tokens += 1;
-  m->position += 1;
+  m->tokens += count;
+  m->position += count;
   m->mtp_chain_active = 0;
+}
+
+static int valid_block(const or_model* m, const uint32_t* tokens, size_t count) {
+  if (count == 0 || m->position + count > m->cfg.max_context) return 0;
+  for (size_t i = 0; i < count; ++i) {
+    if (tokens[i] >= m->cfg.vocab) return 0;
+  }
+  return 1;
+}
+
+/* qwen_runtime.cpp:1264-1318. */
+int or_model_greedy_step(or_model* m, uint32_t token, uint32_t* next_token) {
+  if (!valid_block(m, &token, 1)) return 1;
+  forward_block(m, &token, 1, 1, next_token);
   return 0;
 }
 
-/* block_step evaluates the same per-token arithmetic causally (qwen_runtime.cpp:1320-1392). */
+/* qwen_runtime.cpp:1320-1392: the tokens' argmax outputs, one per token. */
 int or_model_block_step(or_model* m, const uint32_t* tokens, unsigned count, uint32_t* outputs) {
-  for (unsigned i = 0; i < count; ++i) {
-    const int status = or_model_greedy_step(m, tokens[i], &outputs[i]);
-    if (status) return status;
+  if (count > OR_BLOCK || !valid_block(m, tokens, count)) return 1;
+  forward_block(m, tokens, count, 2, outputs);
+  return 0;
+}
+
+/* A prompt of any length, in layer-major blocks of OR_BLOCK tokens, without
+ * the LM head (states, caches and the last hidden state as after stepping
+ * each token). */
+int or_model_prefill(or_model* m, const uint32_t* tokens, size_t count) {
+  if (!valid_block(m, tokens, count)) return 1;
+  for (size_t done = 0; done < count; done += OR_BLOCK) {
+    const unsigned n = (unsigned)(count - done < OR_BLOCK ? count - done : OR_BLOCK);
+    forward_block(m, tokens + done, n, 0, NULL);
   }
   return 0;
 }
@@ -1258,19 +1485,18 @@ int or_model_mtp_draft(or_model* m, uint32_t token, int use_mtp_hidden, uint32_t
   embed(m, token, emb);
   or_rms_norm(emb, m->pre_emb_norm, c->hidden, eps, 1, m->mtp_concat);
   or_rms_norm(conditioning, m->pre_hidden_norm, c->hidden, eps, 1, m->mtp_concat + c->hidden);
-  apply_matrix(m, &m->fc, m->mtp_concat, m->update);
+  apply_block(m, &m->fc, m->mtp_concat, 1, m->update);
   for (size_t i = 0; i < c->hidden; ++i) m->mtp_input[i] = or_f32_to_f16(m->update[i]);
   or_rms_norm(m->mtp_input, m->mtp.input_norm, c->hidden, eps, 1, m->normalized);
-  attention_block(m, &m->mtp, m->mtp_keys, m->mtp_values, m->mtp_position, 0);
+  attention_block(m, &m->mtp, m->mtp_keys, m->mtp_values, m->mtp_position, 1);
   or_residual_add_rms_norm(m->mtp_input, m->update, m->mtp.post_norm, c->hidden, eps, 1,
                            m->post_attention, m->post_normalized);
-  mlp_block(m, &m->mtp);
+  mlp_block(m, &m->mtp, 1);
   or_residual_add_rms_norm(m->post_attention, m->update, m->mtp_final_norm, c->hidden, eps, 1,
                            m->mtp_hidden, m->normalized);
   const size_t draft_rows = c->draft_vocab < c->vocab ? c->draft_vocab : c->vocab;
-  or_matrix head = m->lm_head;
-  head.rows = draft_rows;
-  apply_matrix(m, &head, m->normalized, m->logits);
+  apply_block_rows(m, &m->lm_head, draft_rows, m->normalized, 1, m->logits);
+  m->last_logits = m->logits;
   *draft = or_argmax(m->logits, draft_rows);
   m->mtp_position += 1;
   return 0;
@@ -1295,26 +1521,4 @@ int or_set_threads(int threads) {
 #endif
 }
 const uint16_t* or_model_last_hidden(const or_model* m) { return m->last_hidden; }
-const float* or_model_logits(const or_model* m) { return m->logits; }
-
-/* CPU-baseline timing: per-token seconds of `tokens` greedy steps through a model
- * built from the given layers; returns layer seconds per token scaled to the full
- * layer count of the config plus head seconds per token. */
-double or_time_layers(const or_model_config* config, unsigned gdn_layers,
-                      unsigned attention_layers, unsigned include_head, unsigned tokens) {
-  or_model_config sample = *config;
-  sample.layers = gdn_layers + attention_layers;
-  sample.attention_interval = gdn_layers + attention_layers;
-  if (attention_layers == 0) sample.attention_interval = sample.layers + 1;
-  or_model* m = or_model_create(&sample, 0);
-  uint32_t token = 1, next = 0;
-  for (unsigned t = 0; t < tokens; ++t) {
-    or_model_greedy_step(m, token, &next);
-    token = next;
-  }
-  const double layer_per_token = m->layer_seconds / (double)tokens;
-  const double head_per_token = m->head_seconds / (double)tokens;
-  or_model_destroy(m);
-  const double scale = (double)config->layers / (double)(gdn_layers + attention_layers);
-  return layer_per_token * scale + (include_head ? head_per_token : 0.0);
-}
+const float* or_model_logits(const or_model* m) { return m->last_logits; }

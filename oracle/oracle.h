@@ -112,10 +112,17 @@ typedef struct {
 
 typedef struct or_model or_model;
 or_model* or_model_create(const or_model_config* config, int include_mtp);
+/* Every layer runs, but only the first resident_layers hold their own weights
+ * (layer i reuses layer i % resident_layers): the full model's per-token
+ * work in the host memory of a few layers, for CPU-baseline timing. */
+or_model* or_model_create_cycled(const or_model_config* config, unsigned resident_layers);
 void or_model_destroy(or_model* model);
 int or_model_greedy_step(or_model* model, uint32_t token, uint32_t* next_token);
+/* block_step: count <= 64 tokens, layer-major, one argmax per token. */
 int or_model_block_step(or_model* model, const uint32_t* tokens, unsigned count,
                         uint32_t* outputs);
+/* Any number of prompt tokens without the LM head. */
+int or_model_prefill(or_model* model, const uint32_t* tokens, size_t count);
 int or_model_mtp_draft(or_model* model, uint32_t token, int use_mtp_hidden,
                        uint32_t* draft);
 size_t or_model_position(const or_model* model);
@@ -123,8 +130,6 @@ void or_model_timing(const or_model* model, double* layer_seconds, double* head_
 int or_set_threads(int threads);
 const uint16_t* or_model_last_hidden(const or_model* model);
 const float* or_model_logits(const or_model* model);
-double or_time_layers(const or_model_config* config, unsigned gdn_layers,
-                      unsigned attention_layers, unsigned include_head, unsigned tokens);
 uint32_t or_prompt_token(uint64_t seed, uint32_t vocab, uint32_t index);
 
 /* Synthetic weight generators (the engine's generator follows the same rules). */

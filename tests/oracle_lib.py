@@ -87,6 +87,9 @@ class Oracle:
             "or_gated_attention": (None, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_uint, c_uint, c_void_p]),
             "or_argmax": (c_uint32, [c_void_p, c_size_t]),
             "or_model_create": (c_void_p, [POINTER(ModelConfig), c_int]),
+            "or_model_create_cycled": (c_void_p, [POINTER(ModelConfig), c_uint]),
+            "or_model_block_step": (c_int, [c_void_p, c_void_p, c_uint, c_void_p]),
+            "or_model_prefill": (c_int, [c_void_p, c_void_p, c_size_t]),
             "or_model_destroy": (None, [c_void_p]),
             "or_model_greedy_step": (c_int, [c_void_p, c_uint32, POINTER(c_uint32)]),
             "or_model_mtp_draft": (c_int, [c_void_p, c_uint32, c_int, POINTER(c_uint32)]),
@@ -95,7 +98,6 @@ class Oracle:
             "or_set_threads": (c_int, [c_int]),
             "or_model_last_hidden": (c_void_p, [c_void_p]),
             "or_model_logits": (c_void_p, [c_void_p]),
-            "or_time_layers": (c_double, [POINTER(ModelConfig), c_uint, c_uint, c_uint, c_uint]),
             "or_prompt_token": (c_uint32, [c_uint64, c_uint32, c_uint32]),
             "or_gen_codes_rowmajor": (None, [c_uint64, c_uint32, c_size_t, c_size_t, c_int, c_void_p]),
             "or_gen_scales": (None, [c_uint64, c_uint32, c_size_t, c_int, c_void_p]),
@@ -256,15 +258,36 @@ class Reference:
 class OracleModel:
     """Scalar forward of the synthetic model (oracle.c or_model_*)."""
 
-    def __init__(self, oracle: Oracle, config: ModelConfig, include_mtp: bool = True) -> None:
+    def __init__(self, oracle: Oracle, config: ModelConfig, include_mtp: bool = True,
+                 resident_layers: int = 0) -> None:
+        """resident_layers > 0: every layer runs but only that many hold their own weights (timing only)."""
         self.oracle = oracle
         self.config = config
-        self.handle = c_void_p(oracle.lib.or_model_create(ctypes.byref(config), int(include_mtp)))
+        if resident_layers:
+            handle = oracle.lib.or_model_create_cycled(ctypes.byref(config), resident_layers)
+        else:
+            handle = oracle.lib.or_model_create(ctypes.byref(config), int(include_mtp))
+        self.handle = c_void_p(handle)
 
     def greedy_step(self, token: int) -> int:
         out = c_uint32()
         assert self.oracle.lib.or_model_greedy_step(self.handle, token, ctypes.byref(out)) == 0
         return out.value
+
+    def block_step(self, tokens) -> list[int]:
+        """Up to 64 tokens, layer-major; one argmax per token (same bits as stepping them one by one)."""
+        ids = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.zeros(len(ids), np.uint32)
+        assert self.oracle.lib.or_model_block_step(self.handle, _ptr(ids), len(ids), _ptr(out)) == 0
+        return [int(x) for x in out]
+
+    def prefill(self, tokens) -> None:
+        """A prompt of any length without the LM head."""
+        ids = np.ascontiguousarray(tokens, dtype=np.uint32)
+        assert self.oracle.lib.or_model_prefill(self.handle, _ptr(ids), len(ids)) == 0
+
+    def position(self) -> int:
+        return int(self.oracle.lib.or_model_position(self.handle))
 
     def mtp_draft(self, token: int, use_mtp_hidden: bool = False) -> int:
         out = c_uint32()

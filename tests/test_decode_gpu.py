@@ -139,6 +139,66 @@ def test_speculative_stream_equals_greedy(oracle, small_engine, depth, graph):
     assert spec.position() == serial.position()
 
 
+@pytest.mark.parametrize("graph", [False, True])
+def test_speculative_forced_acceptance(oracle, small_engine, graph):
+    """Rounds whose drafts come from the serial greedy stream, with the first wrong draft planted at
+    every position k = 0..D-1 and none at all: each round must accept exactly k (or all D) drafts,
+    emit the greedy stream, and leave states that later rounds and plain greedy steps continue
+    correctly. Covers the partial-acceptance replay (qwen_runtime.cpp:1497-1519) and the
+    full-acceptance state commit with the MTP cache advance (:1520-1534), which random MTP weights
+    never reach."""
+    from gfxinfer_b200 import session as gs
+
+    cfg = model_config(**SMALL_MODEL)
+    start = prompt_tokens(oracle, cfg.seed + 17, cfg.vocab, 1)[0]
+    serial = _session(small_engine)
+    reference = [serial.greedy_step(start)]
+    while len(reference) < 160:
+        reference.append(serial.greedy_step(reference[-1]))
+    depth = 4
+    spec = gs.QwenDecodeSession.create(small_engine, graph_verifier_batch=depth + 1 if graph else 0)
+    emitted = [spec.greedy_step(start)]
+    plan = [depth, 0, 1, 2, 3, depth, depth, 2, 0, depth, 3, 1]  # accepted drafts per round
+    for wanted in plan:
+        n = len(emitted)
+        drafts = reference[n:n + depth]
+        if wanted < depth:
+            drafts[wanted] = (drafts[wanted] + 1) % cfg.vocab  # the first wrong draft
+        result = spec.speculative_step(emitted[-1], depth, drafts=drafts)
+        assert result.accepted_drafts == wanted
+        assert result.tokens == reference[n:n + wanted + 1]
+        emitted.extend(result.tokens)
+        assert spec.position() == len(emitted)  # the start token and every emitted token but the newest
+    # regular MTP rounds and greedy steps continue from the committed / rolled-back states
+    while len(emitted) < 100:
+        emitted.extend(spec.speculative_step(emitted[-1], depth).tokens)
+    for _ in range(5):
+        emitted.append(spec.greedy_step(emitted[-1]))
+    assert emitted == reference[:len(emitted)]
+
+
+def test_prefill_equals_serial_greedy(oracle, small_engine):
+    """Chunked prefill (32-token causal blocks, LM head on the last token only) leaves the state and
+    the next token of greedy steps over every prompt token, for prompts that end inside, at and
+    after a block boundary."""
+    cfg = model_config(**SMALL_MODEL)
+    for length in (1, 31, 32, 33, 100):
+        prompt = prompt_tokens(oracle, cfg.seed + length, cfg.vocab, length)
+        serial = _session(small_engine)
+        want = _greedy_stream(serial.greedy_step, prompt, 20)
+        chunked = _session(small_engine)
+        token = chunked.prefill(prompt)
+        assert chunked.position() == length
+        got = []
+        for _ in range(20):
+            got.append(token)
+            token = chunked.greedy_step(token)
+        assert got == want, length
+        np.testing.assert_array_equal(chunked.read_state()[0], serial.read_state()[0])
+        serial.close()
+        chunked.close()
+
+
 def test_speculative_graph_with_other_depths_runs_eagerly(oracle, small_engine):
     """A session captured for 4 drafts still serves rounds of 2 drafts (eagerly), interleaved."""
     from gfxinfer_b200 import session as gs

@@ -212,6 +212,73 @@ def test_gated_attention_bit_exact(oracle, lib, base_count):
     np.testing.assert_array_equal(gpu_attention(lib, case, base_count, capacity), _oracle_attention(oracle, case, base_count))
 
 
+@pytest.mark.parametrize("base_count,batch", [(2047, 3), (2048, 3), (3968, 32), (4095, 2)])
+def test_gated_attention_long_context_bit_exact(oracle, lib, base_count, batch):
+    """Configs 3 and 4 (contexts 2048 and 4096): up to 32 chunks merged per head, and a 32-token
+    verifier block ending at the last cache slot."""
+    capacity = 4096
+    case = _attention_case(np.random.default_rng(base_count), capacity, batch=batch)
+    np.testing.assert_array_equal(gpu_attention(lib, case, base_count, capacity),
+                                  _oracle_attention(oracle, case, base_count))
+
+
+def test_gated_attention_device_position_long_context(oracle, lib):
+    """The graph-capture form (first position read from device memory, grid sized by the capacity)
+    at capacity 4096 equals the host-count form and the oracle."""
+    capacity, base_count = 4096, 3000
+    case = _attention_case(np.random.default_rng(77), capacity, batch=4)
+    query, gate, keys, values = case
+    scratch_bytes = lib.lib().gfxb_gated_attention_scratch_bytes(24, capacity, 4)
+    scratch = torch.empty(scratch_bytes, dtype=torch.uint8, device="cuda")
+    out = torch.empty((4, 24, 256), dtype=torch.int16, device="cuda")
+    position = _dev(np.array([base_count - 1], np.uint64))
+    lib.check(lib.lib().gfxb_gated_attention(_p(_dev(query)), _p(_dev(gate)), _p(_dev(keys)), _p(_dev(values)),
+                                             _p(out), 0, _p(position), capacity, 24, 4, 4, _p(scratch),
+                                             scratch_bytes, _stream()))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy().view(np.uint16), _oracle_attention(oracle, case, base_count))
+
+
+def _argmax_cases(vocab):
+    """Rows of logits with planted maxima; the lowest index among equal maxima must win
+    (qwen_ops.hip:782, 794-796). The kernel reads index i in block (i / 256) % 64, so ties are
+    planted across blocks, across the rounds of one block, and at the first and last index."""
+    rng = np.random.default_rng(3)
+    rows = []
+    base = rng.normal(0, 1, vocab).astype(np.float32)
+    r = base.copy(); r[[7, 300, 16391, vocab - 1]] = 9.0; rows.append(r)                # across blocks and rounds
+    r = base.copy(); r[[0, vocab - 1]] = 9.0; rows.append(r)                            # first and last
+    r = base.copy(); r[vocab - 1] = 9.0; rows.append(r)                                 # last alone
+    rows.append(np.zeros(vocab, np.float32))                                            # all equal
+    rows.append(np.full(vocab, -np.inf, np.float32))                                    # all -inf
+    r = base.copy(); r[::5] = np.nan; r[[1001, 99999]] = 9.0; r[0] = np.nan; rows.append(r)  # NaNs ignored
+    r = base.copy(); r[[16383, 16384]] = 9.0; rows.append(r)                            # block 63 vs block 0 round 2
+    r = base.copy(); r[[255, 256]] = 9.0; rows.append(r)                                # adjacent blocks
+    r = base.copy(); r[np.arange(64) * 256 + 17] = 9.0; rows.append(r)                  # one tie in every block
+    r = np.full(vocab, np.nan, np.float32); rows.append(r)                              # all NaN
+    return np.stack(rows)
+
+
+def test_argmax_ties_lowest_index_bit_exact(oracle, lib):
+    vocab, stride = 151936, 151936 + 64
+    logits = _argmax_cases(vocab)
+    batch = logits.shape[0]
+    padded = np.full((batch, stride), 100.0, np.float32)  # the row padding must never be read
+    padded[:, :vocab] = logits
+    scratch_bytes = lib.lib().gfxb_argmax_scratch_bytes(batch)
+    scratch = torch.empty(scratch_bytes, dtype=torch.uint8, device="cuda")
+    ids = np.arange(vocab, dtype=np.uint32)[::-1].copy()
+    for mapped in (False, True):
+        tokens = torch.zeros(batch, dtype=torch.int32, device="cuda")
+        lib.check(lib.lib().gfxb_argmax(_p(_dev(padded)), _p(_dev(ids)) if mapped else None, _p(tokens), vocab,
+                                        stride, batch, _p(scratch), scratch_bytes, _stream()))
+        torch.cuda.synchronize()
+        got = tokens.cpu().numpy().view(np.uint32)
+        want = np.array([oracle.lib.or_argmax(_ptr(_host(row)), vocab) for row in logits], np.uint32)
+        assert list(want[:8]) == [7, 0, vocab - 1, 0, 0, 1001, 16383, 255]
+        np.testing.assert_array_equal(got, ids[want] if mapped else want)
+
+
 def test_qk_norm_rope_and_kv_append_bit_exact(oracle, lib):
     rng = np.random.default_rng(9)
     q_heads, k_heads, batch, position, capacity = 24, 4, 3, 77, 128
