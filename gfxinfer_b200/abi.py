@@ -58,6 +58,16 @@ class TensorWrite(ctypes.Structure):
                 ("aux", c_void_p), ("aux_bytes", c_uint64), ("alignment", c_uint32)]
 
 
+class ConvertSource(ctypes.Structure):
+    _fields_ = [("name", c_char_p), ("dtype", ctypes.c_uint16), ("rank", ctypes.c_uint16),
+                ("dimensions", c_uint64 * 4), ("data", c_void_p), ("data_bytes", c_uint64)]
+
+
+class ConvertOptions(ctypes.Structure):
+    _fields_ = [(name, c_uint32) for name in (
+        "layout", "mlp_bits", "w3_start_layer", "w4_tail_layers", "head_bits", "layers", "chunk_rows")]
+
+
 class ArtifactLoadOptions(ctypes.Structure):
     _fields_ = [(name, c_uint32) for name in (
         "activation_bits", "max_context", "draft_vocab", "include_mtp", "verify_checksums")]
@@ -71,6 +81,13 @@ SIGNATURES: dict[str, tuple] = {
     "gfxb_repack_rowmajor_to_b200": (c_int, [c_int, P, P, c_size_t, c_size_t, P]),
     "gfxb_repack_gfx12_to_b200": (c_int, [c_int, P, P, c_size_t, c_size_t, P]),
     "gfxb_tile_scales": (c_int, [P, P, c_size_t, c_size_t, P]),
+    "gfxb_packed_row_bytes": (c_size_t, [c_int, c_size_t]),
+    "gfxb_quantize_group128": (c_int, [c_int, c_int, P, c_size_t, c_size_t, P, P, P]),
+    "gfxb_tile_group128_for_gfx12": (c_int, [c_int, P, P, c_size_t, c_size_t, P, P, P]),
+    "gfxb_dequantize_group128": (c_int, [c_int, P, P, c_size_t, c_size_t, P, P]),
+    "gfxb_dequantized_weight": (ctypes.c_float, [c_int, P, P, c_size_t, c_size_t, c_size_t, c_size_t]),
+    "gfxb_convert_scratch_bytes": (c_size_t, [c_int, c_size_t, c_size_t]),
+    "gfxb_convert_group128": (c_int, [c_int, c_int, P, c_size_t, c_size_t, c_int, P, P, P, c_size_t, P]),
     "gfxb_pack_activation": (c_int, [c_int, P, P, P, P, P, c_size_t, c_uint, P]),
     "gfxb_lowbit_gemv": (c_int, [c_int, POINTER(GemvMatrix), c_uint, P, P, P, c_size_t, c_uint, P]),
     "gfxb_quantize_activation_i4": (c_int, [P, P, P, c_size_t, c_uint, P]),
@@ -126,6 +143,8 @@ SIGNATURES: dict[str, tuple] = {
     "gfxb_artifact_tensor_at": (c_int, [P, c_size_t, POINTER(TensorView)]),
     "gfxb_artifact_find": (c_int, [P, c_char_p, POINTER(TensorView), POINTER(c_int)]),
     "gfxb_artifact_write": (c_int, [c_char_p, POINTER(ArtifactIdentity), POINTER(TensorWrite), c_size_t]),
+    "gfxb_convert_to_artifact": (c_int, [c_char_p, POINTER(ArtifactIdentity), POINTER(ConvertSource), c_size_t,
+                                         POINTER(ConvertOptions), c_int]),
     "gfxb_engine_create_from_artifact": (c_int, [c_char_p, POINTER(ArtifactLoadOptions), c_int, c_int, c_int, P,
                                                  POINTER(c_void_p)]),
     "gfxb_engine_config": (c_int, [P, POINTER(ModelConfig)]),

@@ -136,3 +136,36 @@ def write(path: str, identity: dict, tensors: list[TensorWrite]) -> None:
                                    data.ctypes.data if data.size else None, data.size,
                                    aux.ctypes.data if aux.size else None, aux.size, t.alignment)
     check(lib().gfxb_artifact_write(str(path).encode(), ctypes.byref(ident), items, len(tensors)))
+
+
+LAYOUT_B200, LAYOUT_GFX12 = 0, 1
+
+
+def convert(path: str, identity: dict, tensors: dict, layout: int = LAYOUT_B200, mlp_bits: int = 3,
+            w3_start_layer: int = 0, w4_tail_layers: int = 0, head_bits: int = 4, layers: int | None = None,
+            chunk_rows: int = 1024, device: int = 0) -> None:
+    """convert_qwen38 (converter.cpp) for in-memory weights: `tensors` maps reference tensor names to
+    float32 or bfloat16 arrays (numpy float32, or uint16 arrays holding bf16 bits). 2-D tensors are
+    quantized on `device` by choose_quantization's rules, the rest stored as bf16."""
+    ident = abi.ArtifactIdentity(*(identity[k].encode() for k in ("target_arch", "model_id", "weights_id", "recipe_id")))
+    if layers is None:
+        prefix = "model.language_model.layers."
+        ids = [int(n[len(prefix):].split(".")[0]) for n in tensors if n.startswith(prefix)]
+        layers = max(ids) + 1 if ids else 0
+    items = (abi.ConvertSource * len(tensors))()
+    keep = []
+    for i, (name, array) in enumerate(tensors.items()):
+        array = np.ascontiguousarray(array)
+        if array.dtype == np.float32:
+            dtype = DTYPE_F32
+        elif array.dtype == np.uint16:
+            dtype = DTYPE_BF16
+        else:
+            raise TypeError(f"{name}: weights must be float32 or bf16 bits (uint16)")
+        encoded = name.encode()
+        keep += [array, encoded]
+        dims = (ctypes.c_uint64 * 4)(*(list(array.shape) + [0] * (4 - array.ndim)))
+        items[i] = abi.ConvertSource(encoded, dtype, array.ndim, dims, array.ctypes.data, array.nbytes)
+    options = abi.ConvertOptions(layout, mlp_bits, w3_start_layer, w4_tail_layers, head_bits, layers, chunk_rows)
+    check(lib().gfxb_convert_to_artifact(str(path).encode(), ctypes.byref(ident), items, len(tensors),
+                                         ctypes.byref(options), device))

@@ -107,3 +107,60 @@ def gfx12_f16_gemm(fmt, tiled, tiled_scales, x_f16, rows, cols, batch):
     check(lib().gfxb_gfx12_f16_gemm(fmt, _p(tiled), _p(tiled_scales), _p(x_f16), _p(out), rows, cols, batch,
                                     _stream()))
     return out
+
+
+# ---- weight packing (the reference's src/quantization.cpp on the device) ------
+
+DTYPE_F32, DTYPE_BF16 = 5, 4
+LAYOUT_B200, LAYOUT_GFX12, LAYOUT_ROWMAJOR = 0, 1, 2
+
+
+def _dtype_code(weights: torch.Tensor) -> int:
+    if weights.dtype == torch.float32:
+        return DTYPE_F32
+    if weights.dtype == torch.bfloat16:
+        return DTYPE_BF16
+    raise TypeError("weights must be float32 or bfloat16")
+
+
+def packed_row_bytes(fmt: int, cols: int) -> int:
+    return int(lib().gfxb_packed_row_bytes(fmt, cols))
+
+
+def quantize_group128(fmt: int, weights: torch.Tensor):
+    """quantize_group128 (quantization.cpp:163-220): [N][K] fp32/bf16 -> (row-major codes, fp32 scales)."""
+    rows, cols = weights.shape
+    weights = weights.contiguous()
+    codes = torch.empty(rows * packed_row_bytes(fmt, cols), dtype=torch.uint8, device=weights.device)
+    scales = torch.empty((rows, cols // 128), dtype=torch.float32, device=weights.device)
+    check(lib().gfxb_quantize_group128(fmt, _dtype_code(weights), _p(weights), rows, cols, _p(codes), _p(scales),
+                                       _stream()))
+    return codes, scales
+
+
+def tile_group128_for_gfx12(fmt: int, codes: torch.Tensor, scales: torch.Tensor, rows: int, cols: int):
+    """tile_group128_for_gfx12 (quantization.cpp:253-318) on the device."""
+    tiled = torch.empty_like(codes)
+    tiled_scales = torch.empty_like(scales)
+    check(lib().gfxb_tile_group128_for_gfx12(fmt, _p(codes), _p(scales), rows, cols, _p(tiled), _p(tiled_scales),
+                                             _stream()))
+    return tiled, tiled_scales
+
+
+def dequantize_group128(fmt: int, codes: torch.Tensor, scales: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    out = torch.empty((rows, cols), dtype=torch.float32, device=codes.device)
+    check(lib().gfxb_dequantize_group128(fmt, _p(codes), _p(scales), rows, cols, _p(out), _stream()))
+    return out
+
+
+def convert_group128(fmt: int, weights: torch.Tensor, layout: int = LAYOUT_B200):
+    """write_quantized (converter.cpp:345-393) for one weight: codes in `layout` and fp16 scales."""
+    rows, cols = weights.shape
+    weights = weights.contiguous()
+    dev = weights.device
+    codes = torch.empty(rows * packed_row_bytes(fmt, cols), dtype=torch.uint8, device=dev)
+    scales = torch.empty(rows * (cols // 128), dtype=torch.float16, device=dev)
+    scratch = torch.empty(int(lib().gfxb_convert_scratch_bytes(fmt, rows, cols)), dtype=torch.uint8, device=dev)
+    check(lib().gfxb_convert_group128(fmt, _dtype_code(weights), _p(weights), rows, cols, layout, _p(codes),
+                                      _p(scales), _p(scratch), scratch.numel(), _stream()))
+    return codes, scales

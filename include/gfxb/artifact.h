@@ -106,6 +106,41 @@ int gfxb_artifact_find(const gfxb_artifact* artifact, const char* name, gfxb_ten
 int gfxb_artifact_write(const char* path, const gfxb_artifact_identity* identity, const gfxb_tensor_write* tensors,
                         size_t count);
 
+/* ---- conversion (the reference's converter, src/converter.cpp) ---------------- */
+
+/* One source tensor: fp32 or bf16 values in HOST memory, row-major. */
+typedef struct {
+  const char* name;      /* the reference tensor name (qwen38_spec.cpp:32-102) */
+  uint16_t dtype;        /* GFXB_DTYPE_F32 or GFXB_DTYPE_BF16 */
+  uint16_t rank;         /* 1..4 */
+  uint64_t dimensions[4];
+  const void* data;
+  uint64_t data_bytes;
+} gfxb_convert_source;
+
+typedef struct {
+  uint32_t layout;         /* GFXB_LAYOUT_B200 (recipe "b200-v1") or GFXB_LAYOUT_GFX12 (a "tiled-v" recipe) */
+  uint32_t mlp_bits;       /* Qwen38ConversionOptions::mlp_bits: 2, 3 or 4 */
+  uint32_t w3_start_layer; /* with mlp_bits 3, the MLPs of earlier layers are W2 */
+  uint32_t w4_tail_layers; /* the MLPs of the last w4_tail_layers decoder layers are W4 */
+  uint32_t head_bits;      /* lm_head.weight: 2, 3 or 4 */
+  uint32_t layers;         /* decoder layers of the model */
+  uint32_t chunk_rows;     /* rows converted per device step: a multiple of 16, at most 4096 */
+} gfxb_convert_options;
+
+/* convert_qwen38's plan and write (converter.cpp:98-119, 186-330, 345-393)
+ * for tensors already in memory (the safetensors reader is not part of this
+ * library): choose_quantization's rules pick W2/W3/W4 per 2-D tensor (N % 16
+ * == 0, K % 128 == 0), other tensors are stored as bf16 (fp32 rounded to
+ * nearest even); quantized tensors run through gfxb_convert_group128 on
+ * `device` in chunks of chunk_rows rows and are streamed to the file with
+ * fp16 scales. With GFXB_LAYOUT_B200 the embedding is stored row-major (the
+ * b200-v1 recipe). The recipe id in `identity` must name the layout, and a
+ * tiled recipe holding W3 tensors must name the sequential form ("w3seq"). */
+int gfxb_convert_to_artifact(const char* path, const gfxb_artifact_identity* identity,
+                             const gfxb_convert_source* sources, size_t count, const gfxb_convert_options* options,
+                             int device);
+
 /* ---- engine <-> artifact ---------------------------------------------------- */
 
 typedef struct {

@@ -73,6 +73,49 @@ int gfxb_repack_gfx12_to_b200(int format, const uint8_t* gfx12_codes, uint8_t* b
 int gfxb_tile_scales(const uint16_t* rowmajor_scales, uint16_t* tiled_scales, size_t rows,
                      size_t columns, void* stream);
 
+/* ---- weight packing (the reference's src/quantization.cpp on the device) ----
+ * Row-major packed codes ("PackedMatrix", quantization.h): W2 four codes per
+ * byte, W3 three 16-byte bit planes per 128-group, W4 two nibbles per byte;
+ * fp32 group scales [N][K/128]. Bit-identical to the reference's host code. */
+
+/* packed_row_bytes (quantization.cpp:154-161); 0 for an unknown format. Host. */
+size_t gfxb_packed_row_bytes(int format, size_t columns);
+/* quantize_group128 (quantization.cpp:163-220): fp32 or bf16 weights
+ * (input_dtype GFXB_DTYPE_F32 / GFXB_DTYPE_BF16 of artifact.h) [N][K] ->
+ * row-major codes (16-byte aligned) and fp32 scales, per 128-group the
+ * reference's choose_scale (amax / {3,4,8}, four least-squares refits with
+ * double sums in column order). Waits for the stream and returns
+ * GFXB_INVALID_ARGUMENT when a weight is not finite, as the reference does;
+ * allocates a 4-byte flag with cudaMallocAsync on the stream. */
+int gfxb_quantize_group128(int format, int input_dtype, const void* weights, size_t rows, size_t columns,
+                           uint8_t* codes, float* scales, void* stream);
+/* tile_group128_for_gfx12 (quantization.cpp:253-318): row-major codes and fp32
+ * scales -> the reference's gfx12 tiled codes (W3 as sequential 3-bit codes)
+ * and scales [N/16][K/128][16]. N % 16 == 0. */
+int gfxb_tile_group128_for_gfx12(int format, const uint8_t* codes, const float* scales, size_t rows, size_t columns,
+                                 uint8_t* tiled_codes, float* tiled_scales, void* stream);
+/* dequantize_group128 (quantization.cpp:237-251): fp32 [N][K] = level * scale. */
+int gfxb_dequantize_group128(int format, const uint8_t* codes, const float* scales, size_t rows, size_t columns,
+                             float* output, void* stream);
+/* dequantized_weight (quantization.cpp:222-235) over HOST buffers: NaN for an
+ * index outside the matrix or an invalid shape. */
+float gfxb_dequantized_weight(int format, const uint8_t* codes, const float* scales, size_t rows, size_t columns,
+                              size_t row, size_t column);
+
+/* Conversion of one weight for the engines (the converter's write_quantized,
+ * converter.cpp:345-393): fp32 or bf16 [N][K] -> quantize_group128 -> codes in
+ * `layout` and fp16 scales rounded to nearest even (__float2half):
+ *   GFXB_LAYOUT_B200:     b200 codes, scales [N/16][K/128][16] (recipe b200-v1)
+ *   GFXB_LAYOUT_GFX12:    gfx12 tiled codes, W3 sequential, scales [N/16][K/128][16]
+ *                         (the reference's tiled recipes)
+ *   GFXB_LAYOUT_ROWMAJOR: row-major codes, scales [N][K/128] (embeddings)
+ * scratch: gfxb_convert_scratch_bytes() bytes, 16-byte aligned. Waits for the
+ * stream (non-finite weights give GFXB_INVALID_ARGUMENT). */
+enum { GFXB_LAYOUT_B200 = 0, GFXB_LAYOUT_GFX12 = 1, GFXB_LAYOUT_ROWMAJOR = 2 };
+size_t gfxb_convert_scratch_bytes(int format, size_t rows, size_t columns);
+int gfxb_convert_group128(int format, int input_dtype, const void* weights, size_t rows, size_t columns, int layout,
+                          uint8_t* codes, uint16_t* scales, void* scratch, size_t scratch_bytes, void* stream);
+
 /* ---- activation packs --------------------------------------------------------
  * The B200 GEMVs read activations as a pack: int8 codes in mma-fragment order
  * [B][K] (within each 128-group the 32 bytes a lane feeds to the tensor core

@@ -577,7 +577,9 @@ void or_silu_multiply_f16(const float* gate, const float* up, size_t elements,
 void or_gdn_conv_update(const float* projected, const uint16_t* weight, uint16_t* state,
                         uint16_t* output, uint16_t* appended_log, size_t channels,
                         unsigned batch) {
-  for (size_t c = 0; c < channels; ++c) {
+#pragma omp parallel for schedule(static)
+  for (long long cc = 0; cc < (long long)channels; ++cc) {
+    const size_t c = (size_t)cc;
     uint16_t taps[4];
     memcpy(taps, state + c * 4, sizeof taps);
     for (unsigned t = 0; t < batch; ++t) {
@@ -615,7 +617,9 @@ void or_gdn_recurrent(const uint16_t* qkv, const float* z, const float* a, const
   const unsigned value_elements = value_heads * head;
   const unsigned channels = 2 * key_elements + value_elements;
   const unsigned ratio = value_heads / key_heads;
-  for (unsigned vh = 0; vh < value_heads; ++vh) {
+#pragma omp parallel for schedule(static)
+  for (int vhh = 0; vhh < (int)value_heads; ++vhh) {
+    const unsigned vh = (unsigned)vhh;
     const unsigned kh = vh / ratio;
     float* S = state + (size_t)vh * head * head;
     for (unsigned t = 0; t < batch; ++t) {
@@ -761,7 +765,9 @@ void or_gated_attention(const uint16_t* query, const float* gate_projection,
   const unsigned head = 256;
   const unsigned group = q_heads / kv_heads;
   const size_t chunks = (token_count + OR_ATTN_CHUNK - 1) / OR_ATTN_CHUNK;
-  for (unsigned h = 0; h < q_heads; ++h) {
+#pragma omp parallel for schedule(static)
+  for (int hh = 0; hh < (int)q_heads; ++hh) {
+    const unsigned h = (unsigned)hh;
     const unsigned kvh = h / group;
     float q[256];
     for (unsigned d = 0; d < head; ++d) q[d] = or_f16_to_f32(query[h * head + d]);
@@ -965,8 +971,8 @@ struct or_model {
   int32_t* act_sums;     /* [OR_BLOCK][widest/128]: code sum per group */
   uint16_t* act_scales;  /* [OR_BLOCK][widest/128] */
   float* act_scale_values; /* [OR_BLOCK][widest/128]: the fp16 scales as floats */
-  int8_t* act_codes;     /* [widest] one token's codes */
-  uint8_t* act_packed;   /* [widest/2] */
+  int8_t* act_codes;     /* [OR_BLOCK][widest] codes in column order */
+  uint8_t* act_packed;   /* [OR_BLOCK][widest/2] */
   size_t widest;
   double layer_seconds, head_seconds;
   size_t tokens;
@@ -1016,47 +1022,40 @@ static inline int hsum_epi32(__m256i v) {
   x = _mm_add_epi32(x, _mm_shuffle_epi32(x, 0xb1));
   return _mm_cvtsi128_si32(x);
 }
-static inline int group_dot4(const uint8_t* w, const int8_t* p, int sum) {
+/* The unsigned parts of one packed group, four 32-byte planes. */
+typedef struct {
+  __m256i u[4];
+} group_planes;
+static inline group_planes unpack4(const uint8_t* w) {
   const __m256i low = _mm256_set1_epi8(0x0f), eight = _mm256_set1_epi8(0x08);
   const __m256i b0 = _mm256_loadu_si256((const __m256i*)w);
   const __m256i b1 = _mm256_loadu_si256((const __m256i*)(w + 32));
-  const __m256i u0 = _mm256_xor_si256(_mm256_and_si256(b0, low), eight);
-  const __m256i u1 = _mm256_xor_si256(_mm256_and_si256(b1, low), eight);
-  const __m256i u2 = _mm256_xor_si256(_mm256_and_si256(_mm256_srli_epi16(b0, 4), low), eight);
-  const __m256i u3 = _mm256_xor_si256(_mm256_and_si256(_mm256_srli_epi16(b1, 4), low), eight);
-  __m256i d = _mm256_maddubs_epi16(u0, _mm256_loadu_si256((const __m256i*)p));
-  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(u1, _mm256_loadu_si256((const __m256i*)(p + 32))));
-  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(u2, _mm256_loadu_si256((const __m256i*)(p + 64))));
-  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(u3, _mm256_loadu_si256((const __m256i*)(p + 96))));
-  return hsum_epi32(_mm256_madd_epi16(d, _mm256_set1_epi16(1))) - 8 * sum;
+  group_planes g;
+  g.u[0] = _mm256_xor_si256(_mm256_and_si256(b0, low), eight);
+  g.u[1] = _mm256_xor_si256(_mm256_and_si256(b1, low), eight);
+  g.u[2] = _mm256_xor_si256(_mm256_and_si256(_mm256_srli_epi16(b0, 4), low), eight);
+  g.u[3] = _mm256_xor_si256(_mm256_and_si256(_mm256_srli_epi16(b1, 4), low), eight);
+  return g;
 }
-static inline int group_dot2(const uint8_t* w, const int8_t* p, int sum) {
+static inline group_planes unpack2(const uint8_t* w) {
   const __m256i three = _mm256_set1_epi8(0x03);
   const __m256i b = _mm256_loadu_si256((const __m256i*)w);
-  __m256i d = _mm256_maddubs_epi16(_mm256_and_si256(b, three), _mm256_loadu_si256((const __m256i*)p));
-  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(_mm256_and_si256(_mm256_srli_epi16(b, 2), three),
-                                               _mm256_loadu_si256((const __m256i*)(p + 32))));
-  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(_mm256_and_si256(_mm256_srli_epi16(b, 4), three),
-                                               _mm256_loadu_si256((const __m256i*)(p + 64))));
-  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(_mm256_and_si256(_mm256_srli_epi16(b, 6), three),
-                                               _mm256_loadu_si256((const __m256i*)(p + 96))));
-  return 2 * hsum_epi32(_mm256_madd_epi16(d, _mm256_set1_epi16(1))) - 3 * sum;
+  group_planes g;
+  g.u[0] = _mm256_and_si256(b, three);
+  g.u[1] = _mm256_and_si256(_mm256_srli_epi16(b, 2), three);
+  g.u[2] = _mm256_and_si256(_mm256_srli_epi16(b, 4), three);
+  g.u[3] = _mm256_and_si256(_mm256_srli_epi16(b, 6), three);
+  return g;
 }
-#else
-static inline int group_dot4(const uint8_t* w, const int8_t* p, int sum) {
-  int dot = 0;
-  for (unsigned j = 0; j < 64; ++j) {
-    dot += (int)((w[j] & 15) ^ 8) * (int)p[j] + (int)(((w[j] >> 4) & 15) ^ 8) * (int)p[64 + j];
-  }
-  return dot - 8 * sum;
+/* sum over the group of u * a (the unsigned weight parts times the activation planes) */
+static inline int planes_dot(const group_planes* g, const int8_t* p) {
+  __m256i d = _mm256_maddubs_epi16(g->u[0], _mm256_loadu_si256((const __m256i*)p));
+  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(g->u[1], _mm256_loadu_si256((const __m256i*)(p + 32))));
+  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(g->u[2], _mm256_loadu_si256((const __m256i*)(p + 64))));
+  d = _mm256_add_epi16(d, _mm256_maddubs_epi16(g->u[3], _mm256_loadu_si256((const __m256i*)(p + 96))));
+  return hsum_epi32(_mm256_madd_epi16(d, _mm256_set1_epi16(1)));
 }
-static inline int group_dot2(const uint8_t* w, const int8_t* p, int sum) {
-  int dot = 0;
-  for (unsigned j = 0; j < 32; ++j) {
-    for (unsigned k = 0; k < 4; ++k) dot += (int)((w[j] >> (2 * k)) & 3) * (int)p[32 * k + j];
-  }
-  return 2 * dot - 3 * sum;
-}
+#define OR_SIMD 1
 #endif
 
 /* Quantizes `count` fp16 rows of width K (launch_matrix's activation step,
@@ -1064,14 +1063,18 @@ static inline int group_dot2(const uint8_t* w, const int8_t* p, int sum) {
 static void quantize_rows(or_model* m, const uint16_t* input, size_t K, unsigned count, unsigned bits_per_code) {
   const unsigned per_byte = 8u / bits_per_code, group_bytes = GROUP / per_byte;
   const size_t groups = K / GROUP;
-  for (unsigned t = 0; t < count; ++t) {
+#pragma omp parallel for schedule(static)
+  for (int tt = 0; tt < (int)count; ++tt) {
+    const unsigned t = (unsigned)tt;
     const uint16_t* x = input + (size_t)t * K;
     uint16_t* scales = m->act_scales + (size_t)t * (m->widest / GROUP);
+    int8_t* codes = m->act_codes + (size_t)t * m->widest;
     if (m->cfg.activation_bits == 8) {
-      or_quantize_activation_i8(x, K, 1, m->act_codes, scales);
+      or_quantize_activation_i8(x, K, 1, codes, scales);
     } else {
-      or_quantize_activation_i4(x, K, 1, m->act_packed, scales);
-      or_unpack_a4(m->act_packed, K, m->act_codes);
+      uint8_t* packed = m->act_packed + (size_t)t * (m->widest / 2 + 1);
+      or_quantize_activation_i4(x, K, 1, packed, scales);
+      or_unpack_a4(packed, K, codes);
     }
     int8_t* planes = m->act_planes + (size_t)t * m->widest;
     int32_t* sums = m->act_sums + (size_t)t * (m->widest / GROUP);
@@ -1081,7 +1084,7 @@ static void quantize_rows(or_model* m, const uint16_t* input, size_t K, unsigned
       int sum = 0;
       for (unsigned k = 0; k < per_byte; ++k) {
         for (unsigned j = 0; j < group_bytes; ++j) {
-          const int8_t a = m->act_codes[g * GROUP + per_byte * j + k];
+          const int8_t a = codes[g * GROUP + per_byte * j + k];
           planes[g * GROUP + k * group_bytes + j] = a;
           sum += a;
         }
@@ -1109,13 +1112,35 @@ static void apply_block_rows(or_model* m, const or_matrix* w, size_t rows, const
     for (size_t g = 0; g < groups; ++g) {
       const uint8_t* b = row + g * group_bytes;
       const float ws = or_f16_to_f32(w->scales[(size_t)r * groups + g]);
+#if defined(OR_SIMD)
+      /* nibbles: q = (n ^ 8) - 8; W2: q = 2c - 3 (the unsigned parts run on 8-bit multiply-adds,
+       * 16-bit pair sums stay below 2^15, the offset comes from the group's activation sum) */
+      const group_planes planes = w->bits == 4 ? unpack4(b) : unpack2(b);
       for (unsigned t = 0; t < count; ++t) {
         const int8_t* p = m->act_planes + (size_t)t * stride + g * GROUP;
         const int sum = m->act_sums[(size_t)t * scale_stride + g];
-        const int dot = w->bits == 4 ? group_dot4(b, p, sum) : group_dot2(b, p, sum);
+        const int u = planes_dot(&planes, p);
+        const int dot = w->bits == 4 ? u - 8 * sum : 2 * u - 3 * sum;
         const float product = ws * m->act_scale_values[(size_t)t * scale_stride + g];
         accumulator[t] = fmaf((float)dot, product, accumulator[t]);
       }
+#else
+      for (unsigned t = 0; t < count; ++t) {
+        const int8_t* p = m->act_planes + (size_t)t * stride + g * GROUP;
+        int dot = 0;
+        if (w->bits == 4) {
+          for (unsigned j = 0; j < 64; ++j) {
+            dot += ((int)(int8_t)(uint8_t)(b[j] << 4) >> 4) * (int)p[j] + ((int)(int8_t)b[j] >> 4) * (int)p[64 + j];
+          }
+        } else {
+          for (unsigned j = 0; j < 32; ++j) {
+            for (unsigned k = 0; k < 4; ++k) dot += (2 * (int)((b[j] >> (2 * k)) & 3) - 3) * (int)p[32 * k + j];
+          }
+        }
+        const float product = ws * m->act_scale_values[(size_t)t * scale_stride + g];
+        accumulator[t] = fmaf((float)dot, product, accumulator[t]);
+      }
+#endif
     }
     for (unsigned t = 0; t < count; ++t) output[(size_t)t * rows + (size_t)r] = accumulator[t];
   }
@@ -1265,8 +1290,8 @@ static or_model* model_create(const or_model_config* config, int include_mtp, un
   m->act_sums = (int32_t*)calloc(B * (widest / GROUP), 4);
   m->act_scales = (uint16_t*)calloc(B * (widest / GROUP), 2);
   m->act_scale_values = (float*)calloc(B * (widest / GROUP), 4);
-  m->act_codes = (int8_t*)calloc(widest, 1);
-  m->act_packed = (uint8_t*)calloc(widest / 2 + 1, 1);
+  m->act_codes = (int8_t*)calloc(B * widest, 1);
+  m->act_packed = (uint8_t*)calloc(B * (widest / 2 + 1), 1);
   return m;
 }
 
@@ -1352,7 +1377,8 @@ static void mlp_block(or_model* m, const or_layer* L, unsigned count) {
   const size_t I = c->intermediate;
   apply_block(m, &L->gate, m->post_normalized, count, m->gate);
   apply_block(m, &L->up, m->post_normalized, count, m->up);
-  for (unsigned t = 0; t < count; ++t) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < (int)count; ++t) {
     or_silu_multiply_f16(m->gate + t * I, m->up + t * I, I, m->activated + t * I);
   }
   apply_block(m, &L->down, m->activated, count, m->update);
@@ -1383,12 +1409,14 @@ static void run_layer(or_model* m, const or_layer* L, const uint16_t* input, uin
                      m->mixer_out, NULL, NULL, NULL, c->gdn_key_heads, c->gdn_value_heads, count);
     apply_block(m, &L->out, m->mixer_out, count, m->update);
   }
-  for (unsigned t = 0; t < count; ++t) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < (int)count; ++t) {
     or_residual_add_rms_norm(input + t * H, m->update + t * H, L->post_norm, H, eps, 1,
                              m->post_attention + t * H, m->post_normalized + t * H);
   }
   mlp_block(m, L, count);
-  for (unsigned t = 0; t < count; ++t) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < (int)count; ++t) {
     or_residual_add_rms_norm(m->post_attention + t * H, m->update + t * H, next_norm, H, eps, 1,
                              output + t * H, m->normalized + t * H);
   }
@@ -1409,7 +1437,8 @@ static void forward_block(or_model* m, const uint32_t* tokens, unsigned count, i
   const or_model_config* c = &m->cfg;
   const size_t H = c->hidden;
   const double t0 = now_seconds();
-  for (unsigned t = 0; t < count; ++t) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < (int)count; ++t) {
     embed(m, tokens[t], m->hidden + t * H);
     or_rms_norm(m->hidden + t * H, m->layers[0].input_norm, H, 1.0e-6f, 1, m->normalized + t * H);
   }
