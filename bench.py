@@ -313,7 +313,7 @@ def measure_config4(gs, np, torch, world: int, rank: int, local: int, nccl_id, s
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one W3A4 MLP gate+up launch, from the ncu
 # capture summarised in profiles/gemv_pipe_w3_gate_up_config2_ncu.md.
-GATE_UP_DRAM_BYTES = None
+GATE_UP_DRAM_BYTES = 69711872
 
 
 def measure_config0(peak: float) -> dict:

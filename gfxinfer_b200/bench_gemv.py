@@ -1,7 +1,7 @@
 """bench-gemv: time one low-bit GEMV launch on B200 (the reference's `gfxinfer bench-gemv`).
 
     python -m gfxinfer_b200.bench_gemv --format w3 --rows 17408 --columns 5120 --batch 1 \
-        [--activation a4|a8] [--iterations 60] [--copies 6] [--no-graph]
+        [--activation a4|a8] [--iterations 60] [--copies 6] [--matrices 1..4] [--no-graph]
 
 Mirrors src/cli/main.cpp:1529-1700: seeded random code bytes, fp16 scales drawn
 U(0.002, 0.08), activations U(-2, 2) rounded to fp16; timed launches; a sampled
@@ -11,6 +11,8 @@ reference's packed-code GB/s and the full algorithmic GB/s (codes + fp16
 scales + activation + fp32 outputs). Launches rotate over `copies` weight
 buffers so every launch reads HBM, and are replayed from a CUDA graph unless
 --no-graph (host launch overhead would otherwise dominate small shapes).
+--matrices M runs M matrices of the shape sharing one input in one launch
+(the MLP gate+up launch is --matrices 2 of [17408 x 5120]).
 """
 from __future__ import annotations
 
@@ -44,7 +46,7 @@ def _decode_rowmajor(codes_row: np.ndarray, bits: int, columns: int) -> np.ndarr
 
 
 def run(fmt: str, rows: int, columns: int, batch: int, activation: str, iterations: int, copies: int,
-        graph: bool, seed: int = 0x1200) -> dict:
+        graph: bool, seed: int = 0x1200, matrices: int = 1) -> dict:
     bits = FORMATS[fmt]
     fmt_id = BITS_TO_FORMAT[bits]
     ops.require_sm100(0)
@@ -52,7 +54,7 @@ def run(fmt: str, rows: int, columns: int, batch: int, activation: str, iteratio
     row_bytes = columns * bits // 8
     groups = columns // 128
     weights, scales, host = [], [], None
-    for i in range(copies):
+    for i in range(copies * matrices):
         codes = rng.integers(0, 256, size=rows * row_bytes, dtype=np.uint8)
         scale16 = rng.uniform(0.002, 0.08, size=rows * groups).astype(np.float16)
         if i == 0:
@@ -63,11 +65,13 @@ def run(fmt: str, rows: int, columns: int, batch: int, activation: str, iteratio
     x = torch.from_numpy(x16).cuda()
     act_bits = 4 if activation == "a4" else 8
     codes_a, scales_a, sums_a, _ = ops.pack_activation(x, act_bits)
-    out = torch.empty((batch, rows), dtype=torch.float32, device="cuda")
+    outs = [torch.empty((batch, rows), dtype=torch.float32, device="cuda") for _ in range(matrices)]
+    out = outs[0]
 
     def launch(i: int) -> None:
-        ops.lowbit_gemv(fmt_id, [(weights[i % copies], scales[i % copies], out, rows, False)], codes_a, scales_a,
-                        sums_a, columns, batch)
+        c = (i % copies) * matrices
+        ops.lowbit_gemv(fmt_id, [(weights[c + j], scales[c + j], outs[j], rows, False) for j in range(matrices)],
+                        codes_a, scales_a, sums_a, columns, batch)
 
     for i in range(10):
         launch(i)
@@ -111,9 +115,10 @@ def run(fmt: str, rows: int, columns: int, batch: int, activation: str, iteratio
             max_error = max(max_error, error)
             if not np.isfinite(y[b, r]) or error > 0.003 * max(1.0, abs(expected)):
                 raise SystemExit(f"validation failed at batch {b} row {r}: expected={expected} actual={y[b, r]}")
-    code_bytes = rows * row_bytes
-    algorithmic = code_bytes + rows * groups * 2 + batch * (columns * act_bits // 8 + groups * 2) + batch * rows * 4
-    return {"format": fmt, "shape": [rows, columns], "batch": batch, "activation": activation,
+    code_bytes = rows * row_bytes * matrices
+    algorithmic = (code_bytes + matrices * rows * groups * 2 + batch * (columns * act_bits // 8 + groups * 2)
+                   + matrices * batch * rows * 4)
+    return {"format": fmt, "shape": [rows, columns], "matrices": matrices, "batch": batch, "activation": activation,
             "mean_launch_us": round(mean_us, 3), "packed_GBps": round(code_bytes / mean_us / 1e3, 1),
             "algorithmic_GBps": round(algorithmic / mean_us / 1e3, 1), "algorithmic_bytes": algorithmic,
             "launches_per_second": round(1e6 / mean_us, 1), "max_sampled_error": max_error,
@@ -129,10 +134,11 @@ def main() -> None:
     parser.add_argument("--activation", choices=["a4", "a8"], default="a4")
     parser.add_argument("--iterations", type=int, default=60)
     parser.add_argument("--copies", type=int, default=6)
+    parser.add_argument("--matrices", type=int, default=1, choices=[1, 2, 3, 4])
     parser.add_argument("--no-graph", action="store_true")
     args = parser.parse_args()
     print(json.dumps(run(args.format, args.rows, args.columns, args.batch, args.activation, args.iterations,
-                         args.copies, not args.no_graph)))
+                         args.copies, not args.no_graph, matrices=args.matrices)))
 
 
 if __name__ == "__main__":

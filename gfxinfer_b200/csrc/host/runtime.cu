@@ -754,12 +754,12 @@ int mlp_block(gfxb_session& s, const Layer& L, unsigned batch) {
   return all_reduce(s, s.update, static_cast<std::size_t>(batch) * s.e->cfg.hidden);
 }
 
-// Attention mixer: q/k/v GEMV, fused Q/K norm + RoPE + KV append, chunked
-// gated attention with the o_proj input pack fused in its epilogue, o_proj.
-int attention_mixer(gfxb_session& s, const Layer& L, __half* key_cache, __half* value_cache,
-                    const std::uint64_t* device_position, unsigned batch) {
+// Fused Q/K norm + RoPE + KV append, then chunked gated attention with the
+// o_proj input pack fused in its epilogue (the attention mixer between its
+// q/k/v and o projections).
+int attention_core(gfxb_session& s, const Layer& L, __half* key_cache, __half* value_cache,
+                   const std::uint64_t* device_position, unsigned batch) {
   const Shard& sh = s.e->shard;
-  GFXB_TRY(gemv(s, {{&L.q, s.proj_main}, {&L.k, s.proj_k}, {&L.v, s.proj_v}}, batch));
   QkRopeArgs r;
   r.q_input = s.proj_main;
   r.q_weight = L.q_norm;
@@ -796,18 +796,24 @@ int attention_mixer(gfxb_session& s, const Layer& L, __half* key_cache, __half* 
   a.act_codes = s.act_codes;
   a.act_scales = s.act_scales;
   a.act_sums = s.act_sums;
-  GFXB_TRY(launch_attention(a, batch, s.stream));
+  return launch_attention(a, batch, s.stream);
+}
+
+// Attention mixer: q/k/v GEMV, the attention core, o_proj.
+int attention_mixer(gfxb_session& s, const Layer& L, __half* key_cache, __half* value_cache,
+                    const std::uint64_t* device_position, unsigned batch) {
+  GFXB_TRY(gemv(s, {{&L.q, s.proj_main}, {&L.k, s.proj_k}, {&L.v, s.proj_v}}, batch));
+  GFXB_TRY(attention_core(s, L, key_cache, value_cache, device_position, batch));
   GFXB_TRY(gemv(s, {{&L.out, s.update}}, batch));
   return all_reduce(s, s.update, static_cast<std::size_t>(batch) * s.e->cfg.hidden);
 }
 
-// Gated-DeltaNet mixer: fused qkv/z/a/b GEMV, conv, recurrence (+ out_proj
-// pack), out_proj. With `record` the final states go to the snapshot buffers
-// and the per-token logs are written for a later rollback replay.
-int gdn_mixer(gfxb_session& s, const Layer& L, unsigned batch, bool record) {
+// The GDN step between the in- and out-projections: conv and recurrence
+// (+ out_proj pack). With `record` the final states go to the snapshot
+// buffers and the per-token logs are written for a later rollback replay.
+int gdn_recurrent_step(gfxb_session& s, const Layer& L, unsigned batch, bool record) {
   const Shard& sh = s.e->shard;
   const gfxb_model_config& c = s.e->cfg;
-  GFXB_TRY(gemv(s, {{&L.qkv, s.proj_main}, {&L.z, s.proj_z}, {&L.a, s.proj_a}, {&L.b, s.proj_b}}, batch));
   const std::size_t conv_elems = static_cast<std::size_t>(sh.channels) * 4;
   const std::size_t state_elems = static_cast<std::size_t>(sh.nv) * 128 * 128;
   __half* conv_state = s.conv_states + L.state_index * conv_elems;
@@ -851,9 +857,15 @@ int gdn_mixer(gfxb_session& s, const Layer& L, unsigned batch, bool record) {
   g.act_codes = s.act_codes;
   g.act_scales = s.act_scales;
   g.act_sums = s.act_sums;
-  GFXB_TRY(launch_gdn_recurrent(g, s.stream));
+  return launch_gdn_recurrent(g, s.stream);
+}
+
+// Gated-DeltaNet mixer: fused qkv/z/a/b GEMV, the GDN step, out_proj.
+int gdn_mixer(gfxb_session& s, const Layer& L, unsigned batch, bool record) {
+  GFXB_TRY(gemv(s, {{&L.qkv, s.proj_main}, {&L.z, s.proj_z}, {&L.a, s.proj_a}, {&L.b, s.proj_b}}, batch));
+  GFXB_TRY(gdn_recurrent_step(s, L, batch, record));
   GFXB_TRY(gemv(s, {{&L.out, s.update}}, batch));
-  return all_reduce(s, s.update, static_cast<std::size_t>(batch) * c.hidden);
+  return all_reduce(s, s.update, static_cast<std::size_t>(batch) * s.e->cfg.hidden);
 }
 
 __global__ void advance_kernel(std::uint64_t* position, std::uint32_t* tokens, const std::uint32_t* selected,
@@ -1759,6 +1771,7 @@ extern "C" int gfxb_engine_destroy(gfxb_engine* engine) {
   cudaFree(engine->arena);
   cudaStreamDestroy(engine->stream);
   delete engine;
+  cudaGetLastError();  // teardown errors are not reported; keep them from surfacing in a later launch check
   return GFXB_OK;
 }
 
@@ -1843,6 +1856,7 @@ extern "C" int gfxb_session_destroy(gfxb_session* session) {
   release_peer_reduce(*session);
   cudaFree(session->arena);
   delete session;
+  cudaGetLastError();  // teardown errors are not reported; keep them from surfacing in a later launch check
   return GFXB_OK;
 }
 
@@ -2131,6 +2145,107 @@ extern "C" int gfxb_session_read_state(gfxb_session* session, std::uint16_t* hid
     const std::size_t n = std::min<std::size_t>(logits_count, s.e->shard.vocab);
     GFXB_TRY(cuda_check(cudaMemcpy(logits, s.logits, n * sizeof(float), cudaMemcpyDeviceToHost), "logit download failed"));
   }
+  return GFXB_OK;
+}
+
+extern "C" int gfxb_session_enqueue_operation(gfxb_session* session, int kind, unsigned launches,
+                                              std::uint64_t* bytes) {
+  if (session == nullptr || launches == 0 || kind < 0 || kind > GFXB_OP_SILU_PACK) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid operation benchmark arguments");
+  }
+  gfxb_session& s = *session;
+  gfxb_engine& e = *s.e;
+  const gfxb_model_config& c = e.cfg;
+  const Shard& sh = e.shard;
+  const std::uint64_t H = c.hidden;
+  const bool gdn_kind = kind == GFXB_OP_GDN_IN || kind == GFXB_OP_GDN_OUT || kind == GFXB_OP_GDN_STEP;
+  const bool attention_kind = kind == GFXB_OP_ATTN_QKV || kind == GFXB_OP_ATTN_O || kind == GFXB_OP_ATTENTION;
+  // Cycle over the layers that carry the operation so every launch reads its
+  // own weights or states from HBM (one layer's fit in L2; all of them do not).
+  std::vector<const Layer*> layers;
+  for (const Layer& L : e.layers) {
+    if ((!gdn_kind && !attention_kind) || (gdn_kind && !L.attention) || (attention_kind && L.attention)) {
+      layers.push_back(&L);
+    }
+  }
+  if (layers.empty()) return fail(GFXB_INVALID_ARGUMENT, "no layer carries the requested operation");
+  const std::uint64_t act_bytes_per_column = c.activation_bits == 8 ? 1 : 0;  // A8: one byte; A4: half a byte
+  auto act_bytes = [&](std::uint64_t cols) {
+    return (act_bytes_per_column != 0 ? cols : cols / 2) + cols / 128 * 2;
+  };
+  auto matrix_bytes = [&](const QMatrix& m) {
+    const std::uint64_t bits = m.format == GFXB_W2 ? 2 : (m.format == GFXB_W3 ? 3 : 4);
+    return static_cast<std::uint64_t>(m.rows) * m.cols * bits / 8 + static_cast<std::uint64_t>(m.rows) * (m.cols / 128) * 2 +
+           static_cast<std::uint64_t>(m.rows) * 4;
+  };
+  const std::size_t kv_stride = static_cast<std::size_t>(s.cfg.maximum_context_tokens) * sh.nkv * 256;
+  const std::uint64_t position = std::min<std::uint64_t>(s.host_position, s.cfg.maximum_context_tokens - 1);
+  if (kind == GFXB_OP_ATTENTION) {
+    // from pinned memory and without a synchronisation, so the launches can be captured in a graph
+    std::memcpy(s.pinned + 64, &position, sizeof position);
+    GFXB_TRY(cuda_check(cudaMemcpyAsync(s.position, s.pinned + 64, sizeof position, cudaMemcpyHostToDevice, s.stream),
+                        "position upload failed"));
+  }
+  std::uint64_t total = 0;
+  for (unsigned i = 0; i < launches; ++i) {
+    const Layer& L = *layers[i % layers.size()];
+    std::vector<std::pair<const QMatrix*, void*>> mats;
+    std::uint64_t b = 0;
+    switch (kind) {
+      case GFXB_OP_MLP_GATE_UP: mats = {{&L.gate, s.gate}, {&L.up, s.up}}; break;
+      case GFXB_OP_MLP_DOWN: mats = {{&L.down, s.update}}; break;
+      case GFXB_OP_GDN_IN: mats = {{&L.qkv, s.proj_main}, {&L.z, s.proj_z}, {&L.a, s.proj_a}, {&L.b, s.proj_b}}; break;
+      case GFXB_OP_GDN_OUT: mats = {{&L.out, s.update}}; break;
+      case GFXB_OP_ATTN_QKV: mats = {{&L.q, s.proj_main}, {&L.k, s.proj_k}, {&L.v, s.proj_v}}; break;
+      case GFXB_OP_ATTN_O: mats = {{&L.out, s.update}}; break;
+      case GFXB_OP_LM_HEAD: {
+        static thread_local QMatrix head;
+        head = e.lm_head;
+        head.rows = sh.vocab;
+        mats = {{&head, s.logits}};
+        break;
+      }
+      case GFXB_OP_GDN_STEP: {
+        GFXB_TRY(gdn_recurrent_step(s, L, 1, false));
+        const std::uint64_t state = static_cast<std::uint64_t>(sh.nv) * 128 * 128 * 4;
+        b = 2 * state + static_cast<std::uint64_t>(sh.channels) * (4 * 2 * 2 + 4 * 2 + 4) +
+            static_cast<std::uint64_t>(sh.nv) * 128 * (4 + 2) + 2ull * sh.nv * 4 + act_bytes(sh.nv * 128ull) +
+            sh.nv * 128ull / 128 * 4;
+        break;
+      }
+      case GFXB_OP_ATTENTION: {
+        GFXB_TRY(attention_core(s, L, s.key_cache + L.state_index * kv_stride, s.value_cache + L.state_index * kv_stride,
+                                s.position, 1));
+        b = (position + 1) * sh.nkv * 256ull * 2 * 2 + sh.nq * 512ull * 4 + 2ull * sh.nkv * 256 * 4 +
+            act_bytes(sh.nq * 256ull) + sh.nq * 256ull / 128 * 4;
+        break;
+      }
+      case GFXB_OP_NORM_PACK:
+        GFXB_TRY(norm_pack(s, s.hidden[0], s.update, s.hidden[1], L.post_norm, 1));
+        b = H * 2 + H * 4 + H * 2 + H * 2 + act_bytes(H) + H / 128 * 4;
+        break;
+      default: {  // GFXB_OP_SILU_PACK
+        SiluPackArgs a;
+        a.gate = s.gate;
+        a.up = s.up;
+        a.elements = sh.inter;
+        a.batch = 1;
+        a.act_codes = s.act_codes;
+        a.act_scales = s.act_scales;
+        a.act_sums = s.act_sums;
+        GFXB_TRY(launch_silu_pack(a, static_cast<int>(c.activation_bits), s.stream));
+        b = sh.inter * 8ull + act_bytes(sh.inter) + sh.inter / 128 * 4ull;
+        break;
+      }
+    }
+    if (!mats.empty()) {
+      GFXB_TRY(gemv(s, mats, 1));
+      for (const auto& m : mats) b += matrix_bytes(*m.first);
+      b += act_bytes(mats[0].first->cols) + mats[0].first->cols / 128 * 4;
+    }
+    if (i == 0) total = b;
+  }
+  if (bytes != nullptr) *bytes = total;
   return GFXB_OK;
 }
 

@@ -45,7 +45,9 @@ class Engine:
     def __init__(self, handle: int, config: abi.ModelConfig) -> None:
         self._handle = ctypes.c_void_p(handle)
         self.config = config
-        self._sessions: weakref.WeakSet = weakref.WeakSet()
+        # raw handles of the sessions still open on this engine: close() destroys them before the engine
+        # even when their Python objects are unreachable (cyclic garbage finalises in any order)
+        self._session_handles: set[int] = set()
         _LIVE.add(self)
 
     @classmethod
@@ -89,10 +91,18 @@ class Engine:
         check(lib().gfxb_engine_weight_bytes(self._handle, ctypes.byref(out)))
         return out.value
 
+    def _release_session(self, handle: int) -> bool:
+        """True when the session handle is still open and the caller must destroy it."""
+        if handle in self._session_handles:
+            self._session_handles.discard(handle)
+            return True
+        return False
+
     def close(self) -> None:
-        """Destroys the engine; sessions created from it are closed first."""
-        for session in list(self._sessions):
-            session.close()
+        """Destroys the engine; sessions created from it are destroyed first."""
+        for handle in list(self._session_handles):
+            lib().gfxb_session_destroy(ctypes.c_void_p(handle))
+        self._session_handles.clear()
         if self._handle:
             lib().gfxb_engine_destroy(self._handle)
             self._handle = ctypes.c_void_p()
@@ -117,7 +127,7 @@ class QwenDecodeSession:
     def __init__(self, handle: int, engine: Engine) -> None:
         self._handle = ctypes.c_void_p(handle)
         self.engine = engine
-        engine._sessions.add(self)
+        engine._session_handles.add(handle)
 
     @classmethod
     def create(cls, engine: Engine, maximum_context_tokens: int | None = None, graph_verifier_batch: int = 0,
@@ -199,6 +209,12 @@ class QwenDecodeSession:
         check(lib().gfxb_session_enqueue_gemv(self._handle, kind, launches, ctypes.byref(out)))
         return out.value
 
+    def enqueue_operation(self, kind: int, launches: int) -> int:
+        """Enqueue standalone launches of one decode operation (gfxb.h GFXB_OP_*); returns bytes per launch."""
+        out = ctypes.c_uint64()
+        check(lib().gfxb_session_enqueue_operation(self._handle, kind, launches, ctypes.byref(out)))
+        return out.value
+
     def read_state(self, logits_count: int = 0):
         import numpy as np
 
@@ -231,7 +247,8 @@ class QwenDecodeSession:
 
     def close(self) -> None:
         if self._handle:
-            lib().gfxb_session_destroy(self._handle)
+            if self.engine._release_session(self._handle.value):
+                lib().gfxb_session_destroy(self._handle)
             self._handle = ctypes.c_void_p()
 
     def __del__(self) -> None:

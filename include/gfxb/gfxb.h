@@ -372,6 +372,19 @@ void* gfxb_session_stream(gfxb_session* session);
  * bytes of one launch (codes, fp16 scales, A4 activation, fp32 outputs).
  * Used to time the dominant kernel in isolation. */
 int gfxb_session_enqueue_gemv(gfxb_session* session, int kind, unsigned launches, uint64_t* bytes);
+/* Enqueues `launches` launches of one decode operation at batch 1, cycling
+ * over the layers that carry it (each launch reads its own weights or states
+ * from HBM), for timing kernels in isolation; `bytes` receives the
+ * algorithmic bytes one launch moves (weights, scales, states, activations,
+ * outputs). The operations write the session's buffers, and GDN_STEP and
+ * ATTENTION also its recurrent states and KV caches (ATTENTION at the
+ * session's position): time them on a session made for timing. */
+enum {
+  GFXB_OP_MLP_GATE_UP = 0, GFXB_OP_MLP_DOWN = 1, GFXB_OP_GDN_IN = 2, GFXB_OP_GDN_OUT = 3, GFXB_OP_ATTN_QKV = 4,
+  GFXB_OP_ATTN_O = 5, GFXB_OP_LM_HEAD = 6, GFXB_OP_GDN_STEP = 7, GFXB_OP_ATTENTION = 8, GFXB_OP_NORM_PACK = 9,
+  GFXB_OP_SILU_PACK = 10
+};
+int gfxb_session_enqueue_operation(gfxb_session* session, int kind, unsigned launches, uint64_t* bytes);
 /* One greedy step on the persistent token kernel with its timeline recorded
  * (GFXB_UNSUPPORTED when the session runs per-operation launches). timeline
  * receives [op_count + 1][2][ctas] globaltimer nanoseconds: entry (i, 0, c)

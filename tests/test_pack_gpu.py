@@ -285,15 +285,15 @@ def test_converted_artifacts_decode_identically(ops, oracle, tmp_path, mlp_bits)
         token = None
         for t in prompt:
             token = session.greedy_step(t)
-        stream = []
+        stream, drafts = [], []
         for _ in range(24):
             stream.append(token)
             token = session.greedy_step(token)
-        draft = session.mtp_draft(token)
-        results.append((stream, draft, session.read_state(cfg.vocab)))
+            drafts.append(session.mtp_draft(token))  # the MTP draft follows every committed token
+        results.append((stream, drafts, session.read_state(cfg.vocab)))
         session.close()
-    for stream, draft, (hidden, logits) in results[1:]:
-        assert stream == results[0][0] and draft == results[0][1]
+    for stream, drafts, (hidden, logits) in results[1:]:
+        assert stream == results[0][0] and drafts == results[0][1]
         np.testing.assert_array_equal(hidden, results[0][2][0])
         np.testing.assert_array_equal(logits.view(np.uint32), results[0][2][1].view(np.uint32))
     assert len(set(results[0][0])) > 4
