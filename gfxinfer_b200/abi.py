@@ -132,6 +132,7 @@ SIGNATURES: dict[str, tuple] = {
     "gfxb_session_stream": (c_void_p, [P]),
     "gfxb_session_enqueue_gemv": (c_int, [P, c_int, c_uint, POINTER(c_uint64)]),
     "gfxb_session_enqueue_operation": (c_int, [P, c_int, c_uint, POINTER(c_uint64)]),
+    "gfxb_session_time_operation": (c_int, [P, c_int, c_uint, c_int, POINTER(ctypes.c_float), POINTER(c_uint64)]),
     "gfxb_session_read_state": (c_int, [P, P, P, c_size_t]),
     "gfxb_session_trace_step": (c_int, [P, c_uint32, POINTER(c_uint32), P, c_size_t, POINTER(c_uint), POINTER(c_uint),
                                         P]),

@@ -3,7 +3,7 @@
     python -m gfxinfer_b200.bench_ops [--layers 64] [--position 256] [--launches 96] [--ops gdn_step,attention]
 
 One engine with config-2 widths (hidden 5120, MLP 17408 W3, GDN/attention W4, A4) and a session filled to
-`position` by chunked prefill; every operation (gfxb_session_enqueue_operation) is launched `launches` times,
+`position` by chunked prefill; every operation is launched `launches` times (gfxb_session_time_operation),
 cycling over the layers that carry it so each launch reads its weights or states from HBM, replayed from a
 CUDA graph and timed with CUDA events on the session stream. Prints one JSON line per operation: mean
 launch time, algorithmic bytes per launch, GB/s and the fraction of the measured HBM copy bandwidth.
@@ -15,7 +15,6 @@ import json
 import os
 
 import numpy as np
-import torch
 
 from . import session as gs
 
@@ -38,29 +37,10 @@ def run(layers: int, position: int, launches: int, names: list[str], graph: bool
     rng = np.random.default_rng(cfg["seed"])
     if position > 0:
         session.prefill([int(t) for t in rng.integers(0, cfg["vocab"], size=position)])
-    stream = torch.cuda.ExternalStream(session.stream())
     peak, source = measured_peak()
     out = []
     for name in names:
-        kind = OPS[name]
-        session.enqueue_operation(kind, 8)  # warm-up
-        torch.cuda.synchronize()
-        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        if graph:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                per_launch = session.enqueue_operation(kind, launches)
-            g.replay()
-            torch.cuda.synchronize()
-            start.record(stream)
-            g.replay()
-            stop.record(stream)
-        else:
-            start.record(stream)
-            per_launch = session.enqueue_operation(kind, launches)
-            stop.record(stream)
-        stop.synchronize()
-        us = start.elapsed_time(stop) * 1000.0 / launches
+        us, per_launch = session.time_operation(OPS[name], launches, graph)
         gbps = per_launch / (us * 1e-6) / 1e9
         out.append({"op": name, "us": round(us, 3), "bytes": per_launch, "GBps": round(gbps, 1),
                     "frac": round(gbps / peak, 4), "peak": peak, "peak_source": source, "position": position,

@@ -2249,6 +2249,48 @@ extern "C" int gfxb_session_enqueue_operation(gfxb_session* session, int kind, u
   return GFXB_OK;
 }
 
+extern "C" int gfxb_session_time_operation(gfxb_session* session, int kind, unsigned launches, int use_graph,
+                                           float* microseconds, std::uint64_t* bytes) {
+  if (session == nullptr || microseconds == nullptr || launches == 0) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid operation timing arguments");
+  }
+  gfxb_session& s = *session;
+  GFXB_TRY(cuda_check(cudaSetDevice(s.e->device), "cudaSetDevice failed"));
+  GFXB_TRY(gfxb_session_enqueue_operation(session, kind, std::min(launches, 8u), nullptr));  // warm-up
+  cudaEvent_t start = nullptr, stop = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int status = cuda_check(cudaEventCreate(&start), "event creation failed");
+  if (status == GFXB_OK) status = cuda_check(cudaEventCreate(&stop), "event creation failed");
+  if (status == GFXB_OK && use_graph) {
+    // the launches captured once and replayed: host launch cost stays out of the timing
+    cudaGraph_t graph = nullptr;
+    status = cuda_check(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal), "graph capture start failed");
+    if (status == GFXB_OK) {
+      const int enqueued = gfxb_session_enqueue_operation(session, kind, launches, bytes);
+      const cudaError_t end = cudaStreamEndCapture(s.stream, &graph);
+      status = enqueued != GFXB_OK ? enqueued : cuda_check(end, "graph capture end failed");
+    }
+    if (status == GFXB_OK) status = cuda_check(cudaGraphInstantiate(&exec, graph, 0), "graph instantiation failed");
+    if (graph != nullptr) cudaGraphDestroy(graph);
+    if (status == GFXB_OK) status = cuda_check(cudaGraphLaunch(exec, s.stream), "graph launch failed");
+    if (status == GFXB_OK) status = cuda_check(cudaEventRecord(start, s.stream), "event record failed");
+    if (status == GFXB_OK) status = cuda_check(cudaGraphLaunch(exec, s.stream), "graph launch failed");
+  } else if (status == GFXB_OK) {
+    status = cuda_check(cudaStreamSynchronize(s.stream), "warm-up failed");
+    if (status == GFXB_OK) status = cuda_check(cudaEventRecord(start, s.stream), "event record failed");
+    if (status == GFXB_OK) status = gfxb_session_enqueue_operation(session, kind, launches, bytes);
+  }
+  if (status == GFXB_OK) status = cuda_check(cudaEventRecord(stop, s.stream), "event record failed");
+  if (status == GFXB_OK) status = cuda_check(cudaEventSynchronize(stop), "timed launches failed");
+  float ms = 0.0f;
+  if (status == GFXB_OK) status = cuda_check(cudaEventElapsedTime(&ms, start, stop), "event timing failed");
+  if (status == GFXB_OK) *microseconds = ms * 1000.0f / static_cast<float>(launches);
+  if (exec != nullptr) cudaGraphExecDestroy(exec);
+  if (start != nullptr) cudaEventDestroy(start);
+  if (stop != nullptr) cudaEventDestroy(stop);
+  return status;
+}
+
 extern "C" int gfxb_session_enqueue_gemv(gfxb_session* session, int kind, unsigned launches, std::uint64_t* bytes) {
   if (session == nullptr || launches == 0) return fail(GFXB_INVALID_ARGUMENT, "invalid GEMV benchmark arguments");
   gfxb_session& s = *session;

@@ -215,6 +215,13 @@ class QwenDecodeSession:
         check(lib().gfxb_session_enqueue_operation(self._handle, kind, launches, ctypes.byref(out)))
         return out.value
 
+    def time_operation(self, kind: int, launches: int, graph: bool = True) -> tuple[float, int]:
+        """(microseconds per launch, bytes per launch) of one decode operation timed in isolation."""
+        us, out = ctypes.c_float(), ctypes.c_uint64()
+        check(lib().gfxb_session_time_operation(self._handle, kind, launches, int(graph), ctypes.byref(us),
+                                                ctypes.byref(out)))
+        return us.value, out.value
+
     def read_state(self, logits_count: int = 0):
         import numpy as np
 

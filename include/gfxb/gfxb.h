@@ -385,6 +385,12 @@ enum {
   GFXB_OP_SILU_PACK = 10
 };
 int gfxb_session_enqueue_operation(gfxb_session* session, int kind, unsigned launches, uint64_t* bytes);
+/* Times gfxb_session_enqueue_operation: `launches` launches (after 8 warm-up
+ * launches) captured in a CUDA graph and replayed (use_graph != 0) or
+ * enqueued directly, between CUDA events on the session stream; writes the
+ * mean microseconds per launch. Synchronous. */
+int gfxb_session_time_operation(gfxb_session* session, int kind, unsigned launches, int use_graph,
+                                float* microseconds, uint64_t* bytes);
 /* One greedy step on the persistent token kernel with its timeline recorded
  * (GFXB_UNSUPPORTED when the session runs per-operation launches). timeline
  * receives [op_count + 1][2][ctas] globaltimer nanoseconds: entry (i, 0, c)

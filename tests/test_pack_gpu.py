@@ -282,10 +282,11 @@ def test_converted_artifacts_decode_identically(ops, oracle, tmp_path, mlp_bits)
     results = []
     for engine in engines:
         session = gs.QwenDecodeSession.create(engine)
-        token = None
+        token, drafts = None, []
         for t in prompt:
             token = session.greedy_step(t)
-        stream, drafts = [], []
+            drafts.append(session.mtp_draft(token))  # the MTP draft follows every committed token
+        stream = []
         for _ in range(24):
             stream.append(token)
             token = session.greedy_step(token)
