@@ -8,6 +8,8 @@
 // order that the CPU oracle restates, so outputs compare bit for bit.
 #include <type_traits>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "ops.cuh"
 #include "ops_device.cuh"
@@ -145,13 +147,189 @@ __global__ __launch_bounds__(kGdnThreads) void gdn_recurrent_kernel(GdnRecurrent
   float S[kGdnRows];
   gdn_load_state(args, vh, t, S);
   if constexpr (Block) {  // up to kGdnBlockMax tokens: the three-phase form
-    __shared__ GdnBlockScratch scratch;
-    gdn_recurrent_block<FusedConv>(args, vh, t, S, scratch);
+    extern __shared__ __align__(16) std::uint8_t block_scratch[];
+    gdn_recurrent_block<FusedConv>(args, vh, t, S, *reinterpret_cast<GdnBlockScratch*>(block_scratch));
   } else {
     __shared__ GdnScratch scratch;
     gdn_recurrent_tokens<BlockSync, FusedConv>(args, vh, t, S, BlockSync{}, scratch);
   }
   gdn_store_state(args, vh, t, S);
+}
+
+// ---------------------------------------------------------------------------
+// The single-token GDN step with the conv fused in, its 128 state columns split
+// over kGdnParts CTAs per value head (4 x 48 CTAs for config 2 instead of 48).
+// CTA (vh, part) holds columns [32 part, 32 part + 32): lane = column, warp w =
+// rows [32 w, 32 w + 32), so every state load and store is one 128-byte line
+// per warp. Each CTA convolves and normalises the key head's q/k itself; the
+// two ordered fma chains over the 128 rows (memory = sum_k S[k][v] key[k],
+// then mixed = sum_k S'[k][v] query[k]) pass from warp to warp in row order,
+// the same operations in the same order as gdn_recurrent_tokens, hence the
+// same bits. Parts 1..3 send their 32 mixed values to part 0 (st.async on one
+// mbarrier) and exit; part 0 runs the output RMSNorm, SiLU(z) gate and pack
+// for the whole head. The CTAs of one key head form one cluster: one cluster
+// barrier, arrived right after the conv taps are read, orders every CTA's
+// read of the shared q/k conv state before its single writer updates it and
+// shows that part 0's mbarrier is initialised before the first remote store.
+// ---------------------------------------------------------------------------
+
+constexpr unsigned kGdnParts = 4;
+constexpr unsigned kGdnPartColumns = kGdnHead / kGdnParts;
+constexpr unsigned kGdnPartThreads = 128;
+
+struct GdnPartScratch {
+  float query[kGdnHead];
+  float key[kGdnHead];
+  float mixed[kGdnHead];  // part 0: the head's mixed values (own warp 0 + received)
+  float value[kGdnPartColumns];
+  float carry[kGdnPartColumns];
+  float delta[kGdnPartColumns];
+  float sums[3][4];
+  float gates[2];
+  float pack_max[4];
+  int pack_sum[4];
+  std::uint64_t bar;
+};
+
+__global__ __launch_bounds__(kGdnPartThreads) void gdn_parts_kernel(GdnRecurrentArgs args) {
+  __shared__ __align__(16) GdnPartScratch sc;
+  pdl_trigger();
+  const unsigned t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  const unsigned vh = blockIdx.x / kGdnParts, part = blockIdx.x % kGdnParts;
+  const unsigned column = part * kGdnPartColumns + lane;  // this thread's state column
+  const unsigned ratio = args.value_heads / args.key_heads, kh = vh / ratio;
+  const unsigned key_elements = args.key_heads * kGdnHead;
+  const unsigned value_elements = args.value_heads * kGdnHead;
+  const bool qk_owner = vh % ratio == 0 && part == 0;  // writes the shared q/k conv state
+  const std::size_t q_channel = kh * kGdnHead + t, k_channel = key_elements + kh * kGdnHead + t;
+  const std::size_t v_channel = 2u * key_elements + vh * kGdnHead + column;
+  const float* initial = args.initial_state + static_cast<std::size_t>(vh) * kGdnHead * kGdnHead;
+  float* final_state = args.final_state + static_cast<std::size_t>(vh) * kGdnHead * kGdnHead;
+  // weights never change: read before the dependency wait; the state slice is pulled into L2
+  const float neg_exp_a_log = -gx_expf(bf2f(args.a_log[vh]));
+  const float dt_bias = bf2f(args.dt_bias[vh]);
+  const float norm_weight = part == 0 ? bf2f(args.norm_weight[t]) : 0.0f;
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(initial + static_cast<std::size_t>(t) * kGdnHead +
+                                                part * kGdnPartColumns)
+               : "memory");
+  if (part == 0 && t == 0) {
+    mbar_init(&sc.bar, 1);
+    fence_mbar_init();
+    mbar_expect_tx(&sc.bar, (kGdnParts - 1u) * kGdnPartColumns * 4u);
+  }
+  pdl_wait();
+  float S[kGdnPartColumns];
+#pragma unroll
+  for (unsigned j = 0; j < kGdnPartColumns; ++j) S[j] = initial[(warp * kGdnPartColumns + j) * kGdnHead + column];
+  ConvChannel cq, ck, cv;
+  cq.load(args.conv, q_channel);
+  ck.load(args.conv, k_channel);
+  if (warp == 0) cv.load(args.conv, v_channel);
+  const float z = part == 0 ? ld_cg(args.z + static_cast<std::size_t>(vh) * kGdnHead + t) : 0.0f;
+  cluster_arrive();  // this CTA has read the conv taps; part 0's barrier is initialised
+  // q/k conv and norms (element t of the key head), the value conv of this part's columns, the gates
+  const float q = cq.step(args.conv, q_channel, false);
+  const float k = ck.step(args.conv, k_channel, false);
+  if (warp == 0) sc.value[lane] = cv.step(args.conv, v_channel, false);
+  const float qs = warp_sum_down(__fmul_rn(q, q));
+  const float ks = warp_sum_down(__fmul_rn(k, k));
+  if (lane == 0) {
+    sc.sums[0][warp] = qs;
+    sc.sums[1][warp] = ks;
+  }
+  if (t == 0) {
+    const float a_value = __fadd_rn(ld_cg(args.a + vh), dt_bias);
+    const float softplus = a_value > 20.0f ? a_value : gx_log1pf(gx_expf(a_value));
+    sc.gates[0] = gx_expf(__fmul_rn(neg_exp_a_log, softplus));
+    sc.gates[1] = gx_sigmoid(ld_cg(args.b + vh));
+  }
+  __syncthreads();
+  {
+    const float inv_q = __fmul_rn(inv_sqrt_rn(__fadd_rn(tree_of_eight(sc.sums[0], 4), 1.0e-6f)), 0.08838834764831845f);
+    const float inv_k = inv_sqrt_rn(__fadd_rn(tree_of_eight(sc.sums[1], 4), 1.0e-6f));
+    sc.query[t] = __fmul_rn(q, inv_q);
+    sc.key[t] = __fmul_rn(k, inv_k);
+  }
+  __syncthreads();
+  const float decay = sc.gates[0], beta = sc.gates[1];
+  const unsigned row0 = warp * kGdnPartColumns;
+#pragma unroll
+  for (unsigned j = 0; j < kGdnPartColumns; ++j) S[j] = __fmul_rn(S[j], decay);
+  // memory = sum over k in row order of S[k][v] * key[k], warp by warp
+  for (unsigned w = 0; w < 4u; ++w) {
+    if (warp == w) {
+      float memory = w == 0 ? 0.0f : sc.carry[lane];
+#pragma unroll
+      for (unsigned j = 0; j < kGdnPartColumns; ++j) memory = fmaf(S[j], sc.key[row0 + j], memory);
+      sc.carry[lane] = memory;
+    }
+    __syncthreads();
+  }
+  if (warp == 0) sc.delta[lane] = __fmul_rn(__fsub_rn(sc.value[lane], sc.carry[lane]), beta);
+  __syncthreads();
+  const float delta = sc.delta[lane];
+#pragma unroll
+  for (unsigned j = 0; j < kGdnPartColumns; ++j) {
+    S[j] = fmaf(sc.key[row0 + j], delta, S[j]);
+    final_state[(row0 + j) * kGdnHead + column] = S[j];
+  }
+  // mixed = sum over k in row order of S'[k][v] * query[k], warp by warp
+  for (unsigned w = 0; w < 4u; ++w) {
+    if (warp == w) {
+      float mixed = w == 0 ? 0.0f : sc.carry[lane];
+#pragma unroll
+      for (unsigned j = 0; j < kGdnPartColumns; ++j) mixed = fmaf(S[j], sc.query[row0 + j], mixed);
+      sc.carry[lane] = mixed;
+    }
+    __syncthreads();
+  }
+  cluster_wait();  // every CTA of the key head has read the conv taps and part 0 can take stores
+  if (warp == 0) cv.store(args.conv, v_channel);
+  if (qk_owner) {
+    cq.store(args.conv, q_channel);
+    ck.store(args.conv, k_channel);
+  }
+  const std::uint32_t leader = (vh % ratio) * kGdnParts;  // cluster rank of this head's part 0
+  if (part != 0) {
+    if (warp == 0) {
+      st_async_s32(map_shared_rank(smem_addr(&sc.mixed[column]), leader), __float_as_int(sc.carry[lane]),
+                   map_shared_rank(smem_addr(&sc.bar), leader));
+    }
+    return;
+  }
+  if (warp == 0) sc.mixed[lane] = sc.carry[lane];
+  bool arrived = false;
+  for (std::uint32_t i = 0; i < kWaitLimit && !arrived; ++i) arrived = mbar_try_wait_cluster(&sc.bar, 0);
+  if (!arrived && t == 0) atomicOr(&g_ops_error, kDeviceErrorTimeout);
+  __syncthreads();
+  // output RMSNorm, SiLU(z) gate and pack of the head (thread t = column t), as gdn_recurrent_tokens
+  const float m = arrived ? sc.mixed[t] : 0.0f;
+  const float os = warp_sum_down(__fmul_rn(m, m));
+  if (lane == 0) sc.sums[2][warp] = os;
+  __syncthreads();
+  const float inv_o = inv_sqrt_rn(__fadd_rn(__fdiv_rn(tree_of_eight(sc.sums[2], 4), 128.0f), 1.0e-6f));
+  const float normalized = __fmul_rn(__fmul_rn(m, inv_o), norm_weight);
+  const __half y = f2h(__fmul_rn(normalized, gx_silu(z)));
+  args.output[static_cast<std::size_t>(vh) * kGdnHead + t] = y;
+  if (args.act_bits != 0) {
+    const float y_value = h2f(y);
+    const std::size_t row = static_cast<std::size_t>(vh) * kGdnHead;
+    float amax = warp_amax(y_value);
+    if (lane == 0) sc.pack_max[warp] = amax;
+    __syncthreads();
+    amax = fmaxf(fmaxf(sc.pack_max[0], sc.pack_max[1]), fmaxf(sc.pack_max[2], sc.pack_max[3]));
+    const __half scale_h = args.act_bits == 8 ? act_scale_of<8>(amax) : act_scale_of<4>(amax);
+    const float scale = h2f(scale_h), recip = __frcp_rn(scale);
+    const int code = args.act_bits == 8 ? act_code_fast<8>(y_value, scale, recip) : act_code_fast<4>(y_value, scale, recip);
+    args.act_codes[row + fragment_offset(t)] = static_cast<std::int8_t>(code);
+    const int total = warp_sum_int(code);
+    if (lane == 0) sc.pack_sum[warp] = total;
+    __syncthreads();
+    if (t == 0) {
+      args.act_scales[vh] = scale_h;
+      args.act_sums[vh] = sc.pack_sum[0] + sc.pack_sum[1] + sc.pack_sum[2] + sc.pack_sum[3];
+    }
+  }
 }
 
 // Rollback replay (qwen_ops.hip:467-539): conv inputs and delta-rule updates of
@@ -471,6 +649,34 @@ int launch_gdn_conv(const GdnConvArgs& args, cudaStream_t stream) {
   return launch_status("GDN convolution launch failed");
 }
 
+// GFXB_GDN_PARTS=0 keeps single-token steps on the one-CTA-per-head kernel (for A/B timing).
+bool gdn_parts_enabled() {
+  static const bool enabled = [] {
+    const char* value = std::getenv("GFXB_GDN_PARTS");
+    return value == nullptr || value[0] != '0';
+  }();
+  return enabled;
+}
+
+// The block form keeps every token's vectors in dynamic shared memory (above the 48 KB default).
+int configure_gdn_block() {
+  static DeviceOnce configured;
+  return configured.run([](int) {
+    cudaError_t error = cudaFuncSetAttribute(gdn_recurrent_kernel<true, true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(sizeof(GdnBlockScratch)));
+    if (error == cudaSuccess) {
+      error = cudaFuncSetAttribute(gdn_recurrent_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(sizeof(GdnBlockScratch)));
+    }
+    if (error != cudaSuccess) {
+      set_error_cuda(error, "GDN block shared-memory configuration failed");
+      return static_cast<int>(GFXB_CUDA_ERROR);
+    }
+    return static_cast<int>(GFXB_OK);
+  });
+}
+
 int launch_gdn_recurrent(const GdnRecurrentArgs& args, cudaStream_t stream) {
   if (args.z == nullptr || args.a == nullptr || args.b == nullptr || args.a_log == nullptr ||
       args.dt_bias == nullptr || args.norm_weight == nullptr || args.initial_state == nullptr ||
@@ -486,9 +692,25 @@ int launch_gdn_recurrent(const GdnRecurrentArgs& args, cudaStream_t stream) {
       return fail(GFXB_INVALID_ARGUMENT, "fused GDN conv needs its weights and states and at most 8 value heads "
                                          "per key head");
     }
-    if (args.batch >= 2u && args.batch <= kGdnBlockMax) {  // a verifier block: the three-phase form
-      launch_kernel(gdn_recurrent_kernel<true, true>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, ratio,
-                    args);
+    if (args.batch == 1u && ratio * kGdnParts <= 16u && args.key_log == nullptr && args.delta_log == nullptr &&
+        args.decay_log == nullptr && args.conv.appended_log == nullptr && gdn_parts_enabled()) {
+      // one token: the head's columns over kGdnParts CTAs, the key head's CTAs one cluster
+      static DeviceOnce configured;
+      GFXB_TRY(configured.run([](int) {
+        const cudaError_t error =
+            cudaFuncSetAttribute(gdn_parts_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (error != cudaSuccess) {
+          set_error_cuda(error, "GDN cluster configuration failed");
+          return static_cast<int>(GFXB_CUDA_ERROR);
+        }
+        return static_cast<int>(GFXB_OK);
+      }));
+      launch_kernel(gdn_parts_kernel, dim3(args.value_heads * kGdnParts), dim3(kGdnPartThreads), 0, stream,
+                    ratio * kGdnParts, args);
+    } else if (args.batch >= 2u && args.batch <= kGdnBlockMax) {  // a verifier block: the three-phase form
+      GFXB_TRY(configure_gdn_block());
+      launch_kernel(gdn_recurrent_kernel<true, true>, dim3(args.value_heads), dim3(kGdnThreads),
+                    sizeof(GdnBlockScratch), stream, ratio, args);
     } else {
       launch_kernel(gdn_recurrent_kernel<true, false>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, ratio,
                     args);
@@ -496,7 +718,9 @@ int launch_gdn_recurrent(const GdnRecurrentArgs& args, cudaStream_t stream) {
   } else {
     if (args.qkv == nullptr) return fail(GFXB_INVALID_ARGUMENT, "invalid GDN recurrent arguments");
     if (args.batch >= 2u && args.batch <= kGdnBlockMax) {  // a verifier block: the three-phase form
-      launch_kernel(gdn_recurrent_kernel<false, true>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, 0, args);
+      GFXB_TRY(configure_gdn_block());
+      launch_kernel(gdn_recurrent_kernel<false, true>, dim3(args.value_heads), dim3(kGdnThreads),
+                    sizeof(GdnBlockScratch), stream, 0, args);
     } else {
       launch_kernel(gdn_recurrent_kernel<false, false>, dim3(args.value_heads), dim3(kGdnThreads), 0, stream, 0, args);
     }

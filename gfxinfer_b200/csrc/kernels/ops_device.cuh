@@ -564,7 +564,7 @@ __device__ __forceinline__ void gdn_recurrent_tokens(const GdnRecurrentArgs& arg
 // results are identical; only the barriers per token are gone.
 // ---------------------------------------------------------------------------
 
-constexpr unsigned kGdnBlockMax = 16;
+constexpr unsigned kGdnBlockMax = 32;  // the scratch (66 KB) lives in dynamic shared memory
 
 struct GdnBlockScratch {
   float query[kGdnBlockMax][kGdnHead];  // raw, then normalized
