@@ -105,6 +105,9 @@ SIGNATURES: dict[str, tuple] = {
     "gfxb_qk_rms_norm_rope": (c_int, [P, P, P, c_uint, c_size_t, P, P, P, c_uint, c_size_t, c_uint, P, P, c_size_t,
                                       c_uint64, P, c_uint, P, P, P, c_size_t, P]),
     "gfxb_gated_attention_scratch_bytes": (c_size_t, [c_uint, c_size_t, c_uint]),
+    "gfxb_decode_attention_scratch_bytes": (c_size_t, [c_uint, c_size_t]),
+    "gfxb_decode_attention": (c_int, [P, P, c_size_t, P, P, c_size_t, P, c_uint, P, P, c_size_t, P, P, c_size_t,
+                                      c_uint64, P, c_uint, c_uint, P, P, c_size_t, P]),
     "gfxb_gated_attention": (c_int, [P, P, P, P, P, c_size_t, P, c_size_t, c_uint, c_uint, c_uint, P, c_size_t, P]),
     "gfxb_gated_attention_static_scratch": (c_int, [P, P, P, P, P, c_size_t, P, c_size_t, c_uint, c_uint, c_uint, P]),
     "gfxb_argmax_scratch_bytes": (c_size_t, [c_uint]),

@@ -32,6 +32,7 @@ def measured_peak() -> tuple[float, str]:
 
 def run(layers: int, position: int, launches: int, names: list[str], graph: bool = True, **overrides) -> list[dict]:
     cfg = dict(gs.CONFIG2, layers=layers, **overrides)
+    cfg["max_context"] = max(cfg["max_context"], -(-(position + 1) // 128) * 128)
     engine = gs.Engine.create(gs.model_config(**cfg), include_mtp=False)
     session = gs.QwenDecodeSession.create(engine, use_graphs=False)
     rng = np.random.default_rng(cfg["seed"])

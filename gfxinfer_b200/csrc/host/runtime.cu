@@ -538,6 +538,7 @@ struct gfxb_session {
         *proj_v = nullptr, *update = nullptr, *gate = nullptr, *up = nullptr, *logits = nullptr;
   __half *conv_out = nullptr, *gdn_out = nullptr, *query = nullptr, *attn_out = nullptr;
   float* attention_partials = nullptr;
+  std::uint32_t* attention_tickets = nullptr;  // [nq] merge counters of the single-token attention
   std::uint32_t attention_chunks = 0;
   float* argmax_values = nullptr;
   std::uint32_t* argmax_indices = nullptr;
@@ -779,7 +780,6 @@ int attention_core(gfxb_session& s, const Layer& L, __half* key_cache, __half* v
   r.sin_table = s.rope_sin;
   r.table_positions = s.cfg.maximum_context_tokens;
   r.device_base_position = device_position;
-  GFXB_TRY(launch_qk_rope(r, batch, s.stream));
   AttentionArgs a;
   a.query = s.query;
   a.gate = s.proj_main;
@@ -796,6 +796,14 @@ int attention_core(gfxb_session& s, const Layer& L, __half* key_cache, __half* v
   a.act_codes = s.act_codes;
   a.act_scales = s.act_scales;
   a.act_sums = s.act_sums;
+  if (batch == 1 && attention_decode_enabled()) {
+    AttentionDecodeArgs d;
+    d.rope = r;
+    d.attention = a;
+    d.tickets = s.attention_tickets;
+    return launch_attention_decode(d, s.stream);
+  }
+  GFXB_TRY(launch_qk_rope(r, batch, s.stream));
   return launch_attention(a, batch, s.stream);
 }
 
@@ -1356,6 +1364,7 @@ int allocate_session(gfxb_session& s, bool place) {
   s.attn_out = plan.take<__half>(B * sh.nq * 256);
   s.attention_chunks = static_cast<std::uint32_t>((ctx + kAttentionChunk - 1) / kAttentionChunk);
   s.attention_partials = plan.take<float>(attention_partial_bytes(sh.nq, ctx, kMaxBlock) / sizeof(float));
+  s.attention_tickets = plan.take<std::uint32_t>(sh.nq);
   s.argmax_values = plan.take<float>(argmax_scratch_bytes(kMaxBlock) / 8);
   s.argmax_indices = plan.take<std::uint32_t>(argmax_scratch_bytes(kMaxBlock) / 8);
   s.gathered = plan.take<std::uint32_t>(static_cast<std::size_t>(sh.tp) * B * 2);

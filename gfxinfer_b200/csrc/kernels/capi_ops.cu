@@ -182,6 +182,60 @@ extern "C" int gfxb_gated_attention(const std::uint16_t* query, const float* gat
   return launch_attention(a, batch, as_stream(stream));
 }
 
+extern "C" std::size_t gfxb_decode_attention_scratch_bytes(unsigned q_heads, std::size_t capacity) {
+  return attention_partial_bytes(q_heads, capacity, 1) + static_cast<std::size_t>(q_heads) * sizeof(std::uint32_t);
+}
+
+extern "C" int gfxb_decode_attention(const float* q_input, const std::uint16_t* q_weight, std::size_t q_stride,
+                                     const float* k_input, const std::uint16_t* k_weight, std::size_t k_stride,
+                                     const float* v_input, unsigned rotary, const float* cos_table,
+                                     const float* sin_table, std::size_t table_positions, std::uint16_t* key_cache,
+                                     std::uint16_t* value_cache, std::size_t capacity, std::uint64_t position,
+                                     const std::uint64_t* device_position, unsigned q_heads, unsigned kv_heads,
+                                     std::uint16_t* output, void* scratch, std::size_t scratch_bytes, void* stream) {
+  GFXB_REQUIRE(q_heads != 0 && capacity != 0 && scratch != nullptr &&
+                   scratch_bytes >= gfxb_decode_attention_scratch_bytes(q_heads, capacity),
+               "decode attention scratch is too small");
+  GFXB_REQUIRE(q_stride <= 0xffffffffull && k_stride <= 0xffffffffull, "row strides exceed 32 bits");
+  GFXB_REQUIRE(device_position != nullptr || (position < capacity && position < table_positions),
+               "position is outside the cache or the RoPE table");
+  AttentionDecodeArgs d;
+  QkRopeArgs& r = d.rope;
+  r.q_input = q_input;
+  r.q_weight = q_weight;
+  r.k_input = k_input;
+  r.k_weight = k_weight;
+  r.v_input = v_input;
+  r.key_cache = as_half(key_cache);
+  r.value_cache = as_half(value_cache);
+  r.capacity = capacity;
+  r.q_heads = q_heads;
+  r.k_heads = kv_heads;
+  r.q_stride = static_cast<std::uint32_t>(q_stride);
+  r.k_stride = static_cast<std::uint32_t>(k_stride);
+  r.rotary = rotary;
+  r.cos_table = cos_table;
+  r.sin_table = sin_table;
+  r.table_positions = table_positions;
+  r.base_position = position;
+  r.device_base_position = device_position;
+  AttentionArgs& a = d.attention;
+  a.gate = q_input;
+  a.key_cache = r.key_cache;
+  a.value_cache = r.value_cache;
+  a.output = as_half(output);
+  a.partials = static_cast<float*>(scratch);
+  a.max_chunks = static_cast<std::uint32_t>((capacity + kAttentionChunk - 1) / kAttentionChunk);
+  a.capacity = capacity;
+  a.base_token_count = position + 1;
+  a.device_base_position = device_position;
+  a.q_heads = q_heads;
+  a.kv_heads = kv_heads;
+  d.tickets = reinterpret_cast<std::uint32_t*>(static_cast<std::uint8_t*>(scratch) +
+                                               attention_partial_bytes(q_heads, capacity, 1));
+  return launch_attention_decode(d, as_stream(stream));
+}
+
 extern "C" std::size_t gfxb_argmax_scratch_bytes(unsigned batch) { return argmax_scratch_bytes(batch); }
 
 extern "C" int gfxb_argmax(const float* logits, const std::uint32_t* token_ids, std::uint32_t* tokens,

@@ -279,6 +279,26 @@ __device__ __forceinline__ void mbar_init(std::uint64_t* bar, std::uint32_t coun
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
 }
 
+// 16-byte asynchronous global -> shared copy (L2 only), 16-byte aligned addresses.
+__device__ __forceinline__ void cp_async_16(void* shared_dst, const void* global_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(shared_dst)), "l"(global_src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// Wait until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// The mbarrier counts one arrival of this thread once all of its earlier
+// cp.async copies have landed (the barrier is initialised with one expected
+// arrival per thread).
+__device__ __forceinline__ void cp_async_arrive_noinc(std::uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

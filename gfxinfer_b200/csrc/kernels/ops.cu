@@ -463,21 +463,23 @@ __global__ __launch_bounds__(256) void attention_chunk_kernel(AttentionArgs args
   __half* keys = reinterpret_cast<__half*>(stage);
   __half* values = keys + kChunk * 256u;
   if (threadIdx.x == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+    mbar_init(&bars[0], blockDim.x);
+    mbar_init(&bars[1], blockDim.x);
     fence_mbar_init();
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    mbar_expect_tx(&bars[0], n * 512u);
-    mbar_expect_tx(&bars[1], n * 512u);
-  }
+  // the chunk's key rows, then its value rows (512 bytes each), copied 16 bytes per thread
+  // (consecutive threads take consecutive pieces of a row); each thread's copies arrive on
+  // the rows' barrier as they land
   const std::size_t row_stride = static_cast<std::size_t>(args.kv_heads) * 256u;
-  for (std::uint32_t i = threadIdx.x; i < 2u * n; i += blockDim.x) {
-    const bool is_value = i >= n;
-    const std::uint32_t row = is_value ? i - n : i;
-    const __half* source = (is_value ? args.value_cache : args.key_cache) + (begin + row) * row_stride + kvh * 256u;
-    bulk_g2s((is_value ? values : keys) + row * 256u, source, 512u, &bars[is_value ? 1 : 0]);
+  for (int which = 0; which < 2; ++which) {
+    const __half* cache = which == 0 ? args.key_cache : args.value_cache;
+    __half* dest = which == 0 ? keys : values;
+    for (std::uint32_t i = threadIdx.x; i < n * 32u; i += blockDim.x) {
+      const std::uint32_t row = i >> 5, piece = i & 31u;
+      cp_async_16(dest + row * 256u + piece * 8u, cache + (begin + row) * row_stride + kvh * 256u + piece * 8u);
+    }
+    cp_async_arrive_noinc(&bars[which]);
   }
   if (warp < group) {
     const unsigned h = kvh * group + warp;
@@ -508,6 +510,229 @@ __global__ __launch_bounds__(256) void attention_merge_kernel(AttentionArgs args
   __shared__ float pack_max[2][4];
   __shared__ int pack_sum[2][4];
   attention_merge_head(args, h, token, d, chunks, BlockSync{}, pack_max, pack_sum);
+}
+
+// ---------------------------------------------------------------------------
+// Single-token decode attention in one launch: the Q/K RMSNorm + RoPE, the
+// KV append, the chunked online softmax and the merge. One CTA per (chunk of
+// 128 positions, query head), so a head's chunk is spread over the whole CTA
+// instead of one warp:
+//  - the CTA normalises and rotates its query head; the CTA of the last chunk
+//    also builds the new key/value row in shared memory (and one CTA per KV
+//    head appends it to the cache), while the chunk's cached rows land by
+//    cp.async;
+//  - warp w scores positions 16w..16w+15: lane l runs the same 8-term fma
+//    chain over dims 8l..8l+7 for each, and a transposed butterfly (each
+//    exchange halves the positions a lane carries) adds the 32 lane partials
+//    in the xor tree's pairs, 31 shuffles for 16 scores instead of 80;
+//  - 128 threads scan the exact prefix maximum and form the rescale factors;
+//  - thread t runs the accumulation chains of dims 2t and 2t+1 (thread 128
+//    the denominator's);
+//  - with one chunk the CTA finishes the head; otherwise the last CTA of the
+//    head to arrive (ticket counter) merges the partials in ascending chunk
+//    order.
+// Every float operation and its order is that of qk_norm_rope_kernel,
+// attention_chunk_kernel and attention_merge_kernel, so the outputs and the
+// cache rows are bit-identical to the three-launch path.
+// ---------------------------------------------------------------------------
+
+constexpr std::uint32_t kDecodeStageBytes = 2u * kChunk * 256u * 2u;  // the chunk's key and value rows
+
+__global__ __launch_bounds__(256) void attention_decode_kernel(const AttentionDecodeArgs args) {
+  extern __shared__ __align__(128) std::uint8_t stage[];
+  __shared__ float normalized[256];
+  __shared__ float warp_sums[8];
+  __shared__ __align__(16) float query[256];
+  __shared__ float scores[kChunk];
+  __shared__ __align__(8) float2 rescale[kChunk];  // (alpha, beta) of each position
+  __shared__ float warp_max[kChunk / 32u];
+  __shared__ float head_max, head_den;
+  __shared__ float pack_max[2][4];
+  __shared__ int pack_sum[2][4];
+  __shared__ bool merge_here;
+  pdl_trigger();
+  pdl_wait();
+  const QkRopeArgs& R = args.rope;
+  const AttentionArgs& A = args.attention;
+  const unsigned chunk = blockIdx.x, h = blockIdx.y;
+  const unsigned group = A.q_heads / A.kv_heads, kvh = h / group;
+  const unsigned tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+  const std::uint64_t count =
+      A.device_base_position != nullptr ? *A.device_base_position + 1u : A.base_token_count;
+  const std::uint64_t position = count - 1u;
+  const std::uint32_t chunks = static_cast<std::uint32_t>((count + kChunk - 1) / kChunk);
+  if (chunk >= chunks) return;
+  if (count > A.capacity) {
+    if (tid == 0 && chunk == 0) atomicOr(&g_ops_error, 4u | 8u);
+    return;
+  }
+  const std::uint64_t begin = static_cast<std::uint64_t>(chunk) * kChunk;
+  const std::uint32_t n = static_cast<std::uint32_t>(min(static_cast<std::uint64_t>(kChunk), count - begin));
+  const bool holds_new = chunk + 1u == chunks;  // row n - 1 is `position`
+  const std::uint32_t cached = holds_new ? n - 1u : n;
+  __half* keys = reinterpret_cast<__half*>(stage);
+  __half* values = keys + kChunk * 256u;
+  {
+    const std::size_t row_stride = static_cast<std::size_t>(A.kv_heads) * 256u;
+    const std::size_t first = (begin * A.kv_heads + kvh) * 256u;
+    for (std::uint32_t i = tid; i < cached * 32u; i += blockDim.x) {
+      const std::uint32_t row = i >> 5, piece = i & 31u;
+      cp_async_16(keys + row * 256u + piece * 8u, A.key_cache + first + row * row_stride + piece * 8u);
+    }
+    cp_async_commit();
+    for (std::uint32_t i = tid; i < cached * 32u; i += blockDim.x) {
+      const std::uint32_t row = i >> 5, piece = i & 31u;
+      cp_async_16(values + row * 256u + piece * 8u, A.value_cache + first + row * row_stride + piece * 8u);
+    }
+    cp_async_commit();
+  }
+  bool out_of_range = false;
+  query[tid] = h2f(qk_norm_rope_value(ld_cg(R.q_input + static_cast<std::size_t>(h) * R.q_stride + tid), R.q_weight,
+                                      position, R, tid, BlockSync{}, normalized, warp_sums, out_of_range));
+  if (holds_new) {
+    const __half key = qk_norm_rope_value(ld_cg(R.k_input + static_cast<std::size_t>(kvh) * R.k_stride + tid),
+                                          R.k_weight, position, R, tid, BlockSync{}, normalized, warp_sums,
+                                          out_of_range);
+    const __half value = f2h(ld_cg(R.v_input + static_cast<std::size_t>(kvh) * 256u + tid));
+    keys[(n - 1u) * 256u + tid] = key;
+    values[(n - 1u) * 256u + tid] = value;
+    if (h % group == 0) {  // one writer per KV head appends the row
+      const std::size_t slot = (position * A.kv_heads + kvh) * 256u + tid;
+      R.key_cache[slot] = key;
+      R.value_cache[slot] = value;
+    }
+  }
+  if (out_of_range && tid == 0) atomicOr(&g_ops_error, 2u);
+  cp_async_wait<1>();  // this thread's key copies
+  __syncthreads();     // everyone's, the new row and the query
+
+  if (16u * warp < n) {
+    float qf[8];
+    {
+      const float4 q0 = *reinterpret_cast<const float4*>(query + 8u * lane);
+      const float4 q1 = *reinterpret_cast<const float4*>(query + 8u * lane + 4u);
+      qf[0] = q0.x, qf[1] = q0.y, qf[2] = q0.z, qf[3] = q0.w;
+      qf[4] = q1.x, qf[5] = q1.y, qf[6] = q1.z, qf[7] = q1.w;
+    }
+    float part[16];
+#pragma unroll
+    for (unsigned i = 0; i < 16; ++i) {
+      const std::uint32_t p = 16u * warp + i;
+      const uint4 raw = *reinterpret_cast<const uint4*>(keys + (p < n ? p : 0u) * 256u + 8u * lane);
+      const __half* hv = reinterpret_cast<const __half*>(&raw);
+      float sum = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum = fmaf(qf[j], h2f(hv[j]), sum);
+      part[i] = sum;
+    }
+    // transposed xor butterfly: after the exchange at distance d a lane keeps
+    // the half of its positions selected by its lane bit d, summed with the
+    // partner's partials of the same positions (the tree's pair at that level)
+#pragma unroll
+    for (unsigned i = 0; i < 8; ++i) {
+      const bool upper = (lane & 16u) != 0;
+      const float send = upper ? part[i] : part[i + 8];
+      const float keep = upper ? part[i + 8] : part[i];
+      part[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+    }
+#pragma unroll
+    for (unsigned i = 0; i < 4; ++i) {
+      const bool upper = (lane & 8u) != 0;
+      const float send = upper ? part[i] : part[i + 4];
+      const float keep = upper ? part[i + 4] : part[i];
+      part[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+    }
+#pragma unroll
+    for (unsigned i = 0; i < 2; ++i) {
+      const bool upper = (lane & 4u) != 0;
+      const float send = upper ? part[i] : part[i + 2];
+      const float keep = upper ? part[i + 2] : part[i];
+      part[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+    }
+    {
+      const bool upper = (lane & 2u) != 0;
+      const float send = upper ? part[0] : part[1];
+      const float keep = upper ? part[1] : part[0];
+      part[0] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+    }
+    part[0] = __fadd_rn(part[0], __shfl_xor_sync(0xffffffffu, part[0], 1));
+    const std::uint32_t p = 16u * warp + (lane >> 1);  // lane bits 4..1 name the position
+    if ((lane & 1u) == 0 && p < n) scores[p] = __fmul_rn(part[0], 0.0625f);
+  }
+  __syncthreads();
+
+  // exact prefix maximum over the chunk and the rescale factors
+  const float negative_infinity = -__int_as_float(0x7f800000);
+  float score = negative_infinity, inclusive = negative_infinity;
+  if (tid < kChunk) {
+    score = tid < n ? scores[tid] : negative_infinity;
+    inclusive = fmaxf(negative_infinity, score);
+#pragma unroll
+    for (unsigned offset = 1; offset < 32; offset <<= 1) {
+      const float other = __shfl_up_sync(0xffffffffu, inclusive, offset);
+      if (lane >= offset) inclusive = fmaxf(inclusive, other);
+    }
+    if (lane == 31) warp_max[warp] = inclusive;
+  }
+  __syncthreads();
+  if (tid < kChunk) {
+    float before = negative_infinity;
+    for (unsigned w = 0; w < warp; ++w) before = fmaxf(before, warp_max[w]);
+    inclusive = fmaxf(before, inclusive);
+    float previous = __shfl_up_sync(0xffffffffu, inclusive, 1);
+    if (lane == 0) previous = before;
+    if (tid < n) rescale[tid] = make_float2(gx_expf(__fsub_rn(previous, inclusive)), gx_expf(__fsub_rn(score, inclusive)));
+    if (tid + 1u == n) head_max = inclusive;
+  }
+  cp_async_wait<0>();  // this thread's value copies
+  __syncthreads();
+
+  // scalar IEEE operations: packed f32x2 multiplies feeding packed adds are fused
+  // into fma by the assembler, which would change the reference's rounding
+  float2 acc = make_float2(0.0f, 0.0f);
+  float den = 0.0f;
+  if (tid < 128u) {
+    const __half2* column = reinterpret_cast<const __half2*>(values) + tid;  // dims 2 tid, 2 tid + 1
+#pragma unroll 8
+    for (std::uint32_t p = 0; p < n; ++p) {
+      const float2 ab = rescale[p];
+      const float2 v = __half22float2(column[p * 128u]);
+      acc.x = __fadd_rn(__fmul_rn(acc.x, ab.x), __fmul_rn(v.x, ab.y));
+      acc.y = __fadd_rn(__fmul_rn(acc.y, ab.x), __fmul_rn(v.y, ab.y));
+    }
+  } else if (tid == 128u) {
+    for (std::uint32_t p = 0; p < n; ++p) den = __fadd_rn(__fmul_rn(den, rescale[p].x), rescale[p].y);
+  }
+
+  if (chunks == 1u) {
+    if (tid < 128u) {
+      normalized[2u * tid] = acc.x;
+      normalized[2u * tid + 1u] = acc.y;
+    } else if (tid == 128u) {
+      head_den = den;
+    }
+    __syncthreads();
+    attention_finish_head(A, h, 0, tid, normalized[tid], head_den, BlockSync{}, pack_max, pack_sum);
+    return;
+  }
+  float* partial = A.partials + (static_cast<std::size_t>(h) * A.max_chunks + chunk) * 258u;
+  if (tid < 128u) {
+    *reinterpret_cast<float2*>(partial + 2u + 2u * tid) = acc;
+  } else if (tid == 128u) {
+    partial[0] = head_max;
+    partial[1] = den;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const std::uint32_t ticket = atomicAdd(&args.tickets[h], 1u);
+    merge_here = ticket + 1u == chunks;
+    if (merge_here) atomicExch(&args.tickets[h], 0u);  // every chunk of this launch has counted
+  }
+  __syncthreads();
+  if (!merge_here) return;
+  __threadfence();
+  attention_merge_head(A, h, 0, tid, chunks, BlockSync{}, pack_max, pack_sum);
 }
 
 // ---------------------------------------------------------------------------
@@ -647,6 +872,15 @@ int launch_gdn_conv(const GdnConvArgs& args, cudaStream_t stream) {
   }
   launch_kernel(gdn_conv_kernel, dim3((args.channels + 255u) / 256u), dim3(256), 0, stream, 0, args);
   return launch_status("GDN convolution launch failed");
+}
+
+// GFXB_ATTENTION_FUSED=0 keeps single-token attention on the three-launch path (for A/B timing).
+bool attention_decode_enabled() {
+  static const bool enabled = [] {
+    const char* value = std::getenv("GFXB_ATTENTION_FUSED");
+    return value == nullptr || value[0] != '0';
+  }();
+  return enabled;
 }
 
 // GFXB_GDN_PARTS=0 keeps single-token steps on the one-CTA-per-head kernel (for A/B timing).
@@ -799,6 +1033,42 @@ int launch_attention(const AttentionArgs& args, unsigned batch, cudaStream_t str
   if (status != GFXB_OK) return status;
   launch_kernel(attention_merge_kernel, dim3(dim3(args.q_heads, batch)), dim3(256), 0, stream, 0, args);
   return launch_status("attention merge launch failed");
+}
+
+int launch_attention_decode(const AttentionDecodeArgs& args, cudaStream_t stream) {
+  const QkRopeArgs& r = args.rope;
+  const AttentionArgs& a = args.attention;
+  if (r.q_input == nullptr || r.q_weight == nullptr || r.k_input == nullptr || r.k_weight == nullptr ||
+      r.v_input == nullptr || r.key_cache == nullptr || r.value_cache == nullptr || r.cos_table == nullptr ||
+      r.sin_table == nullptr || r.q_stride < 256 || r.k_stride < 256 || r.rotary == 0 || r.rotary > 256 ||
+      (r.rotary & 1u) != 0 || a.gate == nullptr || a.output == nullptr || a.partials == nullptr ||
+      args.tickets == nullptr || a.kv_heads == 0 || a.q_heads % a.kv_heads != 0 || r.q_heads != a.q_heads ||
+      r.k_heads != a.kv_heads || a.key_cache != r.key_cache || a.value_cache != r.value_cache ||
+      a.capacity != r.capacity || a.device_base_position != r.device_base_position) {
+    return fail(GFXB_INVALID_ARGUMENT, "invalid single-token attention arguments");
+  }
+  if (a.max_chunks < (a.capacity + kChunk - 1) / kChunk) {
+    return fail(GFXB_INVALID_ARGUMENT, "attention partial buffer is too small for the capacity");
+  }
+  if (a.device_base_position == nullptr &&
+      (a.base_token_count == 0 || a.base_token_count > a.capacity || r.base_position + 1u != a.base_token_count)) {
+    return fail(GFXB_INVALID_ARGUMENT, "attention token count exceeds the cache capacity");
+  }
+  const std::uint32_t grid_chunks = a.device_base_position != nullptr
+                                        ? a.max_chunks
+                                        : static_cast<std::uint32_t>((a.base_token_count + kChunk - 1) / kChunk);
+  static DeviceOnce configured;
+  GFXB_TRY(configured.run([](int) {
+    const cudaError_t error = cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(kDecodeStageBytes));
+    if (error != cudaSuccess) {
+      set_error_cuda(error, "attention shared-memory configuration failed");
+      return static_cast<int>(GFXB_CUDA_ERROR);
+    }
+    return static_cast<int>(GFXB_OK);
+  }));
+  launch_kernel(attention_decode_kernel, dim3(grid_chunks, a.q_heads), dim3(256), kDecodeStageBytes, stream, 0, args);
+  return launch_status("single-token attention launch failed");
 }
 
 std::size_t argmax_scratch_bytes(unsigned batch) {

@@ -142,6 +142,16 @@ struct AttentionArgs {
   std::int32_t* act_sums = nullptr;
 };
 
+// Single-token decode attention: the Q/K RMSNorm + RoPE with the KV append
+// (rope) and the gated attention over the cache (attention) in one launch.
+// `tickets` holds one zero-initialised counter per query head; each launch
+// leaves it at zero again.
+struct AttentionDecodeArgs {
+  QkRopeArgs rope;
+  AttentionArgs attention;
+  std::uint32_t* tickets = nullptr;
+};
+
 struct ArgmaxArgs {
   const float* logits = nullptr;
   std::size_t row_stride = 0;
@@ -160,6 +170,8 @@ int launch_gdn_restore(const GdnRestoreArgs& args, cudaStream_t stream);
 int launch_qk_rope(const QkRopeArgs& args, unsigned batch, cudaStream_t stream);
 std::size_t attention_partial_bytes(unsigned q_heads, std::size_t capacity, unsigned batch);
 int launch_attention(const AttentionArgs& args, unsigned batch, cudaStream_t stream);
+int launch_attention_decode(const AttentionDecodeArgs& args, cudaStream_t stream);
+bool attention_decode_enabled();
 std::size_t argmax_scratch_bytes(unsigned batch);
 int launch_argmax(const ArgmaxArgs& args, unsigned batch, cudaStream_t stream);
 int launch_float_to_half(const float* input, __half* output, std::size_t n, cudaStream_t stream);

@@ -912,6 +912,11 @@ __device__ __forceinline__ void attention_chunk_warp(const __half* q_row, const 
 // gate, fp16 output and (optionally) the o_proj activation pack: 256 threads,
 // thread d owns output dimension d.
 template <class Sync>
+__device__ __forceinline__ void attention_finish_head(const AttentionArgs& args, unsigned h, unsigned token, unsigned d,
+                                                      float Acc, float Den, Sync sync, float (*pack_max)[4],
+                                                      int (*pack_sum)[4]);
+
+template <class Sync>
 __device__ __forceinline__ void attention_merge_head(const AttentionArgs& args, unsigned h, unsigned token, unsigned d,
                                                      std::uint32_t chunks, Sync sync, float (*pack_max)[4],
                                                      int (*pack_sum)[4]) {
@@ -927,6 +932,16 @@ __device__ __forceinline__ void attention_merge_head(const AttentionArgs& args, 
     Acc = __fadd_rn(__fmul_rn(Acc, a1), __fmul_rn(ld_cg(p + 2 + d), a2));
     M = next;
   }
+  attention_finish_head(args, h, token, d, Acc, Den, sync, pack_max, pack_sum);
+}
+
+// Output element d of query head h from its merged accumulator and
+// denominator: Acc / Den times the sigmoid gate, fp16, and (optionally) the
+// o_proj activation pack. 256 threads, thread d owns dimension d.
+template <class Sync>
+__device__ __forceinline__ void attention_finish_head(const AttentionArgs& args, unsigned h, unsigned token, unsigned d,
+                                                      float Acc, float Den, Sync sync, float (*pack_max)[4],
+                                                      int (*pack_sum)[4]) {
   const float gate = ld_cg(args.gate + (static_cast<std::size_t>(token) * args.q_heads + h) * 512u + 256u + d);
   const __half y = f2h(__fmul_rn(__fdiv_rn(Acc, Den), gx_sigmoid(gate)));
   args.output[(static_cast<std::size_t>(token) * args.q_heads + h) * 256u + d] = y;

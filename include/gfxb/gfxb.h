@@ -247,6 +247,23 @@ int gfxb_gated_attention_static_scratch(const uint16_t* query, const float* gate
                                         size_t base_token_count, const uint64_t* device_base_position,
                                         size_t capacity, unsigned q_heads, unsigned kv_heads, unsigned batch,
                                         void* stream);
+/* Scratch (bytes) needed by gfxb_decode_attention: the chunk partials and one
+ * merge counter per query head. */
+size_t gfxb_decode_attention_scratch_bytes(unsigned q_heads, size_t capacity);
+/* Single-token decode attention in one launch: the Q/K RMSNorm(1+w) + NeoX
+ * RoPE of gfxb_qk_rms_norm_rope (batch 1, with the KV append) followed by
+ * gfxb_gated_attention over positions 0..position. Replaces the reference's
+ * launch_qk_norm_rope + launch_gated_attention_decode pair of one decode
+ * step (qwen_ops.hip:599-766); outputs and cache rows are bit-identical to
+ * that pair's. The position is `position`, or *device_position when that is
+ * non-null. Zero-fill the scratch once before the first call: every call
+ * leaves its counters at zero again. */
+int gfxb_decode_attention(const float* q_input, const uint16_t* q_weight, size_t q_stride, const float* k_input,
+                          const uint16_t* k_weight, size_t k_stride, const float* v_input, unsigned rotary,
+                          const float* cos_table, const float* sin_table, size_t table_positions,
+                          uint16_t* key_cache, uint16_t* value_cache, size_t capacity, uint64_t position,
+                          const uint64_t* device_position, unsigned q_heads, unsigned kv_heads,
+                          uint16_t* output, void* scratch, size_t scratch_bytes, void* stream);
 size_t gfxb_argmax_scratch_bytes(unsigned batch);
 /* Replaces launch_argmax(_batch)(_mapped). */
 int gfxb_argmax(const float* logits, const uint32_t* token_ids, uint32_t* tokens, size_t vocabulary_size,

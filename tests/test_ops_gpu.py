@@ -313,6 +313,107 @@ def test_qk_norm_rope_and_kv_append_bit_exact(oracle, lib):
         np.testing.assert_array_equal(values[position + t].cpu().numpy().view(np.float16), v_in[t].astype(np.float16))
 
 
+def _decode_attention_inputs(rng, capacity, q_heads=24, kv_heads=4, spread=1.0):
+    """One decode step's projections and a filled cache; `spread` scales the query/key inputs (and with
+    them the score range, so that the rescale factors underflow for large values)."""
+    q_in = (rng.normal(0, 1, (q_heads, 512)) * spread).astype(np.float32)
+    k_in = (rng.normal(0, 1, (kv_heads, 256)) * spread).astype(np.float32)
+    v_in = rng.normal(0, 1, (kv_heads, 256)).astype(np.float32)
+    qw, kw = _bf16(rng, 256, -0.5, 2.0), _bf16(rng, 256, -0.5, 2.0)
+    keys = (rng.normal(0, 1, (capacity, kv_heads, 256)) * spread).astype(np.float16)
+    values = rng.normal(0, 1, (capacity, kv_heads, 256)).astype(np.float16)
+    return q_in, k_in, v_in, qw, kw, keys, values
+
+
+def _rope(lib, capacity):
+    cos = np.zeros((capacity, 32), np.float32)
+    sin = np.zeros((capacity, 32), np.float32)
+    lib.check(lib.lib().gfxb_rope_table(capacity, 64, ctypes.c_float(1e7), cos.ctypes.data, sin.ctypes.data))
+    return cos, sin
+
+
+def _three_launch_decode(lib, inputs, cos, sin, position, capacity, q_heads=24, kv_heads=4):
+    q_in, k_in, v_in, qw, kw, keys, values = inputs
+    d_keys, d_values = _dev(keys.view(np.int16)), _dev(values.view(np.int16))
+    query = torch.empty((q_heads, 256), dtype=torch.int16, device="cuda")
+    d_q = _dev(q_in)
+    lib.check(lib.lib().gfxb_qk_rms_norm_rope(_p(d_q), _p(_dev(qw)), _p(query), q_heads, 512, _p(_dev(k_in)),
+                                              _p(_dev(kw)), None, kv_heads, 256, 64, _p(_dev(cos)), _p(_dev(sin)),
+                                              capacity, position, None, 1, _p(_dev(v_in)), _p(d_keys),
+                                              _p(d_values), capacity, _stream()))
+    scratch_bytes = lib.lib().gfxb_gated_attention_scratch_bytes(q_heads, capacity, 1)
+    scratch = torch.empty(scratch_bytes, dtype=torch.uint8, device="cuda")
+    out = torch.empty((q_heads, 256), dtype=torch.int16, device="cuda")
+    lib.check(lib.lib().gfxb_gated_attention(_p(query), _p(d_q), _p(d_keys), _p(d_values), _p(out), position + 1,
+                                             None, capacity, q_heads, kv_heads, 1, _p(scratch), scratch_bytes,
+                                             _stream()))
+    torch.cuda.synchronize()
+    return out.cpu().numpy().view(np.uint16), d_keys[position].cpu().numpy(), d_values[position].cpu().numpy()
+
+
+def _fused_decode(lib, inputs, cos, sin, position, capacity, scratch, q_heads=24, kv_heads=4, device_position=None):
+    q_in, k_in, v_in, qw, kw, keys, values = inputs
+    d_keys, d_values = _dev(keys.view(np.int16)), _dev(values.view(np.int16))
+    out = torch.empty((q_heads, 256), dtype=torch.int16, device="cuda")
+    lib.check(lib.lib().gfxb_decode_attention(_p(_dev(q_in)), _p(_dev(qw)), 512, _p(_dev(k_in)), _p(_dev(kw)), 256,
+                                              _p(_dev(v_in)), 64, _p(_dev(cos)), _p(_dev(sin)), capacity, _p(d_keys),
+                                              _p(d_values), capacity, 0 if device_position is not None else position,
+                                              _p(device_position), q_heads, kv_heads, _p(out), _p(scratch),
+                                              scratch.numel(), _stream()))
+    torch.cuda.synchronize()
+    return out.cpu().numpy().view(np.uint16), d_keys[position].cpu().numpy(), d_values[position].cpu().numpy()
+
+
+@pytest.mark.parametrize("spread", [1.0, 4.0])
+def test_decode_attention_equals_three_launch_path(lib, spread):
+    """The single-launch decode attention (norm + RoPE + KV append + attention + merge) against
+    gfxb_qk_rms_norm_rope + gfxb_gated_attention at every chunk shape: one chunk, a chunk boundary,
+    partial and full last chunks, up to 32 chunks at the last cache slot; the output and the appended
+    cache row bit for bit. One zero-filled scratch serves every call (its counters return to zero)."""
+    capacity = 4096
+    cos, sin = _rope(lib, capacity)
+    scratch = torch.zeros(lib.lib().gfxb_decode_attention_scratch_bytes(24, capacity), dtype=torch.uint8,
+                          device="cuda")
+    for position in (0, 1, 63, 64, 107, 108, 127, 128, 129, 255, 256, 300, 1000, 3839, 3840, 3947, 3948, 4095):
+        inputs = _decode_attention_inputs(np.random.default_rng(position), capacity, spread=spread)
+        want = _three_launch_decode(lib, inputs, cos, sin, position, capacity)
+        got = _fused_decode(lib, inputs, cos, sin, position, capacity, scratch)
+        for g, w in zip(got, want):
+            np.testing.assert_array_equal(g, w, err_msg=f"position {position}")
+    tickets = scratch[-24 * 4:].cpu().numpy()
+    assert not tickets.any()
+
+
+def test_decode_attention_device_position_bit_exact(oracle, lib):
+    """The graph form (position read from device memory, grid sized by the capacity) against the
+    oracle's RoPE and attention."""
+    capacity, position = 2048, 1500
+    cos, sin = _rope(lib, capacity)
+    inputs = _decode_attention_inputs(np.random.default_rng(5), capacity)
+    q_in, k_in, v_in, qw, kw, keys, values = inputs
+    scratch = torch.zeros(lib.lib().gfxb_decode_attention_scratch_bytes(24, capacity), dtype=torch.uint8,
+                          device="cuda")
+    got, got_k, got_v = _fused_decode(lib, inputs, cos, sin, position, capacity, scratch,
+                                      device_position=_dev(np.array([position], np.uint64)))
+    ocos, osin = np.zeros_like(cos), np.zeros_like(sin)
+    oracle.lib.or_rope_table(capacity, 64, 1e7, _ptr(ocos), _ptr(osin))
+    want_q = np.zeros((24, 256), np.uint16)
+    want_k = np.zeros((4, 256), np.uint16)
+    oracle.lib.or_qk_norm_rope(_ptr(_host(q_in)), 512, _ptr(qw), 24, position, _ptr(ocos), _ptr(osin), 64,
+                               _ptr(want_q))
+    oracle.lib.or_qk_norm_rope(_ptr(_host(k_in)), 256, _ptr(kw), 4, position, _ptr(ocos), _ptr(osin), 64, _ptr(want_k))
+    np.testing.assert_array_equal(got_k.view(np.uint16), want_k)
+    np.testing.assert_array_equal(got_v.view(np.float16), v_in.astype(np.float16))
+    cache_k = keys.copy()
+    cache_k[position] = want_k.view(np.float16)
+    cache_v = values.copy()
+    cache_v[position] = v_in.astype(np.float16)
+    want = np.zeros((24, 256), np.uint16)
+    oracle.lib.or_gated_attention(_ptr(_host(want_q.view(np.float16))), _ptr(_host(q_in)), _ptr(cache_k),
+                                  _ptr(cache_v), position + 1, 24, 4, _ptr(want))
+    np.testing.assert_array_equal(got, want)
+
+
 @pytest.mark.parametrize("bits", [4, 8])
 def test_residual_norm_pack_bit_exact(oracle, lib, bits):
     rng = np.random.default_rng(bits)
