@@ -191,6 +191,16 @@ __device__ __forceinline__ void mma_s8_16832(int (&c)[4], const std::uint32_t (&
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// The same mma with a zero accumulator input (no register clearing).
+__device__ __forceinline__ void mma_s8_16832_zero(int (&d)[4], const std::uint32_t (&a)[4], std::uint32_t b0,
+                                                  std::uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
 inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
 
 // ---- per-device set-up -------------------------------------------------------
@@ -329,6 +339,30 @@ __device__ __forceinline__ bool mbar_try_wait(std::uint64_t* bar, std::uint32_t 
   return done != 0;
 }
 
+// Non-blocking test of a phase (test_wait never suspends the thread). For
+// phases completed by other threads' arrivals, local or remote, whose waiters
+// are not reliably woken before a suspension expires.
+__device__ __forceinline__ bool mbar_poll(std::uint64_t* bar, std::uint32_t parity) {
+  std::uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_poll_cluster(std::uint64_t* bar, std::uint32_t parity) {
+  std::uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Every wait is bounded: on expiry the kernel records kDeviceErrorTimeout in
 // `error` (when given) and the caller skips the work instead of hanging.
 constexpr std::uint32_t kDeviceErrorTimeout = 1u;
@@ -340,6 +374,34 @@ __device__ __forceinline__ bool mbar_wait_bounded(std::uint64_t* bar, std::uint3
     if (mbar_try_wait(bar, parity)) return true;
   }
   if (error != nullptr) atomicOr(error, kDeviceErrorTimeout);
+  return false;
+}
+
+constexpr std::uint32_t kPollLimit = 1u << 26;
+
+__device__ __forceinline__ bool mbar_poll_bounded(std::uint64_t* bar, std::uint32_t parity, std::uint32_t* error,
+                                                  bool cluster_scope = false) {
+  for (std::uint32_t i = 0; i < kPollLimit; ++i) {
+    if (cluster_scope ? mbar_poll_cluster(bar, parity) : mbar_poll(bar, parity)) return true;
+  }
+  if (error != nullptr) atomicOr(error, kDeviceErrorTimeout);
+  return false;
+}
+
+// Whole-warp bounded wait (every lane calls it): the answer is the same in all
+// lanes, so a warp that gives up leaves its loop together.
+enum class WaitKind { kSuspend, kPoll, kPollCluster };
+
+template <WaitKind Kind>
+__device__ __forceinline__ bool warp_wait_bounded(std::uint64_t* bar, std::uint32_t parity, std::uint32_t* error) {
+  const std::uint32_t limit = Kind == WaitKind::kSuspend ? kWaitLimit : kPollLimit;
+  for (std::uint32_t i = 0; i < limit; ++i) {
+    const bool done = Kind == WaitKind::kSuspend ? mbar_try_wait(bar, parity)
+                      : Kind == WaitKind::kPoll  ? mbar_poll(bar, parity)
+                                                 : mbar_poll_cluster(bar, parity);
+    if (__all_sync(0xffffffffu, done)) return true;
+  }
+  if (error != nullptr && (threadIdx.x & 31u) == 0) atomicOr(error, kDeviceErrorTimeout);
   return false;
 }
 
@@ -379,6 +441,30 @@ __device__ __forceinline__ void st_async_s32(std::uint32_t address, int value, s
                : "memory");
 }
 
+// Plain arrival on this CTA's mbarrier (release at CTA scope).
+__device__ __forceinline__ void mbar_arrive(std::uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Arrival on a cluster peer's mbarrier (address from map_shared_rank).
+__device__ __forceinline__ void mbar_arrive_remote(std::uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before its
+// later asynchronous-proxy (bulk copy) writes to the same memory.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Named barrier over `threads` threads (a multiple of 32) of this CTA.
+__device__ __forceinline__ void named_barrier(std::uint32_t id, std::uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(std::uint64_t* bar, std::uint32_t parity,
+                                                          std::uint32_t* error);
+
 // Wait for a phase completed by peers' st.async (cluster-scope acquire).
 __device__ __forceinline__ bool mbar_try_wait_cluster(std::uint64_t* bar, std::uint32_t parity) {
   std::uint32_t done;
@@ -389,6 +475,15 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(std::uint64_t* bar, std::u
       : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(std::uint64_t* bar, std::uint32_t parity,
+                                                          std::uint32_t* error) {
+  for (std::uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+  }
+  if (error != nullptr) atomicOr(error, kDeviceErrorTimeout);
+  return false;
 }
 
 // Split cluster barrier. A CTA must not touch another CTA's shared memory

@@ -17,6 +17,7 @@
 #include <cstdlib>
 #include <map>
 #include <mutex>
+#include <tuple>
 
 #include "codec.cuh"
 #include "common.cuh"
@@ -719,6 +720,274 @@ __global__ __launch_bounds__(256) void gemv_pipe_kernel(const GemvArgs args, std
   }
 }
 
+// ---------------------------------------------------------------------------
+// Warp-specialised persistent GEMV for one token (the decode regime).
+//
+// A cluster of P CTAs walks the tiles c, c + C, c + 2C, ... (C resident
+// clusters); CTA p owns the 128-column groups [p n, p n + n) of every tile.
+// In each CTA:
+//  - one producer lane streams the CTA's share of each tile's codes through a
+//    ring of S stages (full / empty mbarriers), starting before the previous
+//    kernel has finished;
+//  - eight compute warps (warp w takes the stage's groups w, w + 8, ...) turn
+//    the staged codes into exact int32 group dots against the activation
+//    codes and group sums, which were staged once in shared memory, and put
+//    the dots of token 0 into the cluster leader's dot buffer of the tile:
+//    locally, or by st.async whose bytes count on the leader's dots-full
+//    mbarrier;
+//  - in the leader two chain warps (even and odd tiles) run the reference's
+//    ordered fp32 chain over the tile's groups as soon as its dots are
+//    complete, write the 16 outputs, fetch the scales of the tile D ahead into
+//    the freed slot and hand the dot buffer back to every CTA of the cluster
+//    (a local and P - 1 remote mbarrier arrivals).
+// No warp waits at a CTA barrier inside the loop. The per-group dots and the
+// chain are those of the other GEMV kernels, so every bit is the same.
+// ---------------------------------------------------------------------------
+
+constexpr std::uint32_t kLeanComputeWarps = 8;
+constexpr std::uint32_t kLeanChainWarps = 2;
+constexpr std::uint32_t kLeanThreads = (kLeanComputeWarps + 1u + kLeanChainWarps) * 32u;
+constexpr std::uint32_t kLeanSlots = 3;  // dot buffers / scale slots of the leader
+constexpr std::uint32_t kLeanMaxStages = 8;
+
+struct LeanLayout {
+  std::uint32_t per_part;     // groups per CTA
+  std::uint32_t stage_bytes;  // per_part * block, 128-aligned
+  std::uint32_t stages;
+  std::uint32_t dots_offset;  // [slots][G][16] int32
+  std::uint32_t scales_offset;  // [slots][G][16] fp16
+  std::uint32_t act_offset;   // [per_part][128] int8 activation codes
+  std::uint32_t beta_offset;  // [per_part] int32: beta * group code sum
+  std::uint32_t ascale_offset;  // [G] float activation scales
+  std::uint32_t bar_offset;   // full[S], empty[S], dots_full[D], dots_free[D], scale_full[D]
+  std::uint32_t total;
+};
+
+__host__ __device__ inline LeanLayout lean_layout(int bits, std::uint32_t groups, std::uint32_t parts,
+                                                  std::uint32_t stages) {
+  LeanLayout l{};
+  l.per_part = (groups + parts - 1u) / parts;
+  l.stage_bytes = (l.per_part * static_cast<std::uint32_t>(bits) * 256u + 127u) & ~127u;
+  l.stages = stages;
+  l.dots_offset = stages * l.stage_bytes;
+  l.scales_offset = l.dots_offset + kLeanSlots * groups * 64u;
+  l.act_offset = (l.scales_offset + kLeanSlots * groups * 32u + 15u) & ~15u;
+  l.beta_offset = l.act_offset + l.per_part * kGroup;
+  l.ascale_offset = l.beta_offset + l.per_part * 4u;
+  l.bar_offset = (l.ascale_offset + groups * 4u + 7u) & ~7u;
+  l.total = l.bar_offset + (2u * stages + 3u * kLeanSlots) * 8u;
+  return l;
+}
+
+template <int Bits>
+__global__ __launch_bounds__(kLeanThreads, 2) void gemv_lean_kernel(const GemvArgs args, std::uint32_t total_tiles,
+                                                                     std::uint32_t parts, std::uint32_t stages) {
+  extern __shared__ __align__(128) std::uint8_t smem[];
+  pdl_trigger();
+  const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const std::uint32_t G = args.groups;
+  constexpr std::uint32_t kBlock = Bits * 256u;
+  constexpr int kAlpha = Codec<Bits>::alpha, kBeta = Codec<Bits>::beta;
+  const LeanLayout layout = lean_layout(Bits, G, parts, stages);
+  const std::uint32_t part = parts > 1u ? cluster_ctarank() : 0u;
+  const std::uint32_t clusters = gridDim.x / parts, cluster = blockIdx.x / parts;
+  const std::uint32_t count = cluster < total_tiles ? (total_tiles - cluster + clusters - 1u) / clusters : 0u;
+  const std::uint32_t g_begin = min(G, part * layout.per_part);
+  const std::uint32_t n = min(G, g_begin + layout.per_part) - g_begin;
+  const std::uint32_t remote_bytes = (G - min(G, layout.per_part)) * 64u;  // the peers' dots of one tile
+  {
+    std::uint32_t bad = 0;
+    if (parts > 1u && (cluster_nctarank() != parts || part >= parts)) bad |= kGemvErrorCluster;
+    if (layout.total > dynamic_smem_bytes() || stages > kLeanMaxStages || stages < 2u) bad |= kGemvErrorSmem;
+    if (args.batch != 1u) bad |= kGemvErrorTile;
+    if (bad != 0) {  // every CTA sees the same values: all return together, before any barrier
+      if (threadIdx.x == 0) atomicOr(&g_gemv_error, bad);
+      return;
+    }
+  }
+  std::uint8_t* ring = smem;
+  std::int32_t* dots = reinterpret_cast<std::int32_t*>(smem + layout.dots_offset);
+  __half* tile_scales = reinterpret_cast<__half*>(smem + layout.scales_offset);
+  std::int8_t* act = reinterpret_cast<std::int8_t*>(smem + layout.act_offset);
+  std::int32_t* beta_sums = reinterpret_cast<std::int32_t*>(smem + layout.beta_offset);
+  float* act_scales = reinterpret_cast<float*>(smem + layout.ascale_offset);
+  std::uint64_t* full = reinterpret_cast<std::uint64_t*>(smem + layout.bar_offset);
+  std::uint64_t* empty = full + stages;
+  std::uint64_t* dots_full = empty + stages;
+  std::uint64_t* dots_free = dots_full + kLeanSlots;
+  std::uint64_t* scale_full = dots_free + kLeanSlots;
+  auto tile_of = [&](std::uint32_t i) { return cluster + i * clusters; };
+
+  if (threadIdx.x == 0) {
+    for (std::uint32_t s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kLeanComputeWarps);
+    }
+    for (std::uint32_t d = 0; d < kLeanSlots; ++d) {
+      mbar_init(&dots_full[d], kLeanComputeWarps + 1u);  // the leader's warps + the chain warp's expect-tx
+      mbar_init(&dots_free[d], 1);
+      mbar_init(&scale_full[d], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool leader = part == 0;
+  const bool chain_warp = warp > kLeanComputeWarps;
+  if (chain_warp && leader && lane == 0) {
+    // the first slots: the tiles' scales and the expected peer bytes (before any peer can store)
+    for (std::uint32_t i = warp - kLeanComputeWarps - 1u; i < kLeanSlots && i < count; i += kLeanChainWarps) {
+      std::uint32_t tile = tile_of(i);
+      const MatrixArg m = select_matrix(args, tile);
+      mbar_expect_tx(&scale_full[i], G * 32u);
+      bulk_g2s(tile_scales + static_cast<std::size_t>(i) * G * 16u, m.scales + static_cast<std::size_t>(tile) * G * 16u,
+               G * 32u, &scale_full[i]);
+      mbar_expect_tx(&dots_full[i], remote_bytes);
+    }
+  }
+  __syncwarp();
+  if (parts > 1u) {
+    cluster_arrive_relaxed();  // barriers initialised, first expect-tx posted
+    cluster_wait();
+  }
+
+  if (warp == kLeanComputeWarps) {
+    // producer: the weight ring (no dependence on the previous kernel); the
+    // whole warp waits, lane 0 issues, so the warp stays converged
+    for (std::uint32_t i = 0; i < count; ++i) {
+      const std::uint32_t s = i % stages;
+      if (!warp_wait_bounded<WaitKind::kPoll>(&empty[s], ((i / stages) & 1u) ^ 1u, &g_gemv_error)) break;
+      if (lane == 0) {
+        std::uint32_t tile = tile_of(i);
+        const MatrixArg m = select_matrix(args, tile);
+        mbar_expect_tx(&full[s], n * kBlock);
+        bulk_g2s(ring + s * layout.stage_bytes, m.codes + (static_cast<std::size_t>(tile) * G + g_begin) * kBlock,
+                 n * kBlock, &full[s]);
+      }
+      __syncwarp();
+    }
+  } else if (warp < kLeanComputeWarps) {
+    pdl_wait();
+    {
+      const std::uint32_t act_groups = args.act_stride / kGroup;
+      const uint4* source = reinterpret_cast<const uint4*>(args.act + static_cast<std::size_t>(g_begin) * kGroup);
+      for (std::uint32_t v = threadIdx.x; v < n * 8u; v += kLeanComputeWarps * 32u) {
+        reinterpret_cast<uint4*>(act)[v] = __ldg(source + v);
+      }
+      for (std::uint32_t l = threadIdx.x; l < n; l += kLeanComputeWarps * 32u) {
+        beta_sums[l] = kBeta * __ldg(args.act_sums + g_begin + l);
+      }
+      (void)act_groups;
+    }
+    named_barrier(1, kLeanComputeWarps * 32u);
+    const unsigned gl = lane >> 2, tq = lane & 3u;
+    const std::uint32_t leader_dots = parts > 1u ? map_shared_rank(smem_addr(dots), 0) : 0u;
+    const std::uint32_t leader_full = parts > 1u ? map_shared_rank(smem_addr(dots_full), 0) : 0u;
+    for (std::uint32_t i = 0; i < count; ++i) {
+      const std::uint32_t s = i % stages, d = i % kLeanSlots;
+      if (!warp_wait_bounded<WaitKind::kSuspend>(&full[s], (i / stages) & 1u, &g_gemv_error)) break;
+      if (!warp_wait_bounded<WaitKind::kPollCluster>(&dots_free[d], ((i / kLeanSlots) & 1u) ^ 1u, &g_gemv_error)) break;
+      const std::uint8_t* stage = ring + s * layout.stage_bytes;
+      for (std::uint32_t l = warp; l < n; l += kLeanComputeWarps) {
+        const uint4 b0 = *reinterpret_cast<const uint4*>(act + l * kGroup + tq * 32u);
+        const uint4 b1 = *reinterpret_cast<const uint4*>(act + l * kGroup + tq * 32u + 16u);
+        const int beta_sum = beta_sums[l];
+        LaneWords<Bits> w;
+        load_lane_shared<Bits>(stage + l * kBlock, lane, w);
+        std::uint32_t a[4][4];
+        unpack(w, a);
+        int c[4];
+        mma_s8_16832_zero(c, a[0], b0.x, b0.y);
+        mma_s8_16832(c, a[1], b0.z, b0.w);
+        mma_s8_16832(c, a[2], b1.x, b1.y);
+        mma_s8_16832(c, a[3], b1.z, b1.w);
+        if (tq == 0) {  // token 0: rows gl and gl + 8
+          const std::uint32_t index = (d * G + g_begin + l) * 16u + gl;
+          const int low = kAlpha * c[0] + beta_sum, high = kAlpha * c[2] + beta_sum;
+          if (leader) {
+            dots[index] = low;
+            dots[index + 8u] = high;
+          } else {
+            st_async_s32(leader_dots + index * 4u, low, leader_full + d * 8u);
+            st_async_s32(leader_dots + (index + 8u) * 4u, high, leader_full + d * 8u);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&empty[s]);
+        if (leader) mbar_arrive(&dots_full[d]);
+      }
+    }
+  } else if (leader) {
+    // chain warps: tiles k, k + 2, ... of this cluster
+    pdl_wait();
+    const std::uint32_t k = warp - kLeanComputeWarps - 1u;
+    {
+      const std::uint32_t t = threadIdx.x - (kLeanComputeWarps + 1u) * 32u;
+      for (std::uint32_t g = t; g < G; g += kLeanChainWarps * 32u) act_scales[g] = h2f(args.act_scales[g]);
+    }
+    named_barrier(2, kLeanChainWarps * 32u);
+    for (std::uint32_t i = k; i < count; i += kLeanChainWarps) {
+      const std::uint32_t d = i % kLeanSlots, phase = (i / kLeanSlots) & 1u;
+      if (!warp_wait_bounded<WaitKind::kSuspend>(&scale_full[d], phase, &g_gemv_error)) break;
+      if (!warp_wait_bounded<WaitKind::kPollCluster>(&dots_full[d], phase, &g_gemv_error)) break;
+      std::uint32_t tile = tile_of(i);
+      const MatrixArg m = select_matrix(args, tile);
+      float accumulator = 0.0f;
+      if (lane < 16u) {
+        const std::int32_t* tile_dots = dots + d * G * 16u + lane;
+        const __half* scales = tile_scales + d * G * 16u + lane;
+        std::uint32_t g = 0;
+        for (; g + 8u <= G; g += 8u) {
+          float product[8];
+          int dot[8];
+#pragma unroll
+          for (unsigned j = 0; j < 8; ++j) {
+            product[j] = __fmul_rn(h2f(scales[(g + j) * 16u]), act_scales[g + j]);
+            dot[j] = tile_dots[(g + j) * 16u];
+          }
+#pragma unroll
+          for (unsigned j = 0; j < 8; ++j) accumulator = fmaf(static_cast<float>(dot[j]), product[j], accumulator);
+        }
+        for (; g < G; ++g) {
+          accumulator = fmaf(static_cast<float>(tile_dots[g * 16u]), __fmul_rn(h2f(scales[g * 16u]), act_scales[g]),
+                             accumulator);
+        }
+      }
+      __syncwarp();
+      // hand the slot back before the output stores, so that the releases below
+      // do not wait for them
+      if (lane == 0 && i + kLeanSlots < count) {
+        // slot d now serves tile i + D: its scales, its expected peer bytes, then the buffer goes back
+        std::uint32_t next = tile_of(i + kLeanSlots);
+        const MatrixArg nm = select_matrix(args, next);
+        fence_proxy_async_shared();
+        mbar_expect_tx(&scale_full[d], G * 32u);
+        bulk_g2s(tile_scales + static_cast<std::size_t>(d) * G * 16u, nm.scales + static_cast<std::size_t>(next) * G * 16u,
+                 G * 32u, &scale_full[d]);
+        mbar_expect_tx(&dots_full[d], remote_bytes);
+        mbar_arrive(&dots_free[d]);
+        for (std::uint32_t r = 1; r < parts; ++r) mbar_arrive_remote(map_shared_rank(smem_addr(&dots_free[d]), r));
+      }
+      if (lane < 16u) {
+        const std::size_t index = static_cast<std::size_t>(tile) * 16u + lane;
+        if (m.output_f16) {
+          static_cast<__half*>(m.output)[index] = f2h(accumulator);
+        } else {
+          static_cast<float*>(m.output)[index] = accumulator;
+        }
+      }
+      __syncwarp();
+    }
+  }
+  // No CTA of the cluster leaves while a peer may still address its shared memory.
+  __syncthreads();
+  if (parts > 1u) {
+    cluster_arrive();
+    cluster_wait();
+  }
+}
+
 template <int Bits>
 int launch_pipe(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t stream) {
   const PipeLayout layout = pipe_layout(Bits, args.groups, args.batch);
@@ -856,6 +1125,122 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
                                           config.dynamicSmemBytes, stream, parts, args, parts, chunk);
   if (error != cudaSuccess) {
     set_error_cuda(error, "streaming GEMV launch failed");
+    return GFXB_CUDA_ERROR;
+  }
+  return GFXB_OK;
+}
+
+// Warp-specialised persistent GEMV for one token: two CTAs per SM, the
+// deepest ring that fits. Which shapes take it follows what measured fastest
+// on B200 against the older kernels: P = 1 for very tall matrices (the LM
+// head: 73 -> 60 us alone), P = 2 for small matrices (the output projections:
+// 7.1 -> 6.5 us); decode 199.9 -> 202.0 tok/s with both. Wide K at P = 4 (the
+// MLP down projection) is faster alone (16.5 -> 14.5 us) but slowed the whole
+// decode (192.7 tok/s: its two large CTAs per SM cannot start until the
+// previous kernel has left the SMs), so it is off by default (bit 1 of
+// GFXB_GEMV_LEAN_SHAPES turns it on); other shapes keep the pipelined and
+// streaming kernels, which were faster there. Larger clusters were slower on
+// every shape (each tile waits for its slowest CTA); one CTA per SM (room for
+// the next kernel) lost bandwidth: 163 tok/s.
+struct LeanPlan {
+  std::uint32_t parts = 0, stages = 0, clusters = 0;
+  std::uint32_t smem = 0;
+};
+
+constexpr std::uint32_t kLeanSmemBudget = 110u * 1024u;
+constexpr std::uint32_t kLeanOneCtaSmem = 120u * 1024u;  // occupancy query size: at most one CTA per SM
+
+template <int Bits>
+int lean_plan(const GemvArgs& args, std::uint32_t total_tiles, LeanPlan* out) {
+  static DeviceOnce configured;
+  GFXB_TRY(configured.run([](int) {
+    const cudaError_t error = cudaFuncSetAttribute(gemv_lean_kernel<Bits>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(kLeanOneCtaSmem));
+    if (error != cudaSuccess) {
+      set_error_cuda(error, "persistent GEMV shared-memory configuration failed");
+      return static_cast<int>(GFXB_CUDA_ERROR);
+    }
+    return static_cast<int>(GFXB_OK);
+  }));
+  int device = 0;
+  GFXB_TRY(current_device(&device));
+  static std::mutex plan_mutex;
+  static std::map<std::tuple<int, std::uint32_t, std::uint32_t>, LeanPlan> plans;
+  const auto key = std::make_tuple(device, args.groups, total_tiles);
+  std::lock_guard<std::mutex> lock(plan_mutex);
+  const auto found = plans.find(key);
+  if (found != plans.end()) {
+    *out = found->second;
+    return GFXB_OK;
+  }
+  static const std::uint32_t forced = env_value("GFXB_GEMV_LEAN_PARTS", 0);
+  static const std::uint32_t ctas_per_sm = env_value("GFXB_GEMV_LEAN_CTAS", 2) == 1u ? 1u : 2u;
+  // shape classes that take this kernel (bit 0 very tall, bit 1 wide K, bit 2 small)
+  static const std::uint32_t classes = env_value("GFXB_GEMV_LEAN_SHAPES", 5);
+  std::uint32_t wanted = forced;
+  if (wanted == 0) {
+    if (total_tiles >= 4096u) {
+      wanted = (classes & 1u) != 0 ? 1u : 0u;
+    } else if (args.groups >= 96u) {
+      wanted = (classes & 2u) != 0 ? 4u : 0u;
+    } else if (total_tiles <= 640u) {
+      wanted = (classes & 4u) != 0 ? 2u : 0u;
+    }
+  }
+  LeanPlan best;
+  for (std::uint32_t parts = 1; parts <= 8u && wanted != 0; parts <<= 1) {
+    if (parts != wanted) continue;
+    const std::uint32_t per_part = (args.groups + parts - 1u) / parts;
+    if (parts > 1u && (per_part < 4u || per_part * (parts - 1u) >= args.groups)) continue;
+    std::uint32_t stages = 0;
+    for (std::uint32_t s = kLeanMaxStages; s >= 2u; --s) {
+      if (lean_layout(Bits, args.groups, parts, s).total <= kLeanSmemBudget) {
+        stages = s;
+        break;
+      }
+    }
+    if (stages == 0) continue;
+    const std::uint32_t smem = lean_layout(Bits, args.groups, parts, stages).total;
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(parts);
+    config.blockDim = dim3(kLeanThreads);
+    config.dynamicSmemBytes = ctas_per_sm == 1u ? kLeanOneCtaSmem : smem;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeClusterDimension;
+    attribute[0].val.clusterDim.x = parts;
+    attribute[0].val.clusterDim.y = 1;
+    attribute[0].val.clusterDim.z = 1;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    int clusters = 0;
+    const cudaError_t error = cudaOccupancyMaxActiveClusters(&clusters, gemv_lean_kernel<Bits>, &config);
+    if (error != cudaSuccess || clusters < 1) {
+      cudaGetLastError();
+      continue;
+    }
+    const std::uint32_t c = static_cast<std::uint32_t>(clusters);
+    {
+      best.parts = parts;
+      best.stages = stages;
+      best.clusters = std::min(c, total_tiles);
+      best.smem = smem;
+    }
+  }
+  plans[key] = best;
+  *out = best;
+  return GFXB_OK;
+}
+
+template <int Bits>
+int launch_lean(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t stream) {
+  LeanPlan plan;
+  GFXB_TRY(lean_plan<Bits>(args, total_tiles, &plan));
+  if (plan.parts == 0) return kNoStreamPath;
+  const cudaError_t error = launch_kernel(gemv_lean_kernel<Bits>, dim3(plan.clusters * plan.parts), dim3(kLeanThreads),
+                                          plan.smem, stream, plan.parts > 1u ? plan.parts : 0u, args, total_tiles,
+                                          plan.parts, plan.stages);
+  if (error != cudaSuccess) {
+    set_error_cuda(error, "persistent GEMV launch failed");
     return GFXB_CUDA_ERROR;
   }
   return GFXB_OK;
@@ -1645,6 +2030,13 @@ int lowbit_gemv(int format, const gfxb_gemv_matrix* matrices, unsigned matrix_co
   const unsigned grid = static_cast<unsigned>(total_tiles);
   static const bool force_v1 = env_value("GFXB_GEMV_V1", 0) != 0;
   static const std::uint32_t pipe_mode = env_value("GFXB_GEMV_PIPE", 1);  // 0: never, 1: tall matrices, 2: always
+  static const bool lean = env_value("GFXB_GEMV_LEAN", 1) != 0;           // the persistent kernel for one token
+  if (batch == 1 && lean && !force_v1) {
+    const int status = bits == 2   ? launch_lean<2>(args, grid, stream)
+                       : bits == 3 ? launch_lean<3>(args, grid, stream)
+                                   : launch_lean<4>(args, grid, stream);
+    if (status != kNoStreamPath) return status;
+  }
   if (batch <= 8 && batch < tuning().tall_cascade && !force_v1 && pipe_mode != 0) {
     // tall matrices (one CTA per tile would need several waves) whose two stages leave room for two CTAs per SM
     const PipeLayout pipe = pipe_layout(bits, args.groups, batch);

@@ -1,8 +1,9 @@
 """Child process of test_cluster_splits_bit_exact (tests/test_gemv_gpu.py).
 
 Runs the GEMV over shapes whose group counts do not divide evenly by the
-cluster size (or by the pipelined kernel's K-chunks) that the parent chose
-through the environment, and compares every output bit with the oracle.
+cluster size (or by the pipelined kernel's K-chunks, or the persistent
+single-token kernel's parts) that the parent chose through the environment,
+and compares every output bit with the oracle.
 Exit status 0 when all match.
 """
 import os
@@ -25,6 +26,11 @@ def main() -> int:
     cases = [(W3, 48, 17 * 128, 1), (W4, 32, 3 * 128, 8), (W2, 160, 40 * 128, 5), (W3, 16, 128, 2),
              (W4, 48, 40 * 128, 2), (W3, 32, 136 * 128, 3), (W2, 16, 131 * 128, 8), (W3, 48, 17 * 128, 12),
              (W4, 32, 40 * 128, 16)]
+    if os.environ.get("GFXB_GEMV_LEAN_PARTS"):
+        # one token through the persistent kernel: several rounds of tiles per cluster (the ring and the
+        # dot slots wrap), uneven parts, multi-round small matrices
+        cases += [(W3, 4800, 40 * 128, 1), (W4, 2048, 48 * 128, 1), (W3, 640, 136 * 128, 1),
+                  (W2, 1024, 131 * 128, 1), (W4, 48, 40 * 128, 1), (W3, 3216, 20 * 128, 1)]
     for fmt, rows, cols, batch in cases:
         rng = np.random.default_rng(rows * 7 + cols + batch)
         w = rng.normal(0.0, 0.02, size=(rows, cols)).astype(np.float32)

@@ -274,17 +274,23 @@ def test_wide_k_bit_exact(oracle, ops, fmt, rows, cols, batch, bits):
     np.testing.assert_array_equal(got.view(np.uint32), oracle.gemv(logical, scales16, a, a_scales).view(np.uint32))
 
 
-@pytest.mark.parametrize("parts", ["1", "2", "4", "8", "pipe"])
+@pytest.mark.parametrize("parts", ["1", "2", "4", "8", "pipe", "lean1", "lean2", "lean4", "lean8"])
 def test_cluster_splits_bit_exact(parts):
-    """Every cluster size of the streaming GEMV, and the pipelined GEMV on every
-    shape, in a fresh process (the choice is read once per process): G = 17
-    over 8 CTAs leaves two CTAs without groups; G = 136 and 131 stream each
-    tile in several K-chunks."""
+    """Every cluster size of the streaming GEMV, the pipelined GEMV on every
+    shape, and every split of the persistent single-token GEMV, in a fresh
+    process (the choice is read once per process): G = 17 over 8 CTAs leaves
+    two CTAs without groups; G = 136 and 131 stream each tile in several
+    K-chunks; the persistent kernel runs several rounds of tiles per cluster."""
     import os
     import subprocess
     import sys
 
-    env = dict(os.environ, GFXB_GEMV_PIPE="2") if parts == "pipe" else dict(os.environ, GFXB_GEMV_PARTS=parts)
+    if parts == "pipe":
+        env = dict(os.environ, GFXB_GEMV_PIPE="2", GFXB_GEMV_LEAN="0")
+    elif parts.startswith("lean"):
+        env = dict(os.environ, GFXB_GEMV_LEAN_PARTS=parts[4:])
+    else:
+        env = dict(os.environ, GFXB_GEMV_PARTS=parts, GFXB_GEMV_LEAN="0")
     child = os.path.join(os.path.dirname(os.path.abspath(__file__)), "gemv_split_child.py")
     result = subprocess.run([sys.executable, child], env=env, capture_output=True, text=True, timeout=600)
     assert result.returncode == 0, result.stdout + result.stderr
