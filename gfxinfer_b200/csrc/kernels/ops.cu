@@ -209,6 +209,10 @@ __global__ __launch_bounds__(kGdnPartThreads) void gdn_parts_kernel(GdnRecurrent
   const float neg_exp_a_log = -gx_expf(bf2f(args.a_log[vh]));
   const float dt_bias = bf2f(args.dt_bias[vh]);
   const float norm_weight = part == 0 ? bf2f(args.norm_weight[t]) : 0.0f;
+  ConvChannel cq, ck, cv;
+  cq.load_weights(args.conv, q_channel);
+  ck.load_weights(args.conv, k_channel);
+  if (warp == 0) cv.load_weights(args.conv, v_channel);
   asm volatile("prefetch.global.L2 [%0];" ::"l"(initial + static_cast<std::size_t>(t) * kGdnHead +
                                                 part * kGdnPartColumns)
                : "memory");
@@ -218,19 +222,24 @@ __global__ __launch_bounds__(kGdnPartThreads) void gdn_parts_kernel(GdnRecurrent
     mbar_expect_tx(&sc.bar, (kGdnParts - 1u) * kGdnPartColumns * 4u);
   }
   pdl_wait();
+  // every input of the step is requested at once (one memory round trip instead of one per use)
+  const float xq = ld_cg(args.conv.projected + q_channel);
+  const float xk = ld_cg(args.conv.projected + k_channel);
+  const float xv = warp == 0 ? ld_cg(args.conv.projected + v_channel) : 0.0f;
+  const float z = part == 0 ? ld_cg(args.z + static_cast<std::size_t>(vh) * kGdnHead + t) : 0.0f;
+  const float a_in = t == 0 ? ld_cg(args.a + vh) : 0.0f;
+  const float b_in = t == 0 ? ld_cg(args.b + vh) : 0.0f;
+  cq.load_taps(args.conv, q_channel);
+  ck.load_taps(args.conv, k_channel);
+  if (warp == 0) cv.load_taps(args.conv, v_channel);
   float S[kGdnPartColumns];
 #pragma unroll
   for (unsigned j = 0; j < kGdnPartColumns; ++j) S[j] = initial[(warp * kGdnPartColumns + j) * kGdnHead + column];
-  ConvChannel cq, ck, cv;
-  cq.load(args.conv, q_channel);
-  ck.load(args.conv, k_channel);
-  if (warp == 0) cv.load(args.conv, v_channel);
-  const float z = part == 0 ? ld_cg(args.z + static_cast<std::size_t>(vh) * kGdnHead + t) : 0.0f;
   cluster_arrive();  // this CTA has read the conv taps; part 0's barrier is initialised
   // q/k conv and norms (element t of the key head), the value conv of this part's columns, the gates
-  const float q = cq.step(args.conv, q_channel, false);
-  const float k = ck.step(args.conv, k_channel, false);
-  if (warp == 0) sc.value[lane] = cv.step(args.conv, v_channel, false);
+  const float q = cq.step_input(xq);
+  const float k = ck.step_input(xk);
+  if (warp == 0) sc.value[lane] = cv.step_input(xv);
   const float qs = warp_sum_down(__fmul_rn(q, q));
   const float ks = warp_sum_down(__fmul_rn(k, k));
   if (lane == 0) {
@@ -238,10 +247,10 @@ __global__ __launch_bounds__(kGdnPartThreads) void gdn_parts_kernel(GdnRecurrent
     sc.sums[1][warp] = ks;
   }
   if (t == 0) {
-    const float a_value = __fadd_rn(ld_cg(args.a + vh), dt_bias);
+    const float a_value = __fadd_rn(a_in, dt_bias);
     const float softplus = a_value > 20.0f ? a_value : gx_log1pf(gx_expf(a_value));
     sc.gates[0] = gx_expf(__fmul_rn(neg_exp_a_log, softplus));
-    sc.gates[1] = gx_sigmoid(ld_cg(args.b + vh));
+    sc.gates[1] = gx_sigmoid(b_in);
   }
   __syncthreads();
   {
@@ -269,17 +278,19 @@ __global__ __launch_bounds__(kGdnPartThreads) void gdn_parts_kernel(GdnRecurrent
   __syncthreads();
   const float delta = sc.delta[lane];
 #pragma unroll
-  for (unsigned j = 0; j < kGdnPartColumns; ++j) {
-    S[j] = fmaf(sc.key[row0 + j], delta, S[j]);
-    final_state[(row0 + j) * kGdnHead + column] = S[j];
-  }
-  // mixed = sum over k in row order of S'[k][v] * query[k], warp by warp
+  for (unsigned j = 0; j < kGdnPartColumns; ++j) S[j] = fmaf(sc.key[row0 + j], delta, S[j]);
+  // mixed = sum over k in row order of S'[k][v] * query[k], warp by warp; a warp
+  // stores its rows of the new state while another warp runs the chain (warps
+  // 1-3 during warp 0's turn, warp 0 during warp 1's)
   for (unsigned w = 0; w < 4u; ++w) {
     if (warp == w) {
       float mixed = w == 0 ? 0.0f : sc.carry[lane];
 #pragma unroll
       for (unsigned j = 0; j < kGdnPartColumns; ++j) mixed = fmaf(S[j], sc.query[row0 + j], mixed);
       sc.carry[lane] = mixed;
+    } else if (w == (warp == 0 ? 1u : 0u)) {
+#pragma unroll
+      for (unsigned j = 0; j < kGdnPartColumns; ++j) final_state[(row0 + j) * kGdnHead + column] = S[j];
     }
     __syncthreads();
   }

@@ -378,6 +378,23 @@ struct ConvChannel {
 #pragma unroll
     for (int i = 0; i < 4; ++i) conv.final_state[channel * 4u + i] = taps[i];
   }
+  // the same loads as two 8-byte reads (weights, then taps): the weights never
+  // change and may be read before the dependency wait, the taps may not
+  __device__ __forceinline__ void load_weights(const GdnConvArgs& conv, std::size_t channel) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(conv.weight + channel * 4u);
+    w[0] = bf2f(static_cast<std::uint16_t>(raw.x & 0xffffu));
+    w[1] = bf2f(static_cast<std::uint16_t>(raw.x >> 16));
+    w[2] = bf2f(static_cast<std::uint16_t>(raw.y & 0xffffu));
+    w[3] = bf2f(static_cast<std::uint16_t>(raw.y >> 16));
+  }
+  __device__ __forceinline__ void load_taps(const GdnConvArgs& conv, std::size_t channel) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(conv.initial_state + channel * 4u);
+    const __half* h = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) taps[i] = h[i];
+  }
+  // one token with its projected input already loaded
+  __device__ __forceinline__ float step_input(float projected) { return h2f(gdn_conv_step(taps, w, projected)); }
   // one token: the same step as gdn_conv_kernel, including its log entry
   __device__ __forceinline__ float step(const GdnConvArgs& conv, std::size_t index, bool log) {
     const float y = h2f(gdn_conv_step(taps, w, ld_cg(conv.projected + index)));
