@@ -45,8 +45,9 @@ def _kernels_per_step(cfg: dict, tp: int) -> int:
     gdn = layers - attention
     # see gfxinfer_b200/csrc/host/runtime.cu enqueue_forward: a GDN layer is in-projection GEMV, recurrent step
     # (causal conv inside), out-projection, norm, gate/up, SiLU pack, down, norm; an attention layer has q/k/v,
-    # Q/K norm + RoPE, attention chunk and merge, o_proj, then the same five
-    per_gdn, per_attention = 8, 10
+    # the single-token attention (Q/K norm + RoPE, KV append, chunks and merge in one launch), o_proj, then
+    # the same five
+    per_gdn, per_attention = 8, 8
     head = 1 + 2 + (2 if tp > 1 else 0)  # LM-head GEMV, argmax (2), TP exchange/select
     return 1 + gdn * per_gdn + attention * per_attention + head + 1  # embed+norm ... advance
 

@@ -222,7 +222,7 @@ __host__ __device__ inline StreamLayout stream_layout(int bits, std::uint32_t gr
   return s;
 }
 
-template <int Bits>
+template <int Bits, bool One>  // One: batch 1 (token 0 only: one mma chain, no second-token lanes)
 __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, std::uint32_t parts,
                                                           std::uint32_t chunk) {
   extern __shared__ __align__(128) std::uint8_t smem[];
@@ -307,7 +307,32 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
       st_async_s32(leader_dots + index * 4u, value, leader_bar);
     }
   };
-  for (std::uint32_t local = warp; local < n; local += 8u) {
+  if constexpr (One) {
+    // token 0 only: lanes with tq = 0 hold its column of the mma; the four
+    // k-steps accumulate in one chain (exact integer sums, the same dot)
+    for (std::uint32_t local = warp; local < n; local += 8u) {
+      const std::uint32_t g = g_begin + local;
+      const std::int8_t* ap = args.act + static_cast<std::size_t>(g) * kGroup + tq * 32u;
+      const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(ap));
+      const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(ap + 16));
+      const int beta_sum = tq == 0 ? kBeta * __ldg(args.act_sums + g) : 0;
+      if (!mbar_wait_bounded(&bars[local / chunk], 0, &g_gemv_error)) break;
+      LaneWords<Bits> w;
+      load_lane_shared<Bits>(stage + local * kBlock, lane, w);
+      std::uint32_t a[4][4];
+      unpack(w, a);
+      int c[4];
+      mma_s8_16832_zero(c, a[0], b0.x, b0.y);
+      mma_s8_16832(c, a[1], b0.z, b0.w);
+      mma_s8_16832(c, a[2], b1.x, b1.y);
+      mma_s8_16832(c, a[3], b1.z, b1.w);
+      if (tq == 0) {
+        put(g, gl, 0, kAlpha * c[0] + beta_sum);
+        put(g, gl + 8u, 0, kAlpha * c[2] + beta_sum);
+      }
+    }
+  }
+  for (std::uint32_t local = warp; !One && local < n; local += 8u) {
     const std::uint32_t g = g_begin + local;
     const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * args.act_stride +
                             static_cast<std::size_t>(g) * kGroup + tq * 32u;
@@ -602,7 +627,7 @@ __host__ __device__ inline PipeLayout pipe_layout(int bits, std::uint32_t groups
   return l;
 }
 
-template <int Bits>
+template <int Bits, bool One>  // One: batch 1 (token 0 only: one mma chain, no second-token lanes)
 __global__ __launch_bounds__(256) void gemv_pipe_kernel(const GemvArgs args, std::uint32_t total_tiles) {
   extern __shared__ __align__(128) std::uint8_t smem[];
   pdl_trigger();
@@ -652,7 +677,27 @@ __global__ __launch_bounds__(256) void gemv_pipe_kernel(const GemvArgs args, std
     const __half* tile_scales = reinterpret_cast<const __half*>(base + layout.weight_bytes);
     std::int32_t* dots = reinterpret_cast<std::int32_t*>(base + layout.weight_bytes + layout.scale_bytes);
     const bool ready = mbar_wait_bounded(&bars[stage], (i / kPipeStages) & 1u, &g_gemv_error);
-    if (ready) {
+    if (ready && One) {
+      for (std::uint32_t g = warp; g < G; g += 8u) {
+        const std::int8_t* ap = args.act + static_cast<std::size_t>(g) * kGroup + tq * 32u;
+        const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(ap));
+        const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(ap + 16));
+        const int beta_sum = tq == 0 ? kBeta * __ldg(args.act_sums + g) : 0;
+        LaneWords<Bits> w;
+        load_lane_shared<Bits>(base + g * kBlock, lane, w);
+        std::uint32_t a[4][4];
+        unpack(w, a);
+        int c[4];
+        mma_s8_16832_zero(c, a[0], b0.x, b0.y);
+        mma_s8_16832(c, a[1], b0.z, b0.w);
+        mma_s8_16832(c, a[2], b1.x, b1.y);
+        mma_s8_16832(c, a[3], b1.z, b1.w);
+        if (tq == 0) {
+          dots[g * 16u + gl] = kAlpha * c[0] + beta_sum;
+          dots[g * 16u + gl + 8u] = kAlpha * c[2] + beta_sum;
+        }
+      }
+    } else if (ready) {
       for (std::uint32_t g = warp; g < G; g += 8u) {
         const std::int8_t* ap = args.act + static_cast<std::size_t>(token) * args.act_stride +
                                 static_cast<std::size_t>(g) * kGroup + tq * 32u;
@@ -993,8 +1038,12 @@ int launch_pipe(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t st
   const PipeLayout layout = pipe_layout(Bits, args.groups, args.batch);
   static DeviceOnce configured;
   GFXB_TRY(configured.run([](int) {
-    const cudaError_t error = cudaFuncSetAttribute(gemv_pipe_kernel<Bits>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaError_t error = cudaFuncSetAttribute(gemv_pipe_kernel<Bits, false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (error == cudaSuccess) {
+      error = cudaFuncSetAttribute(gemv_pipe_kernel<Bits, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   200 * 1024);
+    }
     if (error != cudaSuccess) {
       set_error_cuda(error, "pipelined GEMV shared-memory configuration failed");
       return static_cast<int>(GFXB_CUDA_ERROR);
@@ -1016,7 +1065,7 @@ int launch_pipe(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t st
       cached_blocks = found->second;
     } else {
       const cudaError_t error =
-          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&cached_blocks, gemv_pipe_kernel<Bits>, 256, layout.total);
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&cached_blocks, gemv_pipe_kernel<Bits, false>, 256, layout.total);
       if (error != cudaSuccess || cached_blocks < 1) {
         set_error_cuda(error, "pipelined GEMV occupancy query failed");
         return GFXB_CUDA_ERROR;
@@ -1025,8 +1074,11 @@ int launch_pipe(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t st
     }
   }
   const std::uint32_t grid = std::min<std::uint32_t>(total_tiles, static_cast<std::uint32_t>(sms * cached_blocks));
-  const cudaError_t launch = launch_kernel(gemv_pipe_kernel<Bits>, dim3(grid), dim3(256), layout.total, stream, 0u,
-                                           args, total_tiles);
+  const cudaError_t launch =
+      args.batch == 1u ? launch_kernel(gemv_pipe_kernel<Bits, true>, dim3(grid), dim3(256), layout.total, stream, 0u,
+                                       args, total_tiles)
+                       : launch_kernel(gemv_pipe_kernel<Bits, false>, dim3(grid), dim3(256), layout.total, stream, 0u,
+                                       args, total_tiles);
   if (launch != cudaSuccess) {
     set_error_cuda(launch, "pipelined GEMV launch failed");
     return GFXB_CUDA_ERROR;
@@ -1100,8 +1152,12 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
   const StreamLayout layout = stream_layout(Bits, args.groups, parts, args.batch, chunk);
   static DeviceOnce configured;
   GFXB_TRY(configured.run([](int) {
-    const cudaError_t error = cudaFuncSetAttribute(gemv_stream_kernel<Bits>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaError_t error = cudaFuncSetAttribute(gemv_stream_kernel<Bits, false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (error == cudaSuccess) {
+      error = cudaFuncSetAttribute(gemv_stream_kernel<Bits, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   200 * 1024);
+    }
     if (error != cudaSuccess) {
       set_error_cuda(error, "GEMV shared-memory configuration failed");
       return static_cast<int>(GFXB_CUDA_ERROR);
@@ -1121,8 +1177,11 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
   attribute[0].val.clusterDim.z = 1;
   config.attrs = attribute;
   config.numAttrs = 1;
-  const cudaError_t error = launch_kernel(gemv_stream_kernel<Bits>, config.gridDim, config.blockDim,
-                                          config.dynamicSmemBytes, stream, parts, args, parts, chunk);
+  const cudaError_t error =
+      args.batch == 1u ? launch_kernel(gemv_stream_kernel<Bits, true>, config.gridDim, config.blockDim,
+                                       config.dynamicSmemBytes, stream, parts, args, parts, chunk)
+                       : launch_kernel(gemv_stream_kernel<Bits, false>, config.gridDim, config.blockDim,
+                                       config.dynamicSmemBytes, stream, parts, args, parts, chunk);
   if (error != cudaSuccess) {
     set_error_cuda(error, "streaming GEMV launch failed");
     return GFXB_CUDA_ERROR;

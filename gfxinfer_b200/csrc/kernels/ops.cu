@@ -228,7 +228,7 @@ __global__ __launch_bounds__(kGdnPartThreads) void gdn_parts_kernel(GdnRecurrent
   const float xv = warp == 0 ? ld_cg(args.conv.projected + v_channel) : 0.0f;
   const float z = part == 0 ? ld_cg(args.z + static_cast<std::size_t>(vh) * kGdnHead + t) : 0.0f;
   const float a_in = t == 0 ? ld_cg(args.a + vh) : 0.0f;
-  const float b_in = t == 0 ? ld_cg(args.b + vh) : 0.0f;
+  const float b_in = t == 32u ? ld_cg(args.b + vh) : 0.0f;
   cq.load_taps(args.conv, q_channel);
   ck.load_taps(args.conv, k_channel);
   if (warp == 0) cv.load_taps(args.conv, v_channel);
@@ -246,12 +246,12 @@ __global__ __launch_bounds__(kGdnPartThreads) void gdn_parts_kernel(GdnRecurrent
     sc.sums[0][warp] = qs;
     sc.sums[1][warp] = ks;
   }
-  if (t == 0) {
+  if (t == 0) {  // the decay's dependent exp / log1p / exp chain
     const float a_value = __fadd_rn(a_in, dt_bias);
     const float softplus = a_value > 20.0f ? a_value : gx_log1pf(gx_expf(a_value));
     sc.gates[0] = gx_expf(__fmul_rn(neg_exp_a_log, softplus));
-    sc.gates[1] = gx_sigmoid(b_in);
   }
+  if (t == 32u) sc.gates[1] = gx_sigmoid(b_in);  // beta, on another warp in parallel
   __syncthreads();
   {
     const float inv_q = __fmul_rn(inv_sqrt_rn(__fadd_rn(tree_of_eight(sc.sums[0], 4), 1.0e-6f)), 0.08838834764831845f);
