@@ -222,7 +222,10 @@ __host__ __device__ inline StreamLayout stream_layout(int bits, std::uint32_t gr
   return s;
 }
 
-template <int Bits, bool One>  // One: batch 1 (token 0 only: one mma chain, no second-token lanes)
+// One: batch 1 (token 0 only: one mma chain, no second-token lanes). Long: the
+// leader forms the scale products first (wide K; a separate instantiation so
+// that the short-chain one keeps its lower register count and occupancy).
+template <int Bits, bool One, bool Long = false>
 __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, std::uint32_t parts,
                                                           std::uint32_t chunk) {
   extern __shared__ __align__(128) std::uint8_t smem[];
@@ -239,6 +242,7 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   const std::uint32_t g_begin = min(G, part * layout.per_part);
   const std::uint32_t n = min(G, g_begin + layout.per_part) - g_begin;
   const std::uint32_t chunks = (n + chunk - 1u) / chunk;
+  const std::uint32_t chunk_shift = static_cast<std::uint32_t>(__ffs(static_cast<int>(chunk)) - 1);  // chunk: a power of two
 
   std::uint8_t* stage = smem;
   __half* tile_scales = reinterpret_cast<__half*>(smem + layout.weight_bytes);
@@ -316,7 +320,7 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
       const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(ap));
       const uint4 b1 = __ldg(reinterpret_cast<const uint4*>(ap + 16));
       const int beta_sum = tq == 0 ? kBeta * __ldg(args.act_sums + g) : 0;
-      if (!mbar_wait_bounded(&bars[local / chunk], 0, &g_gemv_error)) break;
+      if (!mbar_wait_bounded(&bars[local >> chunk_shift], 0, &g_gemv_error)) break;
       LaneWords<Bits> w;
       load_lane_shared<Bits>(stage + local * kBlock, lane, w);
       std::uint32_t a[4][4];
@@ -342,7 +346,7 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
     const std::uint32_t act_groups = args.act_stride / kGroup;
     const int s0 = t0 < B ? __ldg(args.act_sums + t0 * act_groups + g) : 0;
     const int s1 = t1 < B ? __ldg(args.act_sums + t1 * act_groups + g) : 0;
-    if (!mbar_wait_bounded(&bars[local / chunk], 0, &g_gemv_error)) break;
+    if (!mbar_wait_bounded(&bars[local >> chunk_shift], 0, &g_gemv_error)) break;
     LaneWords<Bits> w;
     load_lane_shared<Bits>(stage + local * kBlock, lane, w);
     std::uint32_t a[4][4];
@@ -363,6 +367,71 @@ __global__ __launch_bounds__(256) void gemv_stream_kernel(const GemvArgs args, s
   }
   if (part != 0) return;
   __syncthreads();  // the leader's own dots and staged activation scales
+  if constexpr (One && Long) {
+    // Long chains (wide K): the whole CTA forms the tile's scale products
+    // (weight scale x activation scale, the chain's multiplier) in the consumed
+    // weight stage while the peers' dots arrive; the 16 chain threads then only
+    // load and fma.
+    float* products = reinterpret_cast<float*>(stage);
+    const bool scales_ready = mbar_wait_bounded(&bars[scale_bar], 0, &g_gemv_error);
+    if (scales_ready) {
+      for (std::uint32_t i = threadIdx.x; i < G * 16u; i += blockDim.x) {
+        products[i] = __fmul_rn(h2f(tile_scales[i]), h2f(act_scale_stage[i >> 4]));
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x >= 16u || !scales_ready) return;
+    if (parts > 1u) {
+      bool arrived = false;  // outlast every peer's bounded waits, as below
+      for (std::uint32_t r = 0; r < max_chunks + 2u && !arrived; ++r) {
+        for (std::uint32_t i = 0; i < kWaitLimit && !arrived; ++i) arrived = mbar_try_wait_cluster(&bars[dots_bar], 0);
+      }
+      if (!arrived) {
+        atomicOr(&g_gemv_error, kDeviceErrorTimeout);
+        return;
+      }
+    }
+    const std::uint32_t row = threadIdx.x;
+    float accumulator = 0.0f;
+    std::uint32_t g = 0;
+    // the next eight groups' operands load while the current eight fma
+    float product[8];
+    int dot[8];
+#pragma unroll
+    for (unsigned i = 0; i < 8; ++i) {
+      const std::uint32_t gi = min(i, G - 1u);
+      product[i] = products[gi * 16u + row];
+      dot[i] = dots[gi * 16u + row];
+    }
+    for (; g + 8u <= G; g += 8u) {
+      float next_product[8];
+      int next_dot[8];
+#pragma unroll
+      for (unsigned i = 0; i < 8; ++i) {
+        const std::uint32_t gi = min(g + 8u + i, G - 1u);
+        next_product[i] = products[gi * 16u + row];
+        next_dot[i] = dots[gi * 16u + row];
+      }
+#pragma unroll
+      for (unsigned i = 0; i < 8; ++i) accumulator = fmaf(static_cast<float>(dot[i]), product[i], accumulator);
+#pragma unroll
+      for (unsigned i = 0; i < 8; ++i) {
+        product[i] = next_product[i];
+        dot[i] = next_dot[i];
+      }
+    }
+#pragma unroll
+    for (unsigned i = 0; i < 8; ++i) {
+      if (g + i < G) accumulator = fmaf(static_cast<float>(dot[i]), product[i], accumulator);
+    }
+    const std::size_t index = static_cast<std::size_t>(tile) * 16u + row;
+    if (m.output_f16) {
+      static_cast<__half*>(m.output)[index] = f2h(accumulator);
+    } else {
+      static_cast<float*>(m.output)[index] = accumulator;
+    }
+    return;
+  }
   const std::uint32_t pairs = 16u * B;
   if (threadIdx.x >= pairs) return;
   if (!mbar_wait_bounded(&bars[scale_bar], 0, &g_gemv_error)) return;
@@ -462,6 +531,7 @@ __global__ __launch_bounds__(256) void gemv_cascade_kernel(const GemvArgs args, 
   const std::uint32_t g_begin = min(G, part * layout.per_part);
   const std::uint32_t n = min(G, g_begin + layout.per_part) - g_begin;
   const std::uint32_t chunks = (n + chunk - 1u) / chunk;
+  const std::uint32_t chunk_shift = static_cast<std::uint32_t>(__ffs(static_cast<int>(chunk)) - 1);  // chunk: a power of two
   const std::uint32_t max_chunks = (layout.per_part + chunk - 1u) / chunk;
   std::uint8_t* stage = smem;
   __half* own_scales = reinterpret_cast<__half*>(smem + layout.scale_offset);
@@ -515,7 +585,7 @@ __global__ __launch_bounds__(256) void gemv_cascade_kernel(const GemvArgs args, 
   bool ok = true;
   for (std::uint32_t local = warp; local < n; local += 8u) {
     const std::uint32_t g = g_begin + local;
-    if (!mbar_wait_bounded(&bars[local / chunk], 0, &g_gemv_error)) {
+    if (!mbar_wait_bounded(&bars[local >> chunk_shift], 0, &g_gemv_error)) {
       ok = false;
       break;
     }
@@ -1094,7 +1164,8 @@ std::uint32_t env_value(const char* name, std::uint32_t fallback) {
 // Tuning knobs (read once): cluster split override and groups per bulk copy.
 struct StreamTuning {
   std::uint32_t parts = env_value("GFXB_GEMV_PARTS", 0);
-  std::uint32_t chunk = std::max<std::uint32_t>(1u, env_value("GFXB_GEMV_CHUNK", 8));
+  // groups per bulk copy: a power of two (the kernels find a group's barrier by a shift)
+  std::uint32_t chunk = 1u << (31 - __builtin_clz(std::max<std::uint32_t>(1u, env_value("GFXB_GEMV_CHUNK", 8))));
   std::uint32_t min_tiles_p1 = env_value("GFXB_GEMV_P1_TILES", 1024);
   std::uint32_t cascade = env_value("GFXB_GEMV_CASCADE", 1);  // 0: several tokens gather in one CTA too
   std::uint32_t tall_cascade = std::max<std::uint32_t>(2u, env_value("GFXB_GEMV_TALL_CASCADE", 9));  // tokens from which tall matrices split in two
@@ -1158,6 +1229,10 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
       error = cudaFuncSetAttribute(gemv_stream_kernel<Bits, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    200 * 1024);
     }
+    if (error == cudaSuccess) {
+      error = cudaFuncSetAttribute(gemv_stream_kernel<Bits, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   200 * 1024);
+    }
     if (error != cudaSuccess) {
       set_error_cuda(error, "GEMV shared-memory configuration failed");
       return static_cast<int>(GFXB_CUDA_ERROR);
@@ -1177,11 +1252,15 @@ int launch_stream(const GemvArgs& args, std::uint32_t total_tiles, cudaStream_t 
   attribute[0].val.clusterDim.z = 1;
   config.attrs = attribute;
   config.numAttrs = 1;
+  // the product-first chain from 64 groups on (measured: faster on the 136-group down projection, slower on
+  // 40-group matrices, whose CTAs are limited by registers rather than shared memory)
   const cudaError_t error =
-      args.batch == 1u ? launch_kernel(gemv_stream_kernel<Bits, true>, config.gridDim, config.blockDim,
+      args.batch != 1u ? launch_kernel(gemv_stream_kernel<Bits, false>, config.gridDim, config.blockDim,
                                        config.dynamicSmemBytes, stream, parts, args, parts, chunk)
-                       : launch_kernel(gemv_stream_kernel<Bits, false>, config.gridDim, config.blockDim,
-                                       config.dynamicSmemBytes, stream, parts, args, parts, chunk);
+      : args.groups >= 64u ? launch_kernel(gemv_stream_kernel<Bits, true, true>, config.gridDim, config.blockDim,
+                                           config.dynamicSmemBytes, stream, parts, args, parts, chunk)
+                           : launch_kernel(gemv_stream_kernel<Bits, true>, config.gridDim, config.blockDim,
+                                           config.dynamicSmemBytes, stream, parts, args, parts, chunk);
   if (error != cudaSuccess) {
     set_error_cuda(error, "streaming GEMV launch failed");
     return GFXB_CUDA_ERROR;

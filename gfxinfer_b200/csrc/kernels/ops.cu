@@ -29,14 +29,13 @@ constexpr unsigned kNormSplitIters = 4;
 template <int ActBits, unsigned Iterations>
 __global__ __launch_bounds__(kNormThreads) void residual_norm_pack_kernel(NormPackArgs args) {
   pdl_trigger();
-  pdl_wait();
   __shared__ float warp_sums[8];
   __shared__ float warp_max[Iterations][8];
   __shared__ int warp_code_sums[Iterations][8];
   const unsigned begin = blockIdx.x * kNormSplitIters;
   const unsigned end = begin + kNormSplitIters < Iterations ? begin + kNormSplitIters : Iterations;
   norm_pack_body<ActBits, Iterations>(args, blockIdx.y, threadIdx.x, BlockSync{}, warp_sums, warp_max, warp_code_sums,
-                                      begin, end);
+                                      begin, end, true);
 }
 
 // ---------------------------------------------------------------------------

@@ -145,10 +145,13 @@ constexpr unsigned kNormMaxIter = 64;  // H <= 16384
 // [it_begin, it_end) limits the outputs (residual, normalized values, pack)
 // to elements it * 256 + t of those iterations, i.e. 128-groups 2 it_begin ..
 // 2 it_end - 1; every thread still reads the whole row for the sum of squares.
+// With dependency_wait the body waits for the previous kernel (pdl_wait) itself,
+// after loading the norm weights, which never depend on it.
 template <int ActBits, unsigned Iterations, class Sync>
 __device__ __forceinline__ void norm_pack_body(const NormPackArgs& args, std::uint32_t token, unsigned t, Sync sync,
                                                float* warp_sums, float (*warp_max)[8], int (*warp_code_sums)[8],
-                                               unsigned it_begin = 0, unsigned it_end = Iterations) {
+                                               unsigned it_begin = 0, unsigned it_end = Iterations,
+                                               bool dependency_wait = false) {
   const std::uint32_t H = args.elements;
   const unsigned lane = t & 31u, warp = t >> 5;
   constexpr unsigned iterations = Iterations;
@@ -168,6 +171,7 @@ __device__ __forceinline__ void norm_pack_body(const NormPackArgs& args, std::ui
     if (args.unit_offset) scale = __fadd_rn(scale, 1.0f);
     weights[it] = scale;
   }
+  if (dependency_wait) pdl_wait();
   if (args.embedding_codes != nullptr) {
     // Embedding row gather fused as the input (lowbit_gemv.hip:158-189, W4/W2 row-major).
     const std::uint32_t id = args.device_tokens != nullptr ? ld_cg(args.device_tokens + token) : args.host_token;
