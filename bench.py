@@ -216,6 +216,35 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def measure_verifier(gs, np, torch, local: int, widths=(5, 32), blocks: int = 6) -> dict:
+    """The causal verifier alone (the reference's block-bench: `QwenDecodeSession::block_step`, evaluated tokens
+    per second) on the config-2 model: after a 64-token prefill, `blocks` timed blocks of each width (one warm-up
+    block first), device-timed with CUDA events on the session stream."""
+    cfg = dict(gs.CONFIG2, max_context=512)
+    engine = gs.Engine.create(gs.model_config(**cfg), device=local, include_mtp=False)
+    rng = np.random.default_rng(cfg["seed"] + 5)
+    out = {"workload": "config-2 causal verifier blocks after a 64-token prompt, evaluated tokens/s", "widths": {}}
+    for width in widths:
+        session = gs.QwenDecodeSession.create(engine, maximum_context_tokens=512)
+        stream = torch.cuda.ExternalStream(session.stream(), device=torch.device("cuda", local))
+        session.prefill([int(t) for t in rng.integers(0, cfg["vocab"], size=64)])
+        tokens = [[int(t) for t in rng.integers(0, cfg["vocab"], size=width)] for _ in range(blocks + 1)]
+        session.block_step(tokens[0])
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for block in tokens[1:]:
+            session.block_step(block)
+        stop.record(stream)
+        stop.synchronize()
+        ms = start.elapsed_time(stop)
+        out["widths"][str(width)] = {"evaluated_tokens_per_s": round(width * blocks / (ms / 1000.0), 3),
+                                     "ms_per_block": round(ms / blocks, 3)}
+        session.close()
+    engine.close()
+    return out
+
+
 def measure_mtp(gs, np, torch, local: int, depths=(4, 8), emitted_target: int = 256) -> dict:
     """the config-2 model plus one MTP layer, context 2048; speculative rounds
     (MTP draft chain + causal verifier, one captured CUDA graph per depth) until 256 tokens are
@@ -476,6 +505,7 @@ def run_b200(args) -> None:
         extras["config4"] = measure_config4(gs, np, torch, world, rank, local, config4_id, min(args.steps, 96), barrier)
         if world == 1:
             extras["mtp"] = measure_mtp(gs, np, torch, local)
+            extras["verifier"] = measure_verifier(gs, np, torch, local)
             extras["config0"] = measure_config0(line["roofline"]["peak"])
     if rank == 0:
         line.update(extras)

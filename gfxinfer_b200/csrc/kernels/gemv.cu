@@ -80,7 +80,9 @@ __global__ __launch_bounds__(256) void gemv_b200_kernel(const GemvArgs args) {
   const std::uint8_t* tile_codes = m.codes + static_cast<std::size_t>(tile) * G * kBlock;
   const __half* tile_scales = m.scales + static_cast<std::size_t>(tile) * G * 16u;
 
-  __shared__ std::int32_t dots[8][16][NB * 8];
+  // one padding word per row: the chain's reads (16 rows x 2 tokens per warp) and the mma lanes' writes
+  // (8 rows per warp) then fall into distinct banks instead of 8-16 on one
+  __shared__ std::int32_t dots[8][16][NB * 8 + 1];
 
   const std::uint32_t pairs = 16u * B;
   float accumulator[2] = {0.0f, 0.0f};
@@ -1428,7 +1430,9 @@ __global__ __launch_bounds__(256) void gemm_gfx12_kernel(
   constexpr std::uint32_t kFrag = Bits == 2 ? 8u : (Bits == 3 ? 12u : 16u);
   constexpr int kAlpha = Codec<Bits>::alpha, kBeta = Codec<Bits>::beta;
   __shared__ std::uint32_t stage[8][kBlock / 4 + 4];
-  __shared__ std::int32_t dots[8][16][NB * 8];
+  // one padding word per row: the chain's reads (16 rows x 2 tokens per warp) and the mma lanes' writes
+  // (8 rows per warp) then fall into distinct banks instead of 8-16 on one
+  __shared__ std::int32_t dots[8][16][NB * 8 + 1];
   const std::uint32_t pairs = 16u * B;
   float accumulator[2] = {0.0f, 0.0f};
   const std::uint32_t rounds = (G + 7u) / 8u;
