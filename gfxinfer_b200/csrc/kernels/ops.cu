@@ -548,6 +548,10 @@ __global__ __launch_bounds__(256) void attention_merge_kernel(AttentionArgs args
 
 constexpr std::uint32_t kDecodeStageBytes = 2u * kChunk * 256u * 2u;  // the chunk's key and value rows
 
+// Shared: the keys and then the values of the chunk pass through one 64 KB stage (the values are copied in
+// once the scores are done), so that three CTAs fit on an SM: for long contexts, where the grid holds several
+// CTAs per SM. Otherwise both are staged at once into 128 KB.
+template <bool Shared>
 __global__ __launch_bounds__(256) void attention_decode_kernel(const AttentionDecodeArgs args) {
   extern __shared__ __align__(128) std::uint8_t stage[];
   __shared__ float normalized[256];
@@ -581,31 +585,34 @@ __global__ __launch_bounds__(256) void attention_decode_kernel(const AttentionDe
   const bool holds_new = chunk + 1u == chunks;  // row n - 1 is `position`
   const std::uint32_t cached = holds_new ? n - 1u : n;
   __half* keys = reinterpret_cast<__half*>(stage);
-  __half* values = keys + kChunk * 256u;
-  {
-    const std::size_t row_stride = static_cast<std::size_t>(A.kv_heads) * 256u;
-    const std::size_t first = (begin * A.kv_heads + kvh) * 256u;
-    for (std::uint32_t i = tid; i < cached * 32u; i += blockDim.x) {
-      const std::uint32_t row = i >> 5, piece = i & 31u;
-      cp_async_16(keys + row * 256u + piece * 8u, A.key_cache + first + row * row_stride + piece * 8u);
-    }
-    cp_async_commit();
+  __half* values = Shared ? keys : keys + kChunk * 256u;
+  const std::size_t row_stride = static_cast<std::size_t>(A.kv_heads) * 256u;
+  const std::size_t first = (begin * A.kv_heads + kvh) * 256u;
+  auto stage_values = [&]() {
     for (std::uint32_t i = tid; i < cached * 32u; i += blockDim.x) {
       const std::uint32_t row = i >> 5, piece = i & 31u;
       cp_async_16(values + row * 256u + piece * 8u, A.value_cache + first + row * row_stride + piece * 8u);
     }
     cp_async_commit();
+  };
+  for (std::uint32_t i = tid; i < cached * 32u; i += blockDim.x) {
+    const std::uint32_t row = i >> 5, piece = i & 31u;
+    cp_async_16(keys + row * 256u + piece * 8u, A.key_cache + first + row * row_stride + piece * 8u);
   }
+  cp_async_commit();
+  if constexpr (!Shared) stage_values();
   bool out_of_range = false;
+  __half new_value = __ushort_as_half(0);
   query[tid] = h2f(qk_norm_rope_value(ld_cg(R.q_input + static_cast<std::size_t>(h) * R.q_stride + tid), R.q_weight,
                                       position, R, tid, BlockSync{}, normalized, warp_sums, out_of_range));
   if (holds_new) {
     const __half key = qk_norm_rope_value(ld_cg(R.k_input + static_cast<std::size_t>(kvh) * R.k_stride + tid),
                                           R.k_weight, position, R, tid, BlockSync{}, normalized, warp_sums,
                                           out_of_range);
-    const __half value = f2h(ld_cg(R.v_input + static_cast<std::size_t>(kvh) * 256u + tid));
+    new_value = f2h(ld_cg(R.v_input + static_cast<std::size_t>(kvh) * 256u + tid));
+    const __half value = new_value;
     keys[(n - 1u) * 256u + tid] = key;
-    values[(n - 1u) * 256u + tid] = value;
+    if constexpr (!Shared) values[(n - 1u) * 256u + tid] = value;
     if (h % group == 0) {  // one writer per KV head appends the row
       const std::size_t slot = (position * A.kv_heads + kvh) * 256u + tid;
       R.key_cache[slot] = key;
@@ -613,8 +620,12 @@ __global__ __launch_bounds__(256) void attention_decode_kernel(const AttentionDe
     }
   }
   if (out_of_range && tid == 0) atomicOr(&g_ops_error, 2u);
-  cp_async_wait<1>();  // this thread's key copies
-  __syncthreads();     // everyone's, the new row and the query
+  if constexpr (Shared) {
+    cp_async_wait<0>();  // this thread's key copies
+  } else {
+    cp_async_wait<1>();  // this thread's key copies
+  }
+  __syncthreads();  // everyone's, the new row and the query
 
   if (16u * warp < n) {
     float qf[8];
@@ -670,6 +681,10 @@ __global__ __launch_bounds__(256) void attention_decode_kernel(const AttentionDe
     if ((lane & 1u) == 0 && p < n) scores[p] = __fmul_rn(part[0], 0.0625f);
   }
   __syncthreads();
+  if constexpr (Shared) {  // every key has been read: the values take the stage
+    stage_values();
+    if (holds_new) values[(n - 1u) * 256u + tid] = new_value;
+  }
 
   // exact prefix maximum over the chunk and the rescale factors
   const float negative_infinity = -__int_as_float(0x7f800000);
@@ -1069,15 +1084,29 @@ int launch_attention_decode(const AttentionDecodeArgs& args, cudaStream_t stream
                                         : static_cast<std::uint32_t>((a.base_token_count + kChunk - 1) / kChunk);
   static DeviceOnce configured;
   GFXB_TRY(configured.run([](int) {
-    const cudaError_t error = cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   static_cast<int>(kDecodeStageBytes));
+    cudaError_t error = cudaFuncSetAttribute(attention_decode_kernel<false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kDecodeStageBytes));
+    if (error == cudaSuccess) {
+      error = cudaFuncSetAttribute(attention_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(kDecodeStageBytes / 2u));
+    }
     if (error != cudaSuccess) {
       set_error_cuda(error, "attention shared-memory configuration failed");
       return static_cast<int>(GFXB_CUDA_ERROR);
     }
     return static_cast<int>(GFXB_OK);
   }));
-  launch_kernel(attention_decode_kernel, dim3(grid_chunks, a.q_heads), dim3(256), kDecodeStageBytes, stream, 0, args);
+  // more CTAs than two per SM (long contexts): the shared 64 KB stage, three CTAs per SM
+  int sms = 0;
+  GFXB_TRY(device_sm_count(&sms));
+  if (static_cast<std::uint64_t>(grid_chunks) * a.q_heads > 2ull * static_cast<std::uint64_t>(sms)) {
+    launch_kernel(attention_decode_kernel<true>, dim3(grid_chunks, a.q_heads), dim3(256), kDecodeStageBytes / 2u,
+                  stream, 0, args);
+  } else {
+    launch_kernel(attention_decode_kernel<false>, dim3(grid_chunks, a.q_heads), dim3(256), kDecodeStageBytes, stream,
+                  0, args);
+  }
   return launch_status("single-token attention launch failed");
 }
 
