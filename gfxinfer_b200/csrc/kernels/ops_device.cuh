@@ -937,21 +937,36 @@ __device__ __forceinline__ void attention_finish_head(const AttentionArgs& args,
                                                       float Acc, float Den, Sync sync, float (*pack_max)[4],
                                                       int (*pack_sum)[4]);
 
-template <class Sync>
+// Batch chunks' loads are issued before their part of the ordered chain (one memory round trip per batch);
+// Batch = 1 keeps the register footprint of a single step.
+template <class Sync, unsigned Batch = 8>
 __device__ __forceinline__ void attention_merge_head(const AttentionArgs& args, unsigned h, unsigned token, unsigned d,
                                                      std::uint32_t chunks, Sync sync, float (*pack_max)[4],
                                                      int (*pack_sum)[4]) {
   const float* partial = args.partials + (static_cast<std::size_t>(token) * args.q_heads + h) * args.max_chunks * 258u;
   float M = ld_cg(partial), Den = ld_cg(partial + 1), Acc = ld_cg(partial + 2 + d);
-  for (std::uint32_t c = 1; c < chunks; ++c) {
-    const float* p = partial + static_cast<std::size_t>(c) * 258u;
-    const float m = ld_cg(p);
-    const float next = fmaxf(M, m);
-    const float a1 = gx_expf(__fsub_rn(M, next));
-    const float a2 = gx_expf(__fsub_rn(m, next));
-    Den = __fadd_rn(__fmul_rn(Den, a1), __fmul_rn(ld_cg(p + 1), a2));
-    Acc = __fadd_rn(__fmul_rn(Acc, a1), __fmul_rn(ld_cg(p + 2 + d), a2));
-    M = next;
+  for (std::uint32_t c0 = 1; c0 < chunks; c0 += Batch) {
+    float m[Batch], den[Batch], acc[Batch];
+#pragma unroll
+    for (unsigned i = 0; i < Batch; ++i) {
+      if (c0 + i < chunks) {
+        const float* p = partial + static_cast<std::size_t>(c0 + i) * 258u;
+        m[i] = ld_cg(p);
+        den[i] = ld_cg(p + 1);
+        acc[i] = ld_cg(p + 2 + d);
+      }
+    }
+#pragma unroll
+    for (unsigned i = 0; i < Batch; ++i) {
+      if (c0 + i < chunks) {
+        const float next = fmaxf(M, m[i]);
+        const float a1 = gx_expf(__fsub_rn(M, next));
+        const float a2 = gx_expf(__fsub_rn(m[i], next));
+        Den = __fadd_rn(__fmul_rn(Den, a1), __fmul_rn(den[i], a2));
+        Acc = __fadd_rn(__fmul_rn(Acc, a1), __fmul_rn(acc[i], a2));
+        M = next;
+      }
+    }
   }
   attention_finish_head(args, h, token, d, Acc, Den, sync, pack_max, pack_sum);
 }

@@ -560,7 +560,7 @@ __device__ __forceinline__ void attention_units(const LoopLaunch& L, Ctx& c, con
     ComputeSync{}();
     if (*flag != 0) {
       for (std::uint32_t j = 0; j < group; ++j) {
-        attention_merge_head(A, kvh * group + j, 0, t, chunks, ComputeSync{}, sc.attention.pack_max,
+        attention_merge_head<ComputeSync, 1>(A, kvh * group + j, 0, t, chunks, ComputeSync{}, sc.attention.pack_max,
                              sc.attention.pack_sum);
         ComputeSync{}();
       }

@@ -364,23 +364,27 @@ def _fused_decode(lib, inputs, cos, sin, position, capacity, scratch, q_heads=24
     return out.cpu().numpy().view(np.uint16), d_keys[position].cpu().numpy(), d_values[position].cpu().numpy()
 
 
+@pytest.mark.parametrize("heads", [(24, 4), (16, 2), (8, 8)], ids=["group6", "group8", "group1"])
 @pytest.mark.parametrize("spread", [1.0, 4.0])
-def test_decode_attention_equals_three_launch_path(lib, spread):
+def test_decode_attention_equals_three_launch_path(lib, spread, heads):
     """The single-launch decode attention (norm + RoPE + KV append + attention + merge) against
     gfxb_qk_rms_norm_rope + gfxb_gated_attention at every chunk shape: one chunk, a chunk boundary,
     partial and full last chunks, up to 32 chunks at the last cache slot; the output and the appended
-    cache row bit for bit. One zero-filled scratch serves every call (its counters return to zero)."""
+    cache row bit for bit, for three head layouts (GQA groups 6, 8 and 1). Long contexts at groups 6
+    and 8 take the shared key/value stage. One zero-filled scratch serves every call (its counters
+    return to zero)."""
+    q_heads, kv_heads = heads
     capacity = 4096
     cos, sin = _rope(lib, capacity)
-    scratch = torch.zeros(lib.lib().gfxb_decode_attention_scratch_bytes(24, capacity), dtype=torch.uint8,
+    scratch = torch.zeros(lib.lib().gfxb_decode_attention_scratch_bytes(q_heads, capacity), dtype=torch.uint8,
                           device="cuda")
     for position in (0, 1, 63, 64, 107, 108, 127, 128, 129, 255, 256, 300, 1000, 3839, 3840, 3947, 3948, 4095):
-        inputs = _decode_attention_inputs(np.random.default_rng(position), capacity, spread=spread)
-        want = _three_launch_decode(lib, inputs, cos, sin, position, capacity)
-        got = _fused_decode(lib, inputs, cos, sin, position, capacity, scratch)
+        inputs = _decode_attention_inputs(np.random.default_rng(position), capacity, q_heads, kv_heads, spread)
+        want = _three_launch_decode(lib, inputs, cos, sin, position, capacity, q_heads, kv_heads)
+        got = _fused_decode(lib, inputs, cos, sin, position, capacity, scratch, q_heads, kv_heads)
         for g, w in zip(got, want):
             np.testing.assert_array_equal(g, w, err_msg=f"position {position}")
-    tickets = scratch[-24 * 4:].cpu().numpy()
+    tickets = scratch[-q_heads * 4:].cpu().numpy()
     assert not tickets.any()
 
 
