@@ -681,6 +681,7 @@ struct PipeLayout {
   std::uint32_t dot_bytes;     // G * 16 * B * 4
   std::uint32_t stage_bytes;   // the three, 128-byte aligned
   std::uint32_t act_offset;    // fp16 activation scales [B][G]
+  std::uint32_t pair_offset;   // one token: (float(dot), scale product) of the tile being chained [G][16]
   std::uint32_t bar_offset;
   std::uint32_t total;
 };
@@ -694,7 +695,8 @@ __host__ __device__ inline PipeLayout pipe_layout(int bits, std::uint32_t groups
   l.dot_bytes = groups * 16u * batch * 4u;
   l.stage_bytes = (l.weight_bytes + l.scale_bytes + l.dot_bytes + 127u) & ~127u;
   l.act_offset = kPipeStages * l.stage_bytes;
-  l.bar_offset = (l.act_offset + groups * batch * 2u + 15u) & ~15u;
+  l.pair_offset = (l.act_offset + groups * batch * 2u + 15u) & ~15u;
+  l.bar_offset = l.pair_offset + (batch == 1u ? groups * 16u * 8u : 0u);
   l.total = l.bar_offset + kPipeStages * 8u;
   return l;
 }
@@ -799,7 +801,34 @@ __global__ __launch_bounds__(256) void gemv_pipe_kernel(const GemvArgs args, std
       }
     }
     __syncthreads();
-    if (ready && threadIdx.x < 16u * B) {
+    if constexpr (One) {
+      // every thread forms (float(dot), scale product) pairs of the tile, so that the 16 chain threads only load
+      // and fma: the same conversions and products as the chain below, in parallel
+      float2* pairs = reinterpret_cast<float2*>(smem + layout.pair_offset);
+      if (ready) {
+        for (std::uint32_t idx = threadIdx.x; idx < G * 16u; idx += blockDim.x) {
+          pairs[idx] = make_float2(static_cast<float>(dots[idx]),
+                                   __fmul_rn(h2f(tile_scales[idx]), h2f(act_scales[idx >> 4])));
+        }
+      }
+      __syncthreads();
+      if (ready && threadIdx.x < 16u) {
+        const std::uint32_t row = threadIdx.x;
+        float accumulator = 0.0f;
+#pragma unroll 8
+        for (std::uint32_t g = 0; g < G; ++g) {
+          const float2 pair = pairs[g * 16u + row];
+          accumulator = fmaf(pair.x, pair.y, accumulator);
+        }
+        const std::size_t index = static_cast<std::size_t>(tile) * 16u + row;
+        if (m.output_f16) {
+          static_cast<__half*>(m.output)[index] = f2h(accumulator);
+        } else {
+          static_cast<float*>(m.output)[index] = accumulator;
+        }
+      }
+    }
+    if (!One && ready && threadIdx.x < 16u * B) {
       const std::uint32_t row = threadIdx.x & 15u, tok = threadIdx.x >> 4;
       const __half* as = act_scales + static_cast<std::size_t>(tok) * G;
       float accumulator = 0.0f;
