@@ -242,17 +242,17 @@ def test_gated_attention_device_position_long_context(oracle, lib):
 def _argmax_cases(vocab):
     """Rows of logits with planted maxima; the lowest index among equal maxima must win
     (qwen_ops.hip:782, 794-796). The kernel reads index i in block (i / 256) % 64, so ties are
-    planted across blocks, across the rounds of one block, and at the first and last index."""
+    planted across blocks, across the strided passes of one block, and at the first and last index."""
     rng = np.random.default_rng(3)
     rows = []
     base = rng.normal(0, 1, vocab).astype(np.float32)
-    r = base.copy(); r[[7, 300, 16391, vocab - 1]] = 9.0; rows.append(r)                # across blocks and rounds
+    r = base.copy(); r[[7, 300, 16391, vocab - 1]] = 9.0; rows.append(r)                # across blocks and passes
     r = base.copy(); r[[0, vocab - 1]] = 9.0; rows.append(r)                            # first and last
     r = base.copy(); r[vocab - 1] = 9.0; rows.append(r)                                 # last alone
     rows.append(np.zeros(vocab, np.float32))                                            # all equal
     rows.append(np.full(vocab, -np.inf, np.float32))                                    # all -inf
     r = base.copy(); r[::5] = np.nan; r[[1001, 99999]] = 9.0; r[0] = np.nan; rows.append(r)  # NaNs ignored
-    r = base.copy(); r[[16383, 16384]] = 9.0; rows.append(r)                            # block 63 vs block 0 round 2
+    r = base.copy(); r[[16383, 16384]] = 9.0; rows.append(r)                            # block 63 vs block 0, 2nd stride
     r = base.copy(); r[[255, 256]] = 9.0; rows.append(r)                                # adjacent blocks
     r = base.copy(); r[np.arange(64) * 256 + 17] = 9.0; rows.append(r)                  # one tie in every block
     r = np.full(vocab, np.nan, np.float32); rows.append(r)                              # all NaN
